@@ -1,0 +1,507 @@
+#!/usr/bin/env python
+"""Benchmark of the MSDA hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
+
+A step is one forward + backward pass (msda3d / msda2d through the public
+autograd API) over one batch of synthetic inputs already resident in HBM.
+Default workload: the BASELINE "3D xl" config -- bf16, B=8 per GPU, Q=100000,
+H=8, C=32, L=4, P=4, levels (64,128,128),(32,64,64),(16,32,32),(8,16,16).
+
+Multi-GPU (torchrun, one process per GPU): batch sharding with no data-path
+collective -- every rank runs its own B=8 instance (weak scaling); the step
+time is the max over ranks (NCCL all_reduce of the CUDA-event time).
+
+--impl reference: the CPU oracle (oracle/, a C restatement of the reference's
+msda*_pytorch path; the reference itself is Python + Triton and cannot run on
+this box's host) times a bounded sample of the same workload on all host
+threads; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+SHAPES_2D = [(100, 150), (50, 75), (25, 38), (13, 19)]
+WORKLOADS = {
+    # the headline (bf16 3D xl fwd+bwd).
+    "3d_xl_bf16": dict(ndim=3, B=8, Q=100000, H=8, C=32, P=4, dtype=torch.bfloat16,
+                       shapes=[(64, 128, 128), (32, 64, 64), (16, 32, 32), (8, 16, 16)]),
+    # BASELINE configs[3].
+    "3d_bf16": dict(ndim=3, B=2, Q=20000, H=8, C=32, P=4, dtype=torch.bfloat16,
+                    shapes=[(32, 64, 64), (16, 32, 32), (8, 16, 16)]),
+    "3d_fp32": dict(ndim=3, B=2, Q=20000, H=8, C=32, P=4, dtype=torch.float32,
+                    shapes=[(32, 64, 64), (16, 32, 32), (8, 16, 16)]),
+    # BASELINE configs[1].
+    "2d_enc_bf16": dict(ndim=2, B=4, Q=19947, H=8, C=32, P=4, dtype=torch.bfloat16, shapes=SHAPES_2D),
+    "2d_enc_fp32": dict(ndim=2, B=4, Q=19947, H=8, C=32, P=4, dtype=torch.float32, shapes=SHAPES_2D),
+    # BASELINE configs[2] (inference: forward only).
+    "2d_dec_bf16": dict(ndim=2, B=8, Q=900, H=8, C=32, P=4, dtype=torch.bfloat16, shapes=SHAPES_2D,
+                        fwd_only=True),
+}
+DTYPE_NAME = {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}
+L2_BYTES = 126 * 1000 * 1000
+
+
+def _num_keys(shapes) -> int:
+    n = 0
+    for s in shapes:
+        p = 1
+        for v in s:
+            p *= v
+        n += p
+    return n
+
+
+def dims(wl):
+    return wl["B"], _num_keys(wl["shapes"]), wl["H"], wl["C"], wl["Q"], len(wl["shapes"]), wl["P"]
+
+
+def algorithmic_bytes(wl, B=None):
+    """Unique bytes per pass (value/loc/weights/out; grads) -- the roofline basis."""
+    B0, K, H, C, Q, L, P = dims(wl)
+    B = B0 if B is None else B
+    d = wl["ndim"]
+    e = torch.tensor([], dtype=wl["dtype"]).element_size()
+    smp = B * Q * H * L * P
+    fwd = e * (B * K * H * C + smp * d + smp + B * Q * H * C)
+    bwd = e * (2 * B * K * H * C + 2 * smp * (d + 1) + B * Q * H * C)
+    # The backward scatter kernel alone: reads value/loc/weights/grad_out,
+    # writes loc/weight grads and the fp32 value-gradient accumulator.
+    acc_bytes = 4 if e == 2 else e
+    bwd_kernel = e * (B * K * H * C + smp * (d + 1) + B * Q * H * C) + e * smp * (d + 1) \
+        + acc_bytes * B * K * H * C
+    return {"fwd": fwd, "bwd": bwd, "fwd_bwd": fwd + bwd, "bwd_kernel": bwd_kernel,
+            "samples": smp}
+
+
+def make_inputs(wl, device, seed):
+    """value ~ N(0,1), loc ~ U[0,1), weights = softmax(N(0,1) logits over L*P),
+    grad_out ~ N(0,1); generated on the device from a seeded generator."""
+    B, K, H, C, Q, L, P = dims(wl)
+    d, dt = wl["ndim"], wl["dtype"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    value = torch.randn(B, K, H, C, generator=g, device=device, dtype=torch.float32).to(dt)
+    loc = torch.rand(B, Q, H, L, P, d, generator=g, device=device, dtype=torch.float32).to(dt)
+    attn = torch.randn(B, Q, H, L * P, generator=g, device=device, dtype=torch.float32)
+    attn = attn.softmax(-1).view(B, Q, H, L, P).to(dt)
+    go = torch.randn(B, Q, H * C, generator=g, device=device, dtype=torch.float32).to(dt)
+    shapes = torch.tensor(wl["shapes"], dtype=torch.int32)
+    return value, shapes, loc, attn, go
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", ",".join(str(g) for g in self.gpus), "-lms", "200"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None:
+            return None
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            lines = open(self.path).read().strip().splitlines()
+        except OSError:
+            return None
+        for line in lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- our arm
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def _traffic(workload, kernel):
+    """DRAM bytes per launch from the committed ncu summary, if any."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "dram_traffic.json")) as f:
+            return json.load(f).get(workload, {}).get(kernel)
+    except (OSError, ValueError):
+        return None
+
+
+def time_events(fn, iters, stream):
+    """Per-call CUDA-event times (ms) of fn() on `stream` after warm-up."""
+    times = []
+    for _ in range(iters):
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        fn()
+        e.record(stream)
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    return times
+
+
+def run_ours(args, wl, rank, world, local_rank):
+    import msda_triton_b200 as M
+    from msda_triton_b200 import _core, _lib
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    fn = M.msda3d if wl["ndim"] == 3 else M.msda2d
+    value, shapes, loc, attn, go = make_inputs(wl, dev, seed=1234 + rank)
+    v = value.requires_grad_(True)
+    lo = loc.requires_grad_(True)
+    a = attn.requires_grad_(True)
+    fwd_only = wl.get("fwd_only", False)
+
+    def step():
+        out = fn(v, shapes, lo, a)
+        if not fwd_only:
+            torch.autograd.grad(out, (v, lo, a), go)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    gpus = list(range(world)) if world > 1 else [local_rank]
+    barrier()
+    with ClockSampler(gpus) if rank == 0 else _Null() as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    if dist is not None:
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+
+    # ---- per-kernel times (one launch each), through the C ABI directly
+    lib = _lib.lib()
+    B, K, H, C, Q, L, P = dims(wl)
+    shp, on_dev = _core.prepare_spatial(shapes)
+    args_c = _core._common_args(value.detach(), shp, on_dev, loc.detach(), attn.detach())
+    out_buf = torch.empty(B, Q, H * C, device=dev, dtype=wl["dtype"])
+    fwd_c = lib.msda3d_fwd if wl["ndim"] == 3 else lib.msda2d_fwd
+    acc_c = lib.msda3d_bwd_accumulate if wl["ndim"] == 3 else lib.msda2d_bwd_accumulate
+    sp = stream.cuda_stream
+    kiters = max(3, min(args.steps, 10))
+
+    def k_fwd():
+        _core.check_status(fwd_c(*args_c, 1, 1e-4, out_buf.data_ptr(), sp))
+
+    fwd_times = time_events(k_fwd, kiters + 2, stream)[2:]
+    kern = {"fwd": statistics.mean(fwd_times)}
+    if not fwd_only:
+        gacc = torch.zeros(B, K, H, C, device=dev, dtype=torch.float32)
+        gl = torch.empty_like(loc)
+        ga = torch.empty_like(attn)
+
+        def k_bwd():
+            _core.check_status(acc_c(*args_c, 1, 1e-4, go.data_ptr(), gacc.data_ptr(),
+                                     gl.data_ptr(), ga.data_ptr(), sp))
+
+        kern["bwd_kernel"] = statistics.mean(time_events(k_bwd, kiters + 2, stream)[2:])
+        del gacc
+    if dist is not None:
+        for k in list(kern):
+            tt = torch.tensor([kern[k]], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            kern[k] = float(tt.item())
+
+    # ---- end to end: pinned host buffers in, results back to the host
+    e2e = run_e2e(args, wl, fn, dev, shapes, value, loc, attn, go, fwd_only, dist)
+
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+
+    ab = algorithmic_bytes(wl)
+    per_pass = ab["fwd"] if fwd_only else ab["fwd_bwd"]
+    samples = ab["samples"] * world
+    peak, peak_kind = _peaks()
+    dom = "fwd" if fwd_only or kern["fwd"] >= kern.get("bwd_kernel", 0.0) else "bwd_kernel"
+    dom_bytes = ab["fwd"] if dom == "fwd" else ab["bwd_kernel"]
+    achieved = dom_bytes / (kern[dom] * 1e-3) / 1e9
+    traffic = _traffic(args.workload, dom)
+    pass_gbs = per_pass / (ms * 1e-3) / 1e9
+    launches_per_step = 1 if fwd_only else 3 if wl["dtype"] != torch.float32 else 2
+    res = {
+        "metric": "MSDA fwd+bwd Gsamples/s" if not fwd_only else "MSDA fwd Gsamples/s",
+        "value": samples / (ms * 1e-3) / 1e9,
+        "unit": "Gsamples/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": DTYPE_NAME[wl["dtype"]],
+        "data": "synthetic (seeded N(0,1) value/grad_out, U[0,1) locations, softmax weights)",
+        "config": {
+            "workload": args.workload, "ndim": wl["ndim"], "batch_per_gpu": B,
+            "global_batch": B * world, "num_queries": Q, "num_heads": H, "channels": C,
+            "num_levels": L, "num_points": P, "spatial_shapes": wl["shapes"],
+            "parallelism": f"batch-sharded dp{world} (no collective)",
+            "l2": f"inputs larger than L2 (value {value.numel() * value.element_size() / 1e9:.2f} GB"
+                  f" > {L2_BYTES / 1e6:.0f} MB); no flush",
+        },
+        "fwd_ms": kern["fwd"],
+        "bwd_kernel_ms": kern.get("bwd_kernel"),
+        "pass_bytes": per_pass,
+        "pass_roofline_frac": pass_gbs / peak,
+        "roofline": {
+            "kernel": "msda_fwd_kernel" if dom == "fwd" else "msda_bwd_kernel",
+            "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_source": peak_kind,
+            "algorithmic_bytes": dom_bytes, "traffic": traffic,
+        },
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+        "e2e": e2e,
+    }
+    res["cpu_baseline"] = cpu_baseline(args, wl)
+    return res
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+    def summary(self):
+        return None
+
+
+def run_e2e(args, wl, fn, dev, shapes, value, loc, attn, go, fwd_only, dist):
+    """Same metric through the public API with pinned HOST buffers: every step
+    copies its inputs host->device and its results device->host."""
+    host_in = [t.detach().cpu().pin_memory() for t in (value, loc, attn, go)]
+    h2d = sum(t.numel() * t.element_size() for t in host_in[:3])
+    if not fwd_only:
+        h2d += host_in[3].numel() * host_in[3].element_size()
+    B, K, H, C, Q, L, P = dims(wl)
+    outs_shape = [(B, Q, H * C)] + ([] if fwd_only else [tuple(value.shape), tuple(loc.shape),
+                                                         tuple(attn.shape)])
+    host_out = [torch.empty(s, dtype=wl["dtype"]).pin_memory() for s in outs_shape]
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        v, lo, a, g = (t.to(dev, non_blocking=True) for t in host_in)
+        v.requires_grad_(True)
+        lo.requires_grad_(True)
+        a.requires_grad_(True)
+        out = fn(v, shapes, lo, a)
+        res = [out]
+        if not fwd_only:
+            res += list(torch.autograd.grad(out, (v, lo, a), g))
+        for h, r in zip(host_out, res):
+            h.copy_(r.detach(), non_blocking=True)
+
+    iters = max(1, min(args.steps, 3))
+    step()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(iters):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / iters
+    if dist is not None:
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    world = dist.get_world_size() if dist is not None else 1
+    samples = algorithmic_bytes(wl)["samples"] * world
+    del host_in, host_out
+    return {"value": samples / (ms * 1e-3) / 1e9, "unit": "Gsamples/s", "ms_per_step": ms,
+            "steps": iters, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+# ---------------------------------------------------------------- CPU (oracle) arm
+def _cpu_sample(wl, target_s):
+    """A bounded sample of the workload for the CPU: batch 1, and a query count
+    that keeps one fwd+bwd near `target_s` seconds (about 2 us of CPU per
+    sample per thread-group, measured on the oracle)."""
+    B, K, H, C, Q, L, P = dims(wl)
+    return dict(wl, B=1, Q=max(64, min(Q, int(Q * target_s / 8.0))))
+
+
+def cpu_oracle_step(wl, inputs, nthreads):
+    from oracle import msda_bwd_oracle, msda_fwd_oracle
+
+    value, shapes, loc, attn, go = inputs
+    t = time.perf_counter()
+    msda_fwd_oracle(value, shapes, loc, attn, True, 1e-4, nthreads)
+    if not wl.get("fwd_only", False):
+        msda_bwd_oracle(value, shapes, loc, attn, go, True, 1e-4, nthreads)
+    return time.perf_counter() - t
+
+
+def cpu_inputs(wl, seed=7):
+    B, K, H, C, Q, L, P = dims(wl)
+    d = wl["ndim"]
+    g = torch.Generator().manual_seed(seed)
+    value = torch.randn(B, K, H, C, generator=g).numpy()
+    loc = torch.rand(B, Q, H, L, P, d, generator=g).numpy()
+    attn = torch.randn(B, Q, H, L * P, generator=g).softmax(-1).view(B, Q, H, L, P).numpy()
+    go = torch.randn(B, Q, H * C, generator=g).numpy()
+    shapes = torch.tensor(wl["shapes"], dtype=torch.int64).numpy()
+    return value, shapes, loc, attn, go
+
+
+def cpu_baseline(args, wl, steps=1, target_s=4.0):
+    nthreads = os.cpu_count() or 1
+    swl = _cpu_sample(wl, target_s)
+    inputs = cpu_inputs(swl)
+    cpu_oracle_step(swl, inputs, nthreads)  # warm-up (page-in, thread pool)
+    ts = [cpu_oracle_step(swl, inputs, nthreads) for _ in range(steps)]
+    t = statistics.median(ts)
+    samples = algorithmic_bytes(swl)["samples"]
+    return {
+        "value": samples / t / 1e9, "unit": "Gsamples/s", "cores": nthreads, "kind": "port",
+        "sample": f"fp32 oracle (C, OpenMP) fwd{'' if wl.get('fwd_only') else '+bwd'} on batch 1, "
+                  f"Q={swl['Q']} of the {args.workload} workload ({samples} samples), "
+                  f"median of {steps} after 1 warm-up; {t:.2f} s per pass",
+    }
+
+
+def run_reference(args, wl, rank):
+    if rank != 0:
+        return None
+    nthreads = os.cpu_count() or 1
+    swl = _cpu_sample(wl, 3.0)
+    inputs = cpu_inputs(swl)
+    for _ in range(args.warmup):
+        cpu_oracle_step(swl, inputs, nthreads)
+    ts = [cpu_oracle_step(swl, inputs, nthreads) for _ in range(args.steps)]
+    t = sum(ts) / len(ts)
+    samples = algorithmic_bytes(swl)["samples"]
+    val = samples / t / 1e9
+    fwd_only = wl.get("fwd_only", False)
+    return {
+        "impl": "reference",
+        "metric": "MSDA fwd+bwd Gsamples/s" if not fwd_only else "MSDA fwd Gsamples/s",
+        "value": val, "unit": "Gsamples/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": args.workload, "ndim": wl["ndim"], "batch_per_gpu": 1,
+                   "num_queries": swl["Q"], "note": "bounded CPU sample of the workload"},
+        "cpu_baseline": {"value": val, "unit": "Gsamples/s", "cores": nthreads, "kind": "port",
+                         "sample": f"oracle fwd{'' if fwd_only else '+bwd'}, batch 1, Q={swl['Q']}"},
+        "e2e": {"value": val, "unit": "Gsamples/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="3d_xl_bf16", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        res = run_reference(args, wl, rank)
+    else:
+        if args.no_cpu_baseline:
+            globals()["cpu_baseline"] = lambda *a, **k: None
+        res = run_ours(args, wl, rank, world, local_rank)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,468 @@
+// msda_capi.cu -- the C ABI declared in include/msda_b200.h: argument
+// validation, level-table resolution, launch-shape selection and dispatch.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+
+#include "../../include/msda_b200.h"
+#include "msda_launch.cuh"
+
+namespace msda {
+
+MSDA_DECLARE_PAIR(float, float)
+MSDA_DECLARE_PAIR(__half, __half)
+MSDA_DECLARE_PAIR(__half, float)
+MSDA_DECLARE_PAIR(__nv_bfloat16, __nv_bfloat16)
+MSDA_DECLARE_PAIR(__nv_bfloat16, float)
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_last_error[0] = '\0';
+  return MSDA_SUCCESS;
+}
+
+int64_t dtype_bytes(int dt) {
+  switch (dt) {
+    case MSDA_FLOAT32: return 4;
+    case MSDA_FLOAT16: return 2;
+    case MSDA_BFLOAT16: return 2;
+    default: return 0;
+  }
+}
+
+const char* dtype_name(int dt) {
+  switch (dt) {
+    case MSDA_FLOAT32: return "float32";
+    case MSDA_FLOAT16: return "float16";
+    case MSDA_BFLOAT16: return "bfloat16";
+    default: return "unknown";
+  }
+}
+
+bool aligned(const void* p, int64_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % static_cast<uintptr_t>(a)) == 0;
+}
+
+struct Args {
+  int ndim;
+  const void* value;
+  int vdt;
+  int64_t B, K, H, C;
+  const int32_t* shapes;
+  int shapes_dev;
+  int64_t L;
+  const void* loc;
+  const void* attn;
+  int sdt;
+  int64_t Q, P;
+  int clamp;
+  double eps;
+};
+
+// Validate arguments, fill the Problem (except the launch shape) and pick
+// the launch shape.  `bufs` are the row-strided buffers whose alignment bounds
+// the chunk width (value, output / grad_out / grad_value).
+int prepare(const Args& a, const void* const* bufs, int nbufs, Problem& p, LaunchShape& ls) {
+  if (a.ndim != 2 && a.ndim != 3) return fail(MSDA_ERROR_INVALID_ARGUMENT, "ndim must be 2 or 3");
+  const int64_t e = dtype_bytes(a.vdt);
+  if (e == 0 || dtype_bytes(a.sdt) == 0)
+    return fail(MSDA_ERROR_UNSUPPORTED_DTYPE,
+                "MSDA only supports fp32, fp16, and bf16 (got value dtype code %d, sampling "
+                "dtype code %d)", a.vdt, a.sdt);
+  if (a.sdt != a.vdt && a.sdt != MSDA_FLOAT32)
+    return fail(MSDA_ERROR_UNSUPPORTED_DTYPE,
+                "sampling_locations/attention_weights dtype (%s) must equal the value dtype "
+                "(%s) or be float32", dtype_name(a.sdt), dtype_name(a.vdt));
+  if (a.B < 0 || a.K < 0 || a.H < 0 || a.C < 0 || a.L < 0 || a.Q < 0 || a.P < 0)
+    return fail(MSDA_ERROR_INVALID_ARGUMENT, "negative tensor dimension");
+  if (a.L > kMaxLevels)
+    return fail(MSDA_ERROR_TOO_MANY_LEVELS, "num_levels=%lld exceeds the supported maximum %d",
+                static_cast<long long>(a.L), kMaxLevels);
+  if (a.clamp && !(a.eps >= 0.0 && a.eps < 1.0))
+    return fail(MSDA_ERROR_INVALID_ARGUMENT, "clamp_eps must be in [0, 1), got %g", a.eps);
+  if (a.K > INT32_MAX)
+    return fail(MSDA_ERROR_INT32_OVERFLOW,
+                "Total number of keys (%lld) exceeds int32 range. Reduce spatial dimensions or "
+                "number of levels.", static_cast<long long>(a.K));
+  const int64_t rows = a.B * a.Q * a.H;
+  if (a.B != 0 && a.Q != 0 && a.H != 0 && rows / a.B / a.Q != a.H)
+    return fail(MSDA_ERROR_INT32_OVERFLOW, "B*Q*H overflows");
+  if (rows > INT32_MAX)
+    return fail(MSDA_ERROR_INT32_OVERFLOW, "B*Q*H = %lld exceeds int32 range",
+                static_cast<long long>(rows));
+  if (a.L > 0 && a.shapes == nullptr)
+    return fail(MSDA_ERROR_INVALID_ARGUMENT, "spatial_shapes is NULL");
+
+  std::memset(&p, 0, sizeof(p));
+  p.value = a.value;
+  p.loc = a.loc;
+  p.attn = a.attn;
+  p.B = a.B; p.K = a.K; p.H = a.H; p.C = a.C; p.Q = a.Q; p.L = a.L; p.P = a.P;
+  p.clamp = a.clamp ? 1 : 0;
+  p.lo = static_cast<float>(-1.0 + a.eps);
+  p.hi = static_cast<float>(1.0 - a.eps);
+  p.shapes_dev = nullptr;
+  if (a.shapes_dev) {
+    p.shapes_dev = a.shapes;
+  } else {
+    int64_t start = 0;
+    for (int64_t l = 0; l < a.L; ++l) {
+      int64_t n = 1;
+      for (int ax = 0; ax < a.ndim; ++ax) {
+        const int64_t v = a.shapes[l * a.ndim + (a.ndim - 1 - ax)];
+        if (v < 0) return fail(MSDA_ERROR_INVALID_ARGUMENT, "negative spatial shape at level %lld",
+                               static_cast<long long>(l));
+        p.lv.size[l][ax] = static_cast<int32_t>(v);
+        n *= v;
+        if (n > INT32_MAX)
+          return fail(MSDA_ERROR_INT32_OVERFLOW, "level %lld has more than 2^31-1 keys",
+                      static_cast<long long>(l));
+      }
+      if (a.ndim == 2) p.lv.size[l][2] = 1;
+      p.lv.start[l] = static_cast<int32_t>(start);
+      start += n;
+      if (start > INT32_MAX)
+        return fail(MSDA_ERROR_INT32_OVERFLOW,
+                    "Total number of keys (%lld) exceeds int32 range. Reduce spatial dimensions "
+                    "or number of levels.", static_cast<long long>(start));
+    }
+    if (start != a.K)
+      return fail(MSDA_ERROR_SHAPE_MISMATCH,
+                  "value dim 1 (%lld) does not match sum of spatial shapes (%lld).",
+                  static_cast<long long>(a.K), static_cast<long long>(start));
+  }
+
+  // Pointer checks: element alignment everywhere.
+  const int64_t se = dtype_bytes(a.sdt);
+  if (!aligned(a.value, e) || !aligned(a.loc, se) || !aligned(a.attn, se))
+    return fail(MSDA_ERROR_MISALIGNED, "input buffers must be aligned to their element size");
+  for (int i = 0; i < nbufs; ++i)
+    if (!aligned(bufs[i], e))
+      return fail(MSDA_ERROR_MISALIGNED, "output buffers must be aligned to their element size");
+
+  // Chunk width: the widest of 16/4/2 bytes that divides the row and every
+  // row-strided buffer's alignment.
+  const int64_t row_bytes = a.C * e;
+  int vb = 0;
+  const int cands[3] = {16, 4, 2};
+  for (int ci = 0; ci < 3 && vb == 0; ++ci) {
+    const int c = cands[ci];
+    if (c < e || row_bytes % c != 0) continue;
+    bool al = aligned(a.value, c);
+    for (int i = 0; i < nbufs; ++i) al = al && aligned(bufs[i], c);
+    if (al) vb = c;
+  }
+  if (vb == 0) vb = static_cast<int>(e);  // e divides everything already checked
+  const int64_t nv = row_bytes / vb;
+  int vpl;
+  if (vb == 16) {
+    vpl = nv <= 32 ? 1 : nv <= 64 ? 2 : nv <= 128 ? 4 : 0;
+  } else {
+    vpl = nv <= 32 ? 1 : nv <= 256 ? 8 : 0;
+  }
+  if (vpl == 0)
+    return fail(MSDA_ERROR_UNSUPPORTED_CHANNELS,
+                "channels per head C=%lld (%lld bytes) exceeds the supported row size",
+                static_cast<long long>(a.C), static_cast<long long>(row_bytes));
+  int64_t lanes = (nv + vpl - 1) / vpl;
+  int log2g = 0;
+  while ((int64_t{1} << log2g) < lanes) ++log2g;
+  p.nv = static_cast<int32_t>(nv);
+  p.log2g = log2g;
+
+  // Heads per scheduling group: the largest divisor of H whose value slice
+  // (K * hg * C * e bytes) stays within a budget that leaves L2 room for the
+  // streamed inputs.  MSDA_HEAD_GROUP overrides (tuning).
+  int64_t hg = a.H > 0 ? a.H : 1;
+  const char* env = std::getenv("MSDA_HEAD_GROUP");
+  int64_t forced = env ? std::atoll(env) : 0;
+  if (forced > 0 && a.H % forced == 0) {
+    hg = forced;
+  } else if (a.H > 0) {
+    const int64_t budget = int64_t{48} << 20;
+    for (hg = a.H; hg > 1; --hg)
+      if (a.H % hg == 0 && a.K * hg * row_bytes <= budget) break;
+  }
+  p.hg = static_cast<int32_t>(hg);
+
+  ls.ndim = a.ndim;
+  ls.vb = vb;
+  ls.vpl = vpl;
+  const int64_t threads = rows << log2g;
+  ls.grid = (threads + kThreads - 1) / kThreads;
+  return MSDA_SUCCESS;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+  return fail(MSDA_ERROR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+}
+
+cudaError_t dispatch_fwd(int vdt, int sdt, const LaunchShape& ls, const Problem& p, void* out,
+                         cudaStream_t st) {
+  switch (vdt) {
+    case MSDA_FLOAT32: return launch_fwd<float, float>(ls, p, out, st);
+    case MSDA_FLOAT16:
+      return sdt == MSDA_FLOAT32 ? launch_fwd<__half, float>(ls, p, out, st)
+                                 : launch_fwd<__half, __half>(ls, p, out, st);
+    default:
+      return sdt == MSDA_FLOAT32 ? launch_fwd<__nv_bfloat16, float>(ls, p, out, st)
+                                 : launch_fwd<__nv_bfloat16, __nv_bfloat16>(ls, p, out, st);
+  }
+}
+
+cudaError_t dispatch_bwd(int vdt, int sdt, const LaunchShape& ls, const Problem& p,
+                         const void* go, float* gacc, void* gl, void* ga, cudaStream_t st) {
+  switch (vdt) {
+    case MSDA_FLOAT32: return launch_bwd<float, float>(ls, p, go, gacc, gl, ga, st);
+    case MSDA_FLOAT16:
+      return sdt == MSDA_FLOAT32 ? launch_bwd<__half, float>(ls, p, go, gacc, gl, ga, st)
+                                 : launch_bwd<__half, __half>(ls, p, go, gacc, gl, ga, st);
+    default:
+      return sdt == MSDA_FLOAT32 ? launch_bwd<__nv_bfloat16, float>(ls, p, go, gacc, gl, ga, st)
+                                 : launch_bwd<__nv_bfloat16, __nv_bfloat16>(ls, p, go, gacc, gl,
+                                                                            ga, st);
+  }
+}
+
+int run_fwd(const Args& a, void* out, void* stream) {
+  if ((a.value == nullptr && a.B * a.K * a.H * a.C > 0) || (out == nullptr && a.B * a.Q * a.H * a.C > 0))
+    return fail(MSDA_ERROR_INVALID_ARGUMENT, "value/output pointer is NULL");
+  const void* bufs[1] = {out};
+  Problem p;
+  LaunchShape ls;
+  int rc = prepare(a, bufs, 1, p, ls);
+  if (rc != MSDA_SUCCESS) return rc;
+  if (a.B * a.Q * a.H * a.C == 0) return ok();
+  const cudaError_t err = dispatch_fwd(a.vdt, a.sdt, ls, p, out, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "forward launch");
+  return ok();
+}
+
+// Validate the backward arguments; on success `p`/`ls` are ready to launch.
+int prepare_bwd(const Args& a, const void* go, const void* gv_like, void* gl, void* ga,
+                Problem& p, LaunchShape& ls) {
+  const int64_t nval = a.B * a.K * a.H * a.C;
+  const int64_t nsmp = a.B * a.Q * a.H * a.L * a.P;
+  if (nval > 0 && (a.value == nullptr || gv_like == nullptr))
+    return fail(MSDA_ERROR_INVALID_ARGUMENT, "value/grad_value pointer is NULL");
+  if (nsmp > 0 && (gl == nullptr || ga == nullptr || a.loc == nullptr || a.attn == nullptr))
+    return fail(MSDA_ERROR_INVALID_ARGUMENT, "sampling/attention (grad) pointer is NULL");
+  if (a.B * a.Q * a.H * a.C > 0 && go == nullptr)
+    return fail(MSDA_ERROR_INVALID_ARGUMENT, "grad_output pointer is NULL");
+  const void* bufs[2] = {go, gv_like};
+  int rc = prepare(a, bufs, 2, p, ls);
+  if (rc != MSDA_SUCCESS) return rc;
+  const int64_t se = dtype_bytes(a.sdt);
+  if (!aligned(gl, se) || !aligned(ga, se))
+    return fail(MSDA_ERROR_MISALIGNED, "gradient buffers must be aligned to their element size");
+  return MSDA_SUCCESS;
+}
+
+// Launch the scatter kernel (or zero-fill the per-sample gradients when
+// C == 0).  `gacc` receives += contributions; it is not cleared here.
+int launch_accumulate(const Args& a, const Problem& p, const LaunchShape& ls, const void* go,
+                      float* gacc, void* gl, void* ga, cudaStream_t st) {
+  const int64_t nsmp = a.B * a.Q * a.H * a.L * a.P;
+  if (nsmp == 0) return MSDA_SUCCESS;
+  cudaError_t err;
+  if (a.C == 0) {
+    const int64_t se = dtype_bytes(a.sdt);
+    err = cudaMemsetAsync(gl, 0, static_cast<size_t>(nsmp * a.ndim * se), st);
+    if (err == cudaSuccess) err = cudaMemsetAsync(ga, 0, static_cast<size_t>(nsmp * se), st);
+    return err == cudaSuccess ? MSDA_SUCCESS : cuda_fail(err, "zeroing gradients");
+  }
+  err = dispatch_bwd(a.vdt, a.sdt, ls, p, go, gacc, gl, ga, st);
+  return err == cudaSuccess ? MSDA_SUCCESS : cuda_fail(err, "backward launch");
+}
+
+cudaError_t cast_from_f32(const float* src, void* dst, int dt, int64_t n, cudaStream_t st) {
+  switch (dt) {
+    case MSDA_FLOAT16: return launch_cast<__half>(src, dst, n, st);
+    case MSDA_BFLOAT16: return launch_cast<__nv_bfloat16>(src, dst, n, st);
+    default: return launch_cast<float>(src, dst, n, st);
+  }
+}
+
+int run_bwd(const Args& a, const void* go, void* gv, void* gl, void* ga, void* ws,
+            size_t ws_bytes, void* stream) {
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Problem p;
+  LaunchShape ls;
+  int rc = prepare_bwd(a, go, gv, gl, ga, p, ls);
+  if (rc != MSDA_SUCCESS) return rc;
+  const int64_t nval = a.B * a.K * a.H * a.C;
+  float* gacc = nullptr;
+  if (a.vdt == MSDA_FLOAT32) {
+    gacc = static_cast<float*>(gv);
+  } else if (nval > 0) {
+    const size_t need = static_cast<size_t>(nval) * sizeof(float);
+    if (ws == nullptr || ws_bytes < need)
+      return fail(MSDA_ERROR_WORKSPACE, "backward needs %zu workspace bytes, got %zu", need,
+                  ws == nullptr ? size_t{0} : ws_bytes);
+    if (!aligned(ws, 16)) return fail(MSDA_ERROR_WORKSPACE, "workspace must be 16-byte aligned");
+    gacc = static_cast<float*>(ws);
+  }
+  cudaError_t err;
+  if (nval > 0) {
+    err = cudaMemsetAsync(gacc, 0, static_cast<size_t>(nval) * sizeof(float), st);
+    if (err != cudaSuccess) return cuda_fail(err, "zeroing the grad_value accumulator");
+  }
+  rc = launch_accumulate(a, p, ls, go, gacc, gl, ga, st);
+  if (rc != MSDA_SUCCESS) return rc;
+  if (a.vdt != MSDA_FLOAT32 && nval > 0) {
+    err = cast_from_f32(gacc, gv, a.vdt, nval, st);
+    if (err != cudaSuccess) return cuda_fail(err, "grad_value cast launch");
+  }
+  return ok();
+}
+
+int run_bwd_accumulate(const Args& a, const void* go, float* gacc, void* gl, void* ga,
+                       void* stream) {
+  Problem p;
+  LaunchShape ls;
+  int rc = prepare_bwd(a, go, gacc, gl, ga, p, ls);
+  if (rc != MSDA_SUCCESS) return rc;
+  if (a.B * a.K * a.H * a.C > 0 && !aligned(gacc, 16))
+    return fail(MSDA_ERROR_MISALIGNED, "grad_value_accum must be 16-byte aligned");
+  rc = launch_accumulate(a, p, ls, go, gacc, gl, ga, static_cast<cudaStream_t>(stream));
+  return rc == MSDA_SUCCESS ? ok() : rc;
+}
+
+}  // namespace
+}  // namespace msda
+
+using msda::Args;
+
+#define MSDA_ARGS(ND)                                                                      \
+  Args a{ND,    value, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes, \
+         spatial_shapes_on_device, num_levels, sampling_locations, attention_weights,      \
+         sampling_dtype, num_queries, num_points, clamp_grid, clamp_eps}
+
+extern "C" {
+
+int msda2d_fwd(const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+               int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+               int spatial_shapes_on_device, int64_t num_levels,
+               const void* sampling_locations, const void* attention_weights,
+               int sampling_dtype, int64_t num_queries, int64_t num_points, int clamp_grid,
+               double clamp_eps, void* output, void* stream) {
+  MSDA_ARGS(2);
+  return msda::run_fwd(a, output, stream);
+}
+
+int msda3d_fwd(const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+               int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+               int spatial_shapes_on_device, int64_t num_levels,
+               const void* sampling_locations, const void* attention_weights,
+               int sampling_dtype, int64_t num_queries, int64_t num_points, int clamp_grid,
+               double clamp_eps, void* output, void* stream) {
+  MSDA_ARGS(3);
+  return msda::run_fwd(a, output, stream);
+}
+
+int msda2d_bwd(const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+               int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+               int spatial_shapes_on_device, int64_t num_levels,
+               const void* sampling_locations, const void* attention_weights,
+               int sampling_dtype, int64_t num_queries, int64_t num_points, int clamp_grid,
+               double clamp_eps, const void* grad_output, void* grad_value,
+               void* grad_sampling_locations, void* grad_attention_weights, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  MSDA_ARGS(2);
+  return msda::run_bwd(a, grad_output, grad_value, grad_sampling_locations,
+                       grad_attention_weights, workspace, workspace_bytes, stream);
+}
+
+int msda3d_bwd(const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+               int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+               int spatial_shapes_on_device, int64_t num_levels,
+               const void* sampling_locations, const void* attention_weights,
+               int sampling_dtype, int64_t num_queries, int64_t num_points, int clamp_grid,
+               double clamp_eps, const void* grad_output, void* grad_value,
+               void* grad_sampling_locations, void* grad_attention_weights, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  MSDA_ARGS(3);
+  return msda::run_bwd(a, grad_output, grad_value, grad_sampling_locations,
+                       grad_attention_weights, workspace, workspace_bytes, stream);
+}
+
+int msda2d_bwd_accumulate(const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+                          int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+                          int spatial_shapes_on_device, int64_t num_levels,
+                          const void* sampling_locations, const void* attention_weights,
+                          int sampling_dtype, int64_t num_queries, int64_t num_points,
+                          int clamp_grid, double clamp_eps, const void* grad_output,
+                          float* grad_value_accum, void* grad_sampling_locations,
+                          void* grad_attention_weights, void* stream) {
+  MSDA_ARGS(2);
+  return msda::run_bwd_accumulate(a, grad_output, grad_value_accum, grad_sampling_locations,
+                                  grad_attention_weights, stream);
+}
+
+int msda3d_bwd_accumulate(const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+                          int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+                          int spatial_shapes_on_device, int64_t num_levels,
+                          const void* sampling_locations, const void* attention_weights,
+                          int sampling_dtype, int64_t num_queries, int64_t num_points,
+                          int clamp_grid, double clamp_eps, const void* grad_output,
+                          float* grad_value_accum, void* grad_sampling_locations,
+                          void* grad_attention_weights, void* stream) {
+  MSDA_ARGS(3);
+  return msda::run_bwd_accumulate(a, grad_output, grad_value_accum, grad_sampling_locations,
+                                  grad_attention_weights, stream);
+}
+
+int msda_cast_from_f32(const float* src, void* dst, int dst_dtype, int64_t count, void* stream) {
+  if (count < 0 || msda::dtype_bytes(dst_dtype) == 0)
+    return msda::fail(MSDA_ERROR_INVALID_ARGUMENT, "bad count or dtype");
+  if (count == 0) return msda::ok();
+  if (src == nullptr || dst == nullptr)
+    return msda::fail(MSDA_ERROR_INVALID_ARGUMENT, "NULL buffer");
+  if (!msda::aligned(src, 16) || !msda::aligned(dst, msda::dtype_bytes(dst_dtype)))
+    return msda::fail(MSDA_ERROR_MISALIGNED, "src must be 16-byte aligned, dst element-aligned");
+  const cudaError_t err =
+      msda::cast_from_f32(src, dst, dst_dtype, count, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? msda::ok() : msda::cuda_fail(err, "cast launch");
+}
+
+size_t msda_bwd_workspace_bytes(int value_dtype, int64_t batch, int64_t num_keys,
+                                int64_t num_heads, int64_t channels) {
+  if (value_dtype == MSDA_FLOAT32 || batch <= 0 || num_keys <= 0 || num_heads <= 0 ||
+      channels <= 0)
+    return 0;
+  return static_cast<size_t>(batch * num_keys * num_heads * channels) * sizeof(float);
+}
+
+const char* msda_status_string(int status) {
+  switch (status) {
+    case MSDA_SUCCESS: return "MSDA_SUCCESS";
+    case MSDA_ERROR_INVALID_ARGUMENT: return "MSDA_ERROR_INVALID_ARGUMENT";
+    case MSDA_ERROR_UNSUPPORTED_DTYPE: return "MSDA_ERROR_UNSUPPORTED_DTYPE";
+    case MSDA_ERROR_SHAPE_MISMATCH: return "MSDA_ERROR_SHAPE_MISMATCH";
+    case MSDA_ERROR_TOO_MANY_LEVELS: return "MSDA_ERROR_TOO_MANY_LEVELS";
+    case MSDA_ERROR_INT32_OVERFLOW: return "MSDA_ERROR_INT32_OVERFLOW";
+    case MSDA_ERROR_MISALIGNED: return "MSDA_ERROR_MISALIGNED";
+    case MSDA_ERROR_WORKSPACE: return "MSDA_ERROR_WORKSPACE";
+    case MSDA_ERROR_UNSUPPORTED_CHANNELS: return "MSDA_ERROR_UNSUPPORTED_CHANNELS";
+    case MSDA_ERROR_CUDA: return "MSDA_ERROR_CUDA";
+    default: return "MSDA_ERROR_UNKNOWN";
+  }
+}
+
+const char* msda_last_error(void) { return msda::g_last_error; }
+
+int msda_abi_version(void) { return MSDA_B200_ABI_VERSION; }
+
+}  // extern "C"

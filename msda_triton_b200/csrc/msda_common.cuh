@@ -1,0 +1,268 @@
+// msda_common.cuh -- shared device code for the multi-scale deformable
+// attention (MSDA) kernels: problem description, level table, vector
+// load/convert helpers and the sampling-coordinate resolution.
+//
+// Semantics follow the reference's pure-PyTorch path
+// (src/msda_triton/pytorch/msda_2d.py:58-114, msda_3d.py:58-118), i.e.
+// grid_sample(align_corners=False, padding_mode="zeros") on a grid-space
+// clamp:
+//   g  = 2*loc - 1, clamped to [lo, hi] = [-1+eps, 1-eps] when clamp_grid
+//   ix = ((g + 1) * size - 1) / 2
+//   corners floor(ix) and floor(ix)+1 per axis, zero outside [0, size).
+// Every coordinate step is an explicitly rounded float op (__f*_rn), so nvcc
+// cannot contract it into an FMA and the cell a point falls in is the same
+// one the CPU restatement picks.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace msda {
+
+constexpr int kMaxLevels = 16;
+constexpr int kThreads = 256;
+
+// Per-level metadata.  Axis order is (x, y, z) = (W, H, D); z size is 1 in 2D.
+struct LevelTable {
+  int32_t size[kMaxLevels][3];
+  int32_t start[kMaxLevels];
+};
+
+// Everything a launch needs, passed by value as one kernel parameter.
+struct Problem {
+  const void* value;          // (B, K, H, C) of T
+  const void* loc;            // (B, Q, H, L, P, d) of TS
+  const void* attn;           // (B, Q, H, L, P) of TS
+  const int32_t* shapes_dev;  // (L, d) int32 on device, or nullptr
+  int64_t B, K, H, C, Q, L, P;
+  int32_t nv;         // vectors per (b,q,h) row: C * sizeof(T) / VB
+  int32_t log2g;      // lanes per row = 1 << log2g
+  int32_t hg;         // heads per scheduling group (divides H)
+  int32_t clamp;      // clamp_grid
+  float lo, hi;       // clamp window in grid space
+  LevelTable lv;      // host-resolved table (used when shapes_dev == nullptr)
+};
+
+// ---------------------------------------------------------------- types
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float x) { return x; }
+  static __device__ __forceinline__ float from_f(float x) { return x; }
+};
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+
+// A VB-byte chunk of a channel row, held as 32-bit words (VB >= 4) or one
+// 16-bit word (VB == 2).
+template <int VB> struct Raw { uint32_t w[VB / 4]; };
+template <> struct Raw<2> { uint16_t h; };
+
+template <int VB> __device__ __forceinline__ Raw<VB> raw_zero() {
+  Raw<VB> r;
+#pragma unroll
+  for (int i = 0; i < VB / 4; ++i) r.w[i] = 0u;
+  return r;
+}
+template <> __device__ __forceinline__ Raw<2> raw_zero<2>() { Raw<2> r; r.h = 0; return r; }
+
+// Read-only (non-coherent path) loads of one chunk.
+template <int VB> __device__ __forceinline__ Raw<VB> ld_chunk(const void* p);
+template <> __device__ __forceinline__ Raw<16> ld_chunk<16>(const void* p) {
+  uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+  Raw<16> r; r.w[0] = v.x; r.w[1] = v.y; r.w[2] = v.z; r.w[3] = v.w; return r;
+}
+template <> __device__ __forceinline__ Raw<8> ld_chunk<8>(const void* p) {
+  uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+  Raw<8> r; r.w[0] = v.x; r.w[1] = v.y; return r;
+}
+template <> __device__ __forceinline__ Raw<4> ld_chunk<4>(const void* p) {
+  Raw<4> r; r.w[0] = __ldg(reinterpret_cast<const unsigned int*>(p)); return r;
+}
+template <> __device__ __forceinline__ Raw<2> ld_chunk<2>(const void* p) {
+  Raw<2> r; r.h = __ldg(reinterpret_cast<const unsigned short*>(p)); return r;
+}
+
+template <int VB> __device__ __forceinline__ void st_chunk(void* p, const Raw<VB>& r);
+template <> __device__ __forceinline__ void st_chunk<16>(void* p, const Raw<16>& r) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(r.w[0], r.w[1], r.w[2], r.w[3]);
+}
+template <> __device__ __forceinline__ void st_chunk<8>(void* p, const Raw<8>& r) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(r.w[0], r.w[1]);
+}
+template <> __device__ __forceinline__ void st_chunk<4>(void* p, const Raw<4>& r) {
+  *reinterpret_cast<unsigned int*>(p) = r.w[0];
+}
+template <> __device__ __forceinline__ void st_chunk<2>(void* p, const Raw<2>& r) {
+  *reinterpret_cast<unsigned short*>(p) = r.h;
+}
+
+// Unpack a chunk into EPV = VB / sizeof(T) floats, and pack floats back.
+template <typename T, int VB> struct Chunk;
+template <int VB> struct Chunk<float, VB> {
+  static constexpr int EPV = VB / 4;
+  static __device__ __forceinline__ void unpack(const Raw<VB>& r, float* f) {
+#pragma unroll
+    for (int i = 0; i < EPV; ++i) f[i] = __uint_as_float(r.w[i]);
+  }
+  static __device__ __forceinline__ Raw<VB> pack(const float* f) {
+    Raw<VB> r;
+#pragma unroll
+    for (int i = 0; i < EPV; ++i) r.w[i] = __float_as_uint(f[i]);
+    return r;
+  }
+};
+template <int VB> struct Chunk<__nv_bfloat16, VB> {
+  static constexpr int EPV = VB / 2;
+  static __device__ __forceinline__ void unpack(const Raw<VB>& r, float* f) {
+#pragma unroll
+    for (int i = 0; i < VB / 4; ++i) {
+      f[2 * i] = __uint_as_float(r.w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(r.w[i] & 0xffff0000u);
+    }
+  }
+  static __device__ __forceinline__ Raw<VB> pack(const float* f) {
+    Raw<VB> r;
+#pragma unroll
+    for (int i = 0; i < VB / 4; ++i) {
+      __nv_bfloat162 v = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      r.w[i] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    return r;
+  }
+};
+template <> struct Chunk<__nv_bfloat16, 2> {
+  static constexpr int EPV = 1;
+  static __device__ __forceinline__ void unpack(const Raw<2>& r, float* f) {
+    f[0] = __uint_as_float(static_cast<uint32_t>(r.h) << 16);
+  }
+  static __device__ __forceinline__ Raw<2> pack(const float* f) {
+    __nv_bfloat16 v = __float2bfloat16_rn(f[0]);
+    Raw<2> r; r.h = *reinterpret_cast<uint16_t*>(&v); return r;
+  }
+};
+template <int VB> struct Chunk<__half, VB> {
+  static constexpr int EPV = VB / 2;
+  static __device__ __forceinline__ void unpack(const Raw<VB>& r, float* f) {
+#pragma unroll
+    for (int i = 0; i < VB / 4; ++i) {
+      uint32_t w = r.w[i];
+      float2 v = __half22float2(*reinterpret_cast<__half2*>(&w));
+      f[2 * i] = v.x; f[2 * i + 1] = v.y;
+    }
+  }
+  static __device__ __forceinline__ Raw<VB> pack(const float* f) {
+    Raw<VB> r;
+#pragma unroll
+    for (int i = 0; i < VB / 4; ++i) {
+      __half2 v = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+      r.w[i] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    return r;
+  }
+};
+template <> struct Chunk<__half, 2> {
+  static constexpr int EPV = 1;
+  static __device__ __forceinline__ void unpack(const Raw<2>& r, float* f) {
+    uint16_t h = r.h;
+    f[0] = __half2float(*reinterpret_cast<__half*>(&h));
+  }
+  static __device__ __forceinline__ Raw<2> pack(const float* f) {
+    __half v = __float2half_rn(f[0]);
+    Raw<2> r; r.h = *reinterpret_cast<uint16_t*>(&v); return r;
+  }
+};
+
+// ---------------------------------------------------------------- levels
+struct LevelSmem {
+  int32_t size[kMaxLevels][3];
+  int32_t start[kMaxLevels];
+};
+
+// Fill the CTA's level table.  Host-resolved tables are copied.  Device
+// shapes are read here (no host sync, like the reference's GPU-shape path,
+// triton/msda_2d.py:76-82); a level that would reach past K is disabled so a
+// malformed device table can never cause an out-of-range read.
+__device__ __forceinline__ void load_levels(const Problem& p, LevelSmem& s, int ndim) {
+  if (threadIdx.x == 0) {
+    if (p.shapes_dev == nullptr) {
+      for (int l = 0; l < p.L; ++l) {
+        s.size[l][0] = p.lv.size[l][0];
+        s.size[l][1] = p.lv.size[l][1];
+        s.size[l][2] = p.lv.size[l][2];
+        s.start[l] = p.lv.start[l];
+      }
+    } else {
+      int64_t start = 0;
+      for (int l = 0; l < p.L; ++l) {
+        int32_t sz[3] = {1, 1, 1};
+        int64_t n = 1;
+        for (int a = 0; a < ndim; ++a) {
+          int32_t v = p.shapes_dev[l * ndim + (ndim - 1 - a)];
+          v = v < 0 ? 0 : v;
+          sz[a] = v;
+          n *= v;
+        }
+        const bool fits = start + n <= p.K;
+        s.size[l][0] = fits ? sz[0] : 0;
+        s.size[l][1] = fits ? sz[1] : 0;
+        s.size[l][2] = fits ? sz[2] : 0;
+        s.start[l] = fits ? static_cast<int32_t>(start) : 0;
+        start += n;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------- coordinates
+// Resolve one normalised coordinate on an axis of `size` cells to the lower
+// corner index i0, the fractional offset f, and the clamp-backward mask.
+__device__ __forceinline__ void resolve_axis(float x, int32_t size, int clamp, float lo,
+                                             float hi, int32_t& i0, float& f, bool& pass) {
+  float g = __fsub_rn(__fmul_rn(2.0f, x), 1.0f);
+  pass = true;
+  if (clamp) {
+    pass = (g >= lo) && (g <= hi);
+    g = (g < lo) ? lo : g;
+    g = (g > hi) ? hi : g;
+  }
+  const float t = __fsub_rn(__fmul_rn(__fadd_rn(g, 1.0f), static_cast<float>(size)), 1.0f);
+  const float ix = __fmul_rn(t, 0.5f);
+  const float fl = floorf(ix);
+  // NaN coordinates resolve to cells -2/-1: both corners read zero padding.
+  i0 = (ix == ix) ? __float2int_rd(fl) : -2;
+  f = __fsub_rn(ix, fl);
+}
+
+// Row scheduling order.  Rows (b, q, h) are enumerated as (b, head-group,
+// q, head-in-group) so CTAs that run at the same time share a small set of
+// heads and therefore a smaller slice of `value` in L2.
+struct RowCoord {
+  int64_t b, q, h;
+};
+__device__ __forceinline__ RowCoord decode_row(uint32_t r, const Problem& p) {
+  const uint32_t hg = static_cast<uint32_t>(p.hg);
+  const uint32_t Q = static_cast<uint32_t>(p.Q);
+  const uint32_t ngroups = static_cast<uint32_t>(p.H) / hg;
+  const uint32_t hi = r % hg;
+  uint32_t t = r / hg;
+  const uint32_t q = t % Q;
+  t /= Q;
+  const uint32_t grp = t % ngroups;
+  const uint32_t b = t / ngroups;
+  RowCoord rc;
+  rc.b = b;
+  rc.q = q;
+  rc.h = static_cast<int64_t>(grp) * hg + hi;
+  return rc;
+}
+
+}  // namespace msda

@@ -1,0 +1,6 @@
+// Kernel instantiations for value dtype __nv_bfloat16, sampling dtype __nv_bfloat16.
+#include "msda_launch.cuh"
+
+namespace msda {
+MSDA_INSTANTIATE_PAIR(__nv_bfloat16, __nv_bfloat16)
+}  // namespace msda

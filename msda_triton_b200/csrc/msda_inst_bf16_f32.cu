@@ -1,0 +1,6 @@
+// Kernel instantiations for value dtype __nv_bfloat16, sampling dtype float.
+#include "msda_launch.cuh"
+
+namespace msda {
+MSDA_INSTANTIATE_PAIR(__nv_bfloat16, float)
+}  // namespace msda

@@ -1,0 +1,6 @@
+// Kernel instantiations for value dtype float, sampling dtype float.
+#include "msda_launch.cuh"
+
+namespace msda {
+MSDA_INSTANTIATE_PAIR(float, float)
+}  // namespace msda

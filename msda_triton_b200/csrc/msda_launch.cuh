@@ -1,0 +1,122 @@
+// msda_launch.cuh -- map the runtime launch shape (ndim, chunk bytes VB,
+// chunks per lane VPL) onto kernel instantiations.  Included once per
+// (value dtype, sampling dtype) pair by the msda_inst_*.cu files so those
+// compile in parallel.
+#pragma once
+
+#include "msda_kernels.cuh"
+
+namespace msda {
+
+struct LaunchShape {
+  int ndim;
+  int vb;
+  int vpl;
+  int64_t grid;  // number of CTAs
+};
+
+template <typename T, typename TS, int NDIM, int VB>
+static cudaError_t fwd_vpl(const LaunchShape& ls, const Problem& p, void* out,
+                           cudaStream_t st) {
+  const dim3 grid(static_cast<unsigned>(ls.grid));
+  T* o = static_cast<T*>(out);
+  switch (ls.vpl) {
+    case 1: msda_fwd_kernel<T, TS, NDIM, VB, 1><<<grid, kThreads, 0, st>>>(p, o); break;
+    case 2:
+      if constexpr (VB == 16) { msda_fwd_kernel<T, TS, NDIM, VB, 2><<<grid, kThreads, 0, st>>>(p, o); break; }
+      return cudaErrorInvalidValue;
+    case 4:
+      if constexpr (VB == 16) { msda_fwd_kernel<T, TS, NDIM, VB, 4><<<grid, kThreads, 0, st>>>(p, o); break; }
+      return cudaErrorInvalidValue;
+    case 8:
+      if constexpr (VB != 16) { msda_fwd_kernel<T, TS, NDIM, VB, 8><<<grid, kThreads, 0, st>>>(p, o); break; }
+      return cudaErrorInvalidValue;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+template <typename T, typename TS, int NDIM, int VB>
+static cudaError_t bwd_vpl(const LaunchShape& ls, const Problem& p, const void* grad_out,
+                           float* gacc, void* grad_loc, void* grad_attn, cudaStream_t st) {
+  const dim3 grid(static_cast<unsigned>(ls.grid));
+  const T* go = static_cast<const T*>(grad_out);
+  TS* gl = static_cast<TS*>(grad_loc);
+  TS* ga = static_cast<TS*>(grad_attn);
+  switch (ls.vpl) {
+    case 1: msda_bwd_kernel<T, TS, NDIM, VB, 1><<<grid, kThreads, 0, st>>>(p, go, gacc, gl, ga); break;
+    case 2:
+      if constexpr (VB == 16) { msda_bwd_kernel<T, TS, NDIM, VB, 2><<<grid, kThreads, 0, st>>>(p, go, gacc, gl, ga); break; }
+      return cudaErrorInvalidValue;
+    case 4:
+      if constexpr (VB == 16) { msda_bwd_kernel<T, TS, NDIM, VB, 4><<<grid, kThreads, 0, st>>>(p, go, gacc, gl, ga); break; }
+      return cudaErrorInvalidValue;
+    case 8:
+      if constexpr (VB != 16) { msda_bwd_kernel<T, TS, NDIM, VB, 8><<<grid, kThreads, 0, st>>>(p, go, gacc, gl, ga); break; }
+      return cudaErrorInvalidValue;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+template <typename T, typename TS, int NDIM>
+static cudaError_t fwd_vb(const LaunchShape& ls, const Problem& p, void* out, cudaStream_t st) {
+  switch (ls.vb) {
+    case 16: return fwd_vpl<T, TS, NDIM, 16>(ls, p, out, st);
+    case 4: return fwd_vpl<T, TS, NDIM, 4>(ls, p, out, st);
+    case 2:
+      if constexpr (sizeof(T) == 2) return fwd_vpl<T, TS, NDIM, 2>(ls, p, out, st);
+      return cudaErrorInvalidValue;
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T, typename TS, int NDIM>
+static cudaError_t bwd_vb(const LaunchShape& ls, const Problem& p, const void* grad_out,
+                          float* gacc, void* grad_loc, void* grad_attn, cudaStream_t st) {
+  switch (ls.vb) {
+    case 16: return bwd_vpl<T, TS, NDIM, 16>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 4: return bwd_vpl<T, TS, NDIM, 4>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 2:
+      if constexpr (sizeof(T) == 2)
+        return bwd_vpl<T, TS, NDIM, 2>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+      return cudaErrorInvalidValue;
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T, typename TS>
+cudaError_t launch_fwd(const LaunchShape& ls, const Problem& p, void* out, cudaStream_t st) {
+  return ls.ndim == 2 ? fwd_vb<T, TS, 2>(ls, p, out, st) : fwd_vb<T, TS, 3>(ls, p, out, st);
+}
+
+template <typename T, typename TS>
+cudaError_t launch_bwd(const LaunchShape& ls, const Problem& p, const void* grad_out,
+                       float* gacc, void* grad_loc, void* grad_attn, cudaStream_t st) {
+  return ls.ndim == 2 ? bwd_vb<T, TS, 2>(ls, p, grad_out, gacc, grad_loc, grad_attn, st)
+                      : bwd_vb<T, TS, 3>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+}
+
+template <typename T>
+cudaError_t launch_cast(const float* src, void* dst, int64_t n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  int64_t blocks = (n + kThreads * 4 - 1) / (kThreads * 4);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  msda_cast_kernel<T><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(src, static_cast<T*>(dst), n);
+  return cudaGetLastError();
+}
+
+// Explicit instantiations live in msda_inst_*.cu.
+#define MSDA_DECLARE_PAIR(T, TS)                                                              \
+  extern template cudaError_t launch_fwd<T, TS>(const LaunchShape&, const Problem&, void*,     \
+                                                cudaStream_t);                                 \
+  extern template cudaError_t launch_bwd<T, TS>(const LaunchShape&, const Problem&,            \
+                                                const void*, float*, void*, void*,             \
+                                                cudaStream_t);
+#define MSDA_INSTANTIATE_PAIR(T, TS)                                                          \
+  template cudaError_t launch_fwd<T, TS>(const LaunchShape&, const Problem&, void*,            \
+                                         cudaStream_t);                                        \
+  template cudaError_t launch_bwd<T, TS>(const LaunchShape&, const Problem&, const void*,      \
+                                         float*, void*, void*, cudaStream_t);
+
+}  // namespace msda

@@ -1,0 +1,123 @@
+"""The C-ABI library on the CPU: it loads, exports every symbol the public
+header declares, and rejects bad arguments on the host before any CUDA call
+(so these checks need no GPU)."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from msda_triton_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "msda_b200.h")
+
+
+def _declared_symbols() -> list[str]:
+    text = open(HEADER).read()
+    return re.findall(r"MSDA_API\s+[\w\s\*]+?\b(\w+)\s*\(", text)
+
+
+def test_library_loads_and_reports_abi():
+    lib = _lib.lib()
+    assert lib.msda_abi_version() == _lib.ABI_VERSION
+
+
+def test_exports_every_declared_symbol():
+    declared = _declared_symbols()
+    assert set(declared) == set(_lib.EXPORTED_SYMBOLS), declared
+    handle = ctypes.CDLL(_lib.LIB_PATH)
+    for name in declared:
+        assert hasattr(handle, name), f"{name} declared in msda_b200.h but not exported"
+
+
+def test_status_strings():
+    assert _lib.status_string(0) == "MSDA_SUCCESS"
+    assert _lib.status_string(_lib.ERROR_SHAPE_MISMATCH) == "MSDA_ERROR_SHAPE_MISMATCH"
+    assert _lib.status_string(12345) == "MSDA_ERROR_UNKNOWN"
+
+
+def test_workspace_bytes():
+    lib = _lib.lib()
+    assert lib.msda_bwd_workspace_bytes(_lib.FLOAT32, 2, 100, 8, 32) == 0
+    assert lib.msda_bwd_workspace_bytes(_lib.BFLOAT16, 2, 100, 8, 32) == 2 * 100 * 8 * 32 * 4
+    assert lib.msda_bwd_workspace_bytes(_lib.FLOAT16, 0, 100, 8, 32) == 0
+
+
+# A fake device address: every case below fails validation on the host before
+# any pointer is dereferenced or any CUDA call is made.
+FAKE = 0x10000
+
+
+def _fwd(ndim=2, vdt=_lib.FLOAT32, B=1, K=20, H=2, C=8, shapes=((4, 5),), L=None,
+         sdt=None, Q=3, P=2, clamp=1, eps=1e-4, value=FAKE, out=FAKE, on_dev=0):
+    lib = _lib.lib()
+    shp = np.ascontiguousarray(np.array(shapes, dtype=np.int32))
+    L = len(shapes) if L is None else L
+    sdt = vdt if sdt is None else sdt
+    fn = lib.msda2d_fwd if ndim == 2 else lib.msda3d_fwd
+    return fn(value, vdt, B, K, H, C, shp.ctypes.data, on_dev, L, FAKE, FAKE, sdt, Q, P,
+              clamp, eps, out, None)
+
+
+def test_rejects_bad_dtype():
+    assert _fwd(vdt=7) == _lib.ERROR_UNSUPPORTED_DTYPE
+    assert "fp32, fp16, and bf16" in _lib.last_error()
+    # sampling dtype must be the value dtype or fp32
+    assert _fwd(vdt=_lib.FLOAT32, sdt=_lib.BFLOAT16) == _lib.ERROR_UNSUPPORTED_DTYPE
+
+
+def test_rejects_k_mismatch_with_host_shapes():
+    assert _fwd(K=21) == _lib.ERROR_SHAPE_MISMATCH
+    assert "does not match sum of spatial shapes" in _lib.last_error()
+
+
+def test_rejects_too_many_levels():
+    shapes = [(1, 1)] * (_lib.MAX_LEVELS + 1)
+    assert _fwd(K=len(shapes), shapes=shapes) == _lib.ERROR_TOO_MANY_LEVELS
+
+
+def test_rejects_int32_overflow():
+    assert _fwd(K=2**31, shapes=[(2**16, 2**15)]) == _lib.ERROR_INT32_OVERFLOW
+    assert "exceeds int32 range" in _lib.last_error()
+
+
+def test_rejects_negative_dims_and_bad_eps():
+    assert _fwd(Q=-1) == _lib.ERROR_INVALID_ARGUMENT
+    assert _fwd(eps=1.5) == _lib.ERROR_INVALID_ARGUMENT
+
+
+def test_rejects_misaligned_buffers():
+    assert _fwd(value=FAKE + 2) == _lib.ERROR_MISALIGNED
+
+
+def test_rejects_huge_channel_rows():
+    assert _fwd(C=4096) == _lib.ERROR_UNSUPPORTED_CHANNELS
+
+
+def test_empty_problem_is_a_noop():
+    # Q = 0: nothing to launch, success without touching any buffer.
+    assert _fwd(Q=0) == _lib.SUCCESS
+    assert _lib.last_error() == ""
+
+
+def test_bwd_requires_workspace_for_half_types():
+    lib = _lib.lib()
+    shp = np.array([[4, 5]], dtype=np.int32)
+    rc = lib.msda2d_bwd(FAKE, _lib.BFLOAT16, 1, 20, 2, 8, shp.ctypes.data, 0, 1, FAKE, FAKE,
+                        _lib.BFLOAT16, 3, 2, 1, 1e-4, FAKE, FAKE, FAKE, FAKE, None, 0, None)
+    assert rc == _lib.ERROR_WORKSPACE
+    assert "workspace" in _lib.last_error()
+
+
+@pytest.mark.parametrize("ndim", [2, 3])
+def test_shape_row_order(ndim):
+    # Shapes rows are (H, W) / (D, H, W): K is their product sum either way.
+    shapes = [(3, 5)] if ndim == 2 else [(2, 3, 5)]
+    K = int(np.prod(shapes[0]))
+    assert _fwd(ndim=ndim, K=K, shapes=shapes, Q=0) == _lib.SUCCESS
+    assert _fwd(ndim=ndim, K=K + 1, shapes=shapes, Q=0) == _lib.ERROR_SHAPE_MISMATCH
