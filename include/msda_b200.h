@@ -37,8 +37,8 @@
  * for every dtype.
  *
  * Memory and threading: the caller owns every buffer.  The library allocates
- * nothing; the backward of fp16/bf16 inputs needs an fp32 workspace of
- * msda_bwd_workspace_bytes() bytes (0 for fp32).  Every call is asynchronous
+ * nothing; the backward needs a workspace of msda_bwd_workspace_bytes() bytes
+ * (256-byte aligned).  Every call is asynchronous
  * on `stream` (a cudaStream_t; NULL = legacy default stream) and keeps no
  * state between calls, so calls on different streams may run concurrently.
  * grad_* buffers need no initialisation: they are fully overwritten.
@@ -63,7 +63,7 @@ extern "C" {
 #define MSDA_API
 #endif
 
-#define MSDA_B200_ABI_VERSION 1
+#define MSDA_B200_ABI_VERSION 2
 #define MSDA_MAX_LEVELS 16
 
 typedef enum msda_dtype {
@@ -153,11 +153,20 @@ MSDA_API int msda3d_bwd_accumulate(const void* value, int value_dtype, int64_t b
 MSDA_API int msda_cast_from_f32(const float* src, void* dst, int dst_dtype, int64_t count,
                                 void* stream);
 
-/* Bytes of fp32 workspace msda{2,3}d_bwd needs (B*K*H*C*4 for fp16/bf16
- * values, 0 for fp32).  The reference allocates its gradient buffers with
- * torch.zeros_like (triton/msda_3d.py:941-944); here the caller allocates. */
-MSDA_API size_t msda_bwd_workspace_bytes(int value_dtype, int64_t batch, int64_t num_keys,
-                                int64_t num_heads, int64_t channels);
+/* Workspace bytes msda{2,3}d_bwd needs for this problem (it depends on the
+ * level shapes, which must be the same pointer/residency as in the call).
+ * Large problems with host-resident shapes use the binned backward (sample
+ * bins + a small fp32 accumulator for coarse levels); others the
+ * gather/scatter backward (B*K*H*C*4 bytes of fp32 accumulator for fp16/bf16
+ * values, 0 for fp32).  The plan assumes value, grad_output and grad_value
+ * are 16-byte aligned.  The reference allocates its gradient buffers with
+ * torch.zeros_like (triton/msda_3d.py:941-944); here the caller allocates.
+ * Returns 0 when no workspace is needed or the arguments are invalid. */
+MSDA_API size_t msda_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batch,
+                                         int64_t num_keys, int64_t num_heads, int64_t channels,
+                                         const int32_t* spatial_shapes,
+                                         int spatial_shapes_on_device, int64_t num_levels,
+                                         int64_t num_queries, int64_t num_points);
 
 /* Name of a status code ("MSDA_SUCCESS", ...). */
 MSDA_API const char* msda_status_string(int status);

@@ -187,7 +187,9 @@ def backward(
     grad_loc = torch.empty_like(loc)
     grad_attn = torch.empty_like(attn)
     lib = _lib.lib()
-    ws_bytes = lib.msda_bwd_workspace_bytes(_DTYPE_CODE[value.dtype], B, K, H, C)
+    Q, L, P = loc.shape[1], loc.shape[3], loc.shape[4]
+    ws_bytes = lib.msda_bwd_workspace_bytes(ndim, _DTYPE_CODE[value.dtype], B, K, H, C,
+                                            shapes.data_ptr(), int(on_dev), L, Q, P)
     ws = torch.empty((ws_bytes,), device=value.device, dtype=torch.uint8) if ws_bytes else None
     fn = lib.msda2d_bwd if ndim == 2 else lib.msda3d_bwd
     with torch.cuda.device(value.device):

@@ -31,7 +31,7 @@ FLOAT16 = 1
 BFLOAT16 = 2
 
 MAX_LEVELS = 16
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 EXPORTED_SYMBOLS = (
     "msda2d_fwd",
@@ -99,7 +99,7 @@ def lib() -> ctypes.CDLL:
                 fn.restype = _int
             handle.msda_cast_from_f32.argtypes = [_vp, _vp, _int, _i64, _vp]
             handle.msda_cast_from_f32.restype = _int
-            handle.msda_bwd_workspace_bytes.argtypes = [_int, _i64, _i64, _i64, _i64]
+            handle.msda_bwd_workspace_bytes.argtypes = [_int, _int, _i64, _i64, _i64, _i64, _vp, _int, _i64, _i64, _i64]
             handle.msda_bwd_workspace_bytes.restype = ctypes.c_size_t
             handle.msda_status_string.argtypes = [_int]
             handle.msda_status_string.restype = ctypes.c_char_p

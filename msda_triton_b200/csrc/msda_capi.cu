@@ -3,9 +3,11 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
 #include <cstring>
 
 #include "../../include/msda_b200.h"
+#include "msda_binned_launch.cuh"
 #include "msda_launch.cuh"
 
 namespace msda {
@@ -15,6 +17,11 @@ MSDA_DECLARE_PAIR(__half, __half)
 MSDA_DECLARE_PAIR(__half, float)
 MSDA_DECLARE_PAIR(__nv_bfloat16, __nv_bfloat16)
 MSDA_DECLARE_PAIR(__nv_bfloat16, float)
+MSDA_DECLARE_BINNED(float, float)
+MSDA_DECLARE_BINNED(__half, __half)
+MSDA_DECLARE_BINNED(__half, float)
+MSDA_DECLARE_BINNED(__nv_bfloat16, __nv_bfloat16)
+MSDA_DECLARE_BINNED(__nv_bfloat16, float)
 
 namespace {
 
@@ -295,6 +302,153 @@ cudaError_t cast_from_f32(const float* src, void* dst, int dt, int64_t n, cudaSt
   }
 }
 
+// ------------------------------------------------------------ backward plan
+// The backward has two implementations: the gather/scatter kernel (any
+// shape; fp32 atomics into grad_value or an fp32 workspace) and the binned
+// tile kernel (msda_binned.cuh) for large problems with host-resident shapes
+// and 16-byte channel rows.  The plan picks one and lays out the workspace.
+constexpr int64_t kBinnedMinSamples = int64_t{1} << 18;
+constexpr int kBinSmemBudget = 110 * 1024;   // two tile CTAs per SM
+constexpr int64_t kAtomicLevelRecords = 8192;
+constexpr int kMaxTilesPerBh = 12288;
+
+struct BwdPlan {
+  bool binned = false;
+  BinPlan bp{};
+  BinLaunch bl{};
+  size_t off[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // counts, starts, cursor, item_start, item_counter, scan_tmp, records, acc
+  size_t ws_bytes = 0;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
+
+bool choose_tile(int ndim, int64_t row_bytes, int64_t C, int budget, int32_t* tile, int* smem) {
+  static const int32_t c3[][3] = {{8, 8, 8}, {8, 8, 4}, {8, 4, 4}, {4, 4, 4}, {4, 4, 2}, {4, 2, 2}, {2, 2, 2}};
+  static const int32_t c2[][3] = {{32, 16, 1}, {16, 16, 1}, {16, 8, 1}, {8, 8, 1}, {8, 4, 1}, {4, 4, 1}, {2, 2, 1}};
+  const char* env = std::getenv("MSDA_BIN_TILE");
+  int32_t forced[3] = {0, 0, 1};
+  if (env && std::sscanf(env, "%d,%d,%d", &forced[0], &forced[1], &forced[2]) >= 2) {
+    if (ndim == 2) forced[2] = 1;
+  } else {
+    forced[0] = 0;
+  }
+  for (int i = -1; i < 7; ++i) {
+    const int32_t* t = i < 0 ? forced : (ndim == 3 ? c3[i] : c2[i]);
+    if (t[0] <= 0 || t[1] <= 0 || t[2] <= 0) continue;
+    const int64_t halo = int64_t{t[0] + 1} * (t[1] + 1) * (ndim == 3 ? t[2] + 1 : 1);
+    const int64_t vox = int64_t{t[0]} * t[1] * t[2];
+    const int64_t bytes = halo * row_bytes + vox * C * 4;
+    if (bytes <= budget || (i < 0 && bytes <= 220 * 1024)) {
+      tile[0] = t[0]; tile[1] = t[1]; tile[2] = t[2];
+      *smem = static_cast<int>(bytes);
+      return true;
+    }
+  }
+  return false;
+}
+
+void plan_bwd(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan& pl) {
+  const int64_t e = dtype_bytes(a.vdt);
+  const int64_t nval = a.B * a.K * a.H * a.C;
+  const int64_t samples = a.B * a.Q * a.H * a.L * a.P;
+  pl = BwdPlan{};
+  const char* env = std::getenv("MSDA_BWD_PATH");
+  // The binned path is opt-in (MSDA_BWD_PATH=binned) until it outruns the
+  // gather/scatter kernel on the benchmark shapes.
+  const bool force_binned = env && std::strcmp(env, "binned") == 0;
+  const bool force_gather = !force_binned;
+  bool ok_binned = !force_gather && p.shapes_dev == nullptr && ls.vb == 16 && ls.vpl == 1 &&
+                   samples > 0 && a.C > 0 && (force_binned || samples >= kBinnedMinSamples) &&
+                   a.Q * a.P < (int64_t{1} << 30) && samples * (int64_t{1} << a.ndim) < INT32_MAX;
+  for (int64_t l = 0; ok_binned && l < a.L; ++l)
+    for (int ax = 0; ax < 3; ++ax) ok_binned = ok_binned && p.lv.size[l][ax] > 0;
+  int smem = 0;
+  BinPlan& bp = pl.bp;
+  if (ok_binned) {
+    const char* sb = std::getenv("MSDA_BIN_SMEM_KB");
+    const int budget = sb ? std::atoi(sb) * 1024 : kBinSmemBudget;
+    ok_binned = choose_tile(a.ndim, a.C * e, a.C, budget, bp.tile, &smem);
+  }
+  if (ok_binned) {
+    int64_t ntl = 0;
+    const double straddle = (1.0 + 1.0 / bp.tile[0]) * (1.0 + 1.0 / bp.tile[1]) *
+                            (a.ndim == 3 ? 1.0 + 1.0 / bp.tile[2] : 1.0);
+    int64_t acc_keys = 0;
+    // Tuning / test knobs: records per tile above which a level reduces
+    // through the fp32 accumulator, and records per work item there.
+    const char* ar = std::getenv("MSDA_BIN_ATOMIC_RECORDS");
+    const int64_t atomic_records = ar ? std::atoll(ar) : kAtomicLevelRecords;
+    const char* sm = std::getenv("MSDA_BIN_SMAX");
+    bp.s_max = sm && std::atoi(sm) > 0 ? std::atoi(sm) : 2048;
+    for (int64_t l = 0; l < a.L; ++l) {
+      int64_t nt = 1;
+      for (int ax = 0; ax < 3; ++ax) {
+        bp.ntile[l][ax] = (p.lv.size[l][ax] + bp.tile[ax] - 1) / bp.tile[ax];
+        nt *= bp.ntile[l][ax];
+      }
+      bp.tile_base[l] = static_cast<int32_t>(ntl);
+      ntl += nt;
+      const double expect = static_cast<double>(a.Q * a.P) * straddle / static_cast<double>(nt);
+      if (expect > static_cast<double>(atomic_records)) {
+        bp.atomic_mask |= 1 << l;
+        const int64_t nkey = int64_t{p.lv.size[l][0]} * p.lv.size[l][1] * p.lv.size[l][2];
+        bp.acc_start[l] = static_cast<int32_t>(a.vdt == MSDA_FLOAT32 ? p.lv.start[l] : acc_keys);
+        acc_keys += nkey;
+      }
+    }
+    if (a.vdt == MSDA_FLOAT32) acc_keys = a.K;
+    ok_binned = ntl <= kMaxTilesPerBh;
+    bp.ntl = static_cast<int32_t>(ntl);
+    bp.acc_keys = acc_keys;
+    const int64_t rpc = std::max<int64_t>(1, 32768 / std::max<int64_t>(1, a.L * a.P));
+    bp.rows_per_chunk = static_cast<int32_t>(rpc);
+    bp.nchunk = static_cast<int32_t>((a.Q + rpc - 1) / rpc);
+    bp.nlevels = static_cast<int32_t>(a.L);
+  }
+  if (!ok_binned) {
+    pl.binned = false;
+    pl.ws_bytes = (a.vdt == MSDA_FLOAT32) ? 0 : static_cast<size_t>(nval) * sizeof(float);
+    return;
+  }
+  pl.binned = true;
+  const int64_t nb = a.B * a.H * bp.ntl;
+  pl.bl.ndim = a.ndim;
+  pl.bl.nb = nb;
+  pl.bl.smem_main = smem;
+  pl.bl.fp32_value = a.vdt == MSDA_FLOAT32;
+  const int64_t scan_blocks = (nb + 1 + kScanThreads * kScanItems - 1) / (kScanThreads * kScanItems);
+  const int64_t max_records = samples * (int64_t{1} << a.ndim);
+  const size_t sizes[8] = {
+      static_cast<size_t>(nb) * 4, static_cast<size_t>(nb + 1) * 4, static_cast<size_t>(nb) * 4,
+      static_cast<size_t>(nb + 1) * 4, 4, static_cast<size_t>(scan_blocks + 1) * 4,
+      static_cast<size_t>(max_records) * 4,
+      (bp.atomic_mask && a.vdt != MSDA_FLOAT32)
+          ? static_cast<size_t>(a.B * bp.acc_keys * a.H * a.C) * sizeof(float) : 0};
+  size_t off = 0;
+  for (int i = 0; i < 8; ++i) {
+    pl.off[i] = off;
+    off += align256(sizes[i]);
+  }
+  pl.ws_bytes = off;
+}
+
+cudaError_t dispatch_bwd_binned(int vdt, int sdt, const BinLaunch& bl, const Problem& p,
+                                const BinPlan& bp, const BinBuffers& bb, const void* go, void* gv,
+                                void* gl, void* ga, cudaStream_t st) {
+  switch (vdt) {
+    case MSDA_FLOAT32: return launch_bwd_binned<float, float>(bl, p, bp, bb, go, gv, gl, ga, st);
+    case MSDA_FLOAT16:
+      return sdt == MSDA_FLOAT32
+                 ? launch_bwd_binned<__half, float>(bl, p, bp, bb, go, gv, gl, ga, st)
+                 : launch_bwd_binned<__half, __half>(bl, p, bp, bb, go, gv, gl, ga, st);
+    default:
+      return sdt == MSDA_FLOAT32
+                 ? launch_bwd_binned<__nv_bfloat16, float>(bl, p, bp, bb, go, gv, gl, ga, st)
+                 : launch_bwd_binned<__nv_bfloat16, __nv_bfloat16>(bl, p, bp, bb, go, gv, gl,
+                                                                   ga, st);
+  }
+}
+
 int run_bwd(const Args& a, const void* go, void* gv, void* gl, void* ga, void* ws,
             size_t ws_bytes, void* stream) {
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -302,19 +456,37 @@ int run_bwd(const Args& a, const void* go, void* gv, void* gl, void* ga, void* w
   LaunchShape ls;
   int rc = prepare_bwd(a, go, gv, gl, ga, p, ls);
   if (rc != MSDA_SUCCESS) return rc;
+  BwdPlan pl;
+  plan_bwd(a, p, ls, pl);
   const int64_t nval = a.B * a.K * a.H * a.C;
+  if (pl.ws_bytes > 0) {
+    if (ws == nullptr || ws_bytes < pl.ws_bytes)
+      return fail(MSDA_ERROR_WORKSPACE, "backward needs %zu workspace bytes, got %zu",
+                  pl.ws_bytes, ws == nullptr ? size_t{0} : ws_bytes);
+    if (!aligned(ws, 256)) return fail(MSDA_ERROR_WORKSPACE, "workspace must be 256-byte aligned");
+  }
+  cudaError_t err;
+  if (pl.binned) {
+    char* w = static_cast<char*>(ws);
+    BinBuffers bb;
+    bb.counts = reinterpret_cast<int32_t*>(w + pl.off[0]);
+    bb.starts = reinterpret_cast<int32_t*>(w + pl.off[1]);
+    bb.cursor = reinterpret_cast<int32_t*>(w + pl.off[2]);
+    bb.item_start = reinterpret_cast<int32_t*>(w + pl.off[3]);
+    bb.item_counter = reinterpret_cast<int32_t*>(w + pl.off[4]);
+    bb.scan_tmp = reinterpret_cast<int32_t*>(w + pl.off[5]);
+    bb.records = reinterpret_cast<int32_t*>(w + pl.off[6]);
+    bb.acc = a.vdt == MSDA_FLOAT32 ? static_cast<float*>(gv) : reinterpret_cast<float*>(w + pl.off[7]);
+    err = dispatch_bwd_binned(a.vdt, a.sdt, pl.bl, p, pl.bp, bb, go, gv, gl, ga, st);
+    if (err != cudaSuccess) return cuda_fail(err, "binned backward launch");
+    return ok();
+  }
   float* gacc = nullptr;
   if (a.vdt == MSDA_FLOAT32) {
     gacc = static_cast<float*>(gv);
   } else if (nval > 0) {
-    const size_t need = static_cast<size_t>(nval) * sizeof(float);
-    if (ws == nullptr || ws_bytes < need)
-      return fail(MSDA_ERROR_WORKSPACE, "backward needs %zu workspace bytes, got %zu", need,
-                  ws == nullptr ? size_t{0} : ws_bytes);
-    if (!aligned(ws, 16)) return fail(MSDA_ERROR_WORKSPACE, "workspace must be 16-byte aligned");
     gacc = static_cast<float*>(ws);
   }
-  cudaError_t err;
   if (nval > 0) {
     err = cudaMemsetAsync(gacc, 0, static_cast<size_t>(nval) * sizeof(float), st);
     if (err != cudaSuccess) return cuda_fail(err, "zeroing the grad_value accumulator");
@@ -437,12 +609,22 @@ int msda_cast_from_f32(const float* src, void* dst, int dst_dtype, int64_t count
   return err == cudaSuccess ? msda::ok() : msda::cuda_fail(err, "cast launch");
 }
 
-size_t msda_bwd_workspace_bytes(int value_dtype, int64_t batch, int64_t num_keys,
-                                int64_t num_heads, int64_t channels) {
-  if (value_dtype == MSDA_FLOAT32 || batch <= 0 || num_keys <= 0 || num_heads <= 0 ||
-      channels <= 0)
-    return 0;
-  return static_cast<size_t>(batch * num_keys * num_heads * channels) * sizeof(float);
+size_t msda_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batch, int64_t num_keys,
+                                int64_t num_heads, int64_t channels,
+                                const int32_t* spatial_shapes, int spatial_shapes_on_device,
+                                int64_t num_levels, int64_t num_queries, int64_t num_points) {
+  // Plan with 256-byte aligned stand-in pointers (never dereferenced).
+  void* fake = reinterpret_cast<void*>(uintptr_t{256});
+  Args a{ndim, fake, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,
+         spatial_shapes_on_device, num_levels, fake, fake, value_dtype, num_queries, num_points,
+         1, 1e-4};
+  msda::Problem p;
+  msda::LaunchShape ls;
+  const void* bufs[2] = {fake, fake};
+  if (msda::prepare(a, bufs, 2, p, ls) != MSDA_SUCCESS) return 0;
+  msda::BwdPlan pl;
+  msda::plan_bwd(a, p, ls, pl);
+  return pl.ws_bytes;
 }
 
 const char* msda_status_string(int status) {

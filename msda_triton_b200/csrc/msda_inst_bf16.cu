@@ -1,6 +1,8 @@
 // Kernel instantiations for value dtype __nv_bfloat16, sampling dtype __nv_bfloat16.
+#include "msda_binned_launch.cuh"
 #include "msda_launch.cuh"
 
 namespace msda {
 MSDA_INSTANTIATE_PAIR(__nv_bfloat16, __nv_bfloat16)
+MSDA_INSTANTIATE_BINNED(__nv_bfloat16, __nv_bfloat16)
 }  // namespace msda

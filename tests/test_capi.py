@@ -41,11 +41,33 @@ def test_status_strings():
     assert _lib.status_string(12345) == "MSDA_ERROR_UNKNOWN"
 
 
-def test_workspace_bytes():
-    lib = _lib.lib()
-    assert lib.msda_bwd_workspace_bytes(_lib.FLOAT32, 2, 100, 8, 32) == 0
-    assert lib.msda_bwd_workspace_bytes(_lib.BFLOAT16, 2, 100, 8, 32) == 2 * 100 * 8 * 32 * 4
-    assert lib.msda_bwd_workspace_bytes(_lib.FLOAT16, 0, 100, 8, 32) == 0
+def _ws(dtype, B, shapes, H, C, Q, P, on_dev=0):
+    shp = np.ascontiguousarray(np.array(shapes, dtype=np.int32))
+    K = int(sum(np.prod(s) for s in shapes))
+    return _lib.lib().msda_bwd_workspace_bytes(len(shapes[0]), dtype, B, K, H, C, shp.ctypes.data,
+                                               on_dev, len(shapes), Q, P)
+
+
+def test_workspace_bytes_gather_path():
+    # Small problems use the gather/scatter backward: an fp32 accumulator for
+    # half-precision values, nothing for fp32.
+    assert _ws(_lib.FLOAT32, 2, [(10, 10)], 8, 32, 50, 4) == 0
+    assert _ws(_lib.BFLOAT16, 2, [(10, 10)], 8, 32, 50, 4) == 2 * 100 * 8 * 32 * 4
+    assert _ws(_lib.FLOAT16, 0, [(10, 10)], 8, 32, 50, 4) == 0
+
+
+def test_workspace_bytes_binned_path(monkeypatch):
+    # Host shapes, binned backward selected: records (at most 2^d per sample)
+    # plus bucket tables; far below the fp32 accumulator.
+    monkeypatch.setenv("MSDA_BWD_PATH", "binned")
+    B, H, C, Q, P = 2, 8, 32, 20000, 4
+    shapes = [(32, 64, 64), (16, 32, 32), (8, 16, 16)]
+    ws = _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P)
+    samples = B * Q * H * len(shapes) * P
+    assert samples * 8 * 4 <= ws < samples * 8 * 4 + 64 * 2**20
+    # device-resident shapes cannot be planned on the host: gather path
+    K = sum(int(np.prod(s)) for s in shapes)
+    assert _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P, on_dev=1) == B * K * H * C * 4
 
 
 # A fake device address: every case below fails validation on the host before
