@@ -168,6 +168,26 @@ MSDA_API size_t msda_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batc
                                          int spatial_shapes_on_device, int64_t num_levels,
                                          int64_t num_queries, int64_t num_points);
 
+/* Backward pass that allocates nothing, for callers that cannot allocate
+ * device memory (an inference-engine plugin whose enqueue must not call
+ * cudaMalloc, code running while another framework owns the device memory
+ * pool, an FFI without access to a CUDA allocator).  No counterpart in the
+ * reference: it is msda{2,3}d_bwd (ndim = 2 or 3) with the workspace taken
+ * from a 32 MiB array inside the library's device image, reserved on every
+ * GPU that loads the library until the process exits.  Problems needing more
+ * than 32 MiB of scratch (msda_bwd_workspace_bytes) are rejected with
+ * MSDA_ERROR_WORKSPACE.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress); make that first call outside any
+ * stream capture.  All calls share the array: calls whose GPU work overlaps
+ * on one device race; serialise them.  Each call clears what it uses. */
+MSDA_API int msda_bwd_static_scratch(int ndim, const void* value, int value_dtype, int64_t batch,
+               int64_t num_keys, int64_t num_heads, int64_t channels,
+               const int32_t* spatial_shapes, int spatial_shapes_on_device, int64_t num_levels,
+               const void* sampling_locations, const void* attention_weights,
+               int sampling_dtype, int64_t num_queries, int64_t num_points, int clamp_grid,
+               double clamp_eps, const void* grad_output, void* grad_value,
+               void* grad_sampling_locations, void* grad_attention_weights, void* stream);
+
 /* Name of a status code ("MSDA_SUCCESS", ...). */
 MSDA_API const char* msda_status_string(int status);
 

@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "msda2d_bwd_accumulate",
     "msda3d_bwd_accumulate",
     "msda_cast_from_f32",
+    "msda_bwd_static_scratch",
     "msda_bwd_workspace_bytes",
     "msda_status_string",
     "msda_last_error",
@@ -97,6 +98,8 @@ def lib() -> ctypes.CDLL:
                 fn = getattr(handle, name)
                 fn.argtypes = _ACC_ARGS
                 fn.restype = _int
+            handle.msda_bwd_static_scratch.argtypes = [_int] + _BWD_ARGS[:-3] + [_vp]
+            handle.msda_bwd_static_scratch.restype = _int
             handle.msda_cast_from_f32.argtypes = [_vp, _vp, _int, _i64, _vp]
             handle.msda_cast_from_f32.restype = _int
             handle.msda_bwd_workspace_bytes.argtypes = [_int, _int, _i64, _i64, _i64, _i64, _vp, _int, _i64, _i64, _i64]

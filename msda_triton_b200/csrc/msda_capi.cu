@@ -513,6 +513,10 @@ int run_bwd_accumulate(const Args& a, const void* go, float* gacc, void* gl, voi
 }
 
 }  // namespace
+
+// Record an error for msda_last_error() from another translation unit.
+int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 }  // namespace msda
 
 using msda::Args;
