@@ -30,7 +30,6 @@
 
 namespace msda {
 
-constexpr int kBinThreads = 512;      // threads of the binned main kernel
 constexpr int kScanThreads = 1024;
 constexpr int kScanItems = 8;         // elements per thread in the scan
 
@@ -308,9 +307,25 @@ __device__ __forceinline__ void rotate_left(float* x, int r) {
 }
 
 // Work item: one tile of one (b, h, level), records [r0, r1).  VB = 16 only
-// (C * sizeof(T) % 16 == 0); G lanes per record own EPV channels each.
+// (C * sizeof(T) % 16 == 0, C % 8 == 0).
+//
+// Records are processed in chunks of R = kTileThreads / G (G lanes per record,
+// each owning EPV channels):
+//   A. per record: corner weights, dot products against the staged value rows
+//      (primary records: write grad_attn / grad_loc), stage a*grad_out in
+//      shared memory, and emit one (voxel, weight) pair per corner the tile
+//      owns, counting pairs per voxel with an integer shared-memory atomic;
+//   B. exclusive scan of the per-voxel counts;
+//   C. scatter the pairs into voxel order;
+//   D. every thread owns fixed (voxel, 8-channel) units and adds
+//      w * a*grad_out for the voxel's pairs into registers.
+// The value gradient of the tile is never touched by an atomic: it lives in
+// the owners' registers until the item ends and is written once.
+constexpr int kTileThreads = 256;
+constexpr int kMaxUnitsPerThread = 8;
+
 template <typename T, typename TS, int NDIM>
-__global__ void __launch_bounds__(kBinThreads, 2)
+__global__ void __launch_bounds__(kTileThreads, 2)
     msda_bwd_binned_kernel(const Problem p, const BinPlan bp, const BinBuffers bb,
                            const T* __restrict__ grad_out, T* __restrict__ grad_value,
                            TS* __restrict__ grad_loc, TS* __restrict__ grad_attn) {
@@ -319,32 +334,39 @@ __global__ void __launch_bounds__(kBinThreads, 2)
   constexpr int NC = 1 << NDIM;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ LevelSmem lv;
-  __shared__ int32_t s_item[4];
+  __shared__ int32_t s_item[2];
   load_levels(p, lv, NDIM);
 
   const int TX = bp.tile[0], TY = bp.tile[1], TZ = bp.tile[2];
   const int HX = TX + 1, HY = TY + 1, HZ = (NDIM == 3) ? TZ + 1 : 1;
   const int nhalo = HX * HY * HZ;
-  const int ntile_vox = TX * TY * TZ;
-  const int64_t C = p.C;
-  const int64_t row_bytes = C * static_cast<int64_t>(sizeof(T));
-  unsigned char* s_val = smem;                                          // nhalo rows
-  float* s_grad = reinterpret_cast<float*>(smem + nhalo * row_bytes);   // ntile_vox * C
-
+  const int V = TX * TY * TZ;
+  const int C = static_cast<int>(p.C);
+  const int NU = C / 8;                       // 8-channel units per voxel
+  const int64_t row_bytes = static_cast<int64_t>(C) * sizeof(T);
   const int G = 1 << p.log2g;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int slot = lane / G;                 // record slot within the warp
-  const int j = lane & (G - 1);              // chunk owned by this lane
-  const int slots_per_warp = 32 / G;
-  const int groups = (kBinThreads / 32) * slots_per_warp;
+  const int R = kTileThreads / G;             // records per chunk
+  // Shared memory carve-up (byte offsets are multiples of 16).
+  unsigned char* s_val = smem;                                                // nhalo rows
+  float* s_go = reinterpret_cast<float*>(smem + nhalo * row_bytes);           // R x C
+  int32_t* s_pvr = reinterpret_cast<int32_t*>(s_go + R * C);                  // R*8: voxel | rank<<10
+  float* s_pw = reinterpret_cast<float*>(s_pvr + R * 8);                      // R*8: weight
+  int2* s_sorted = reinterpret_cast<int2*>(s_pw + R * 8);                     // R*8: (slot, w)
+  int32_t* s_cnt = reinterpret_cast<int32_t*>(s_sorted + R * 8);              // V
+  int32_t* s_off = s_cnt + V;                                                 // V + 1
+  __shared__ int32_t s_warp[32];
+
+  const int slot = threadIdx.x / G;           // record slot within the chunk
+  const int j = threadIdx.x & (G - 1);        // channel chunk of this lane
   const bool has = j < p.nv;
-  const int rot = slot & (EPV - 1);          // bank-conflict-free accumulation order
   const int LP = static_cast<int>(p.L * p.P);
-  const int64_t HC = p.H * C;
   const int64_t NB = p.B * p.H * bp.ntl;
   const TS* loc = static_cast<const TS*>(p.loc);
   const TS* attn = static_cast<const TS*>(p.attn);
+  const int nunits = V * NU;
+  const int upt = (nunits + kTileThreads - 1) / kTileThreads;
+
+  for (int i = threadIdx.x; i < V; i += kTileThreads) s_cnt[i] = 0;
 
   for (;;) {
     if (threadIdx.x == 0) {
@@ -364,7 +386,6 @@ __global__ void __launch_bounds__(kBinThreads, 2)
     __syncthreads();
     const int32_t item = s_item[0];
     const int32_t bucket = s_item[1];
-    __syncthreads();
     if (bucket < 0) break;
 
     const int64_t bh = bucket / bp.ntl;
@@ -374,45 +395,47 @@ __global__ void __launch_bounds__(kBinThreads, 2)
     while (l + 1 < p.L && lb >= bp.tile_base[l + 1]) ++l;
     const int32_t t = lb - bp.tile_base[l];
     const int32_t nx = bp.ntile[l][0], ny = bp.ntile[l][1];
-    const int32_t tx = t % nx, ty = (t / nx) % ny, tz = t / (nx * ny);
-    const int32_t ox = tx * TX, oy = ty * TY, oz = tz * TZ;
+    const int32_t ox = (t % nx) * TX, oy = ((t / nx) % ny) * TY, oz = (t / (nx * ny)) * TZ;
     const int32_t sz[3] = {lv.size[l][0], lv.size[l][1], lv.size[l][2]};
     const int32_t start = lv.start[l];
     const bool atomic_level = (bp.atomic_mask >> l) & 1;
-    const int32_t k_item = item - bb.item_start[bucket];
     int32_t r0 = bb.starts[bucket];
     int32_t r1 = bb.starts[bucket + 1];
     if (atomic_level) {
-      r0 += k_item * bp.s_max;
+      r0 += (item - bb.item_start[bucket]) * bp.s_max;
       r1 = min(r1, r0 + bp.s_max);
     }
 
-    // Stage the value tile + halo (zero outside the level) and clear grads.
-    const int chunks_per_row = static_cast<int>(row_bytes / 16);
+    // Stage the value tile + halo (zero outside the level).
+    const int cpr = static_cast<int>(row_bytes / 16);
     const char* vsrc = static_cast<const char*>(p.value) + (b * p.K * p.H + h) * row_bytes;
-    for (int i = threadIdx.x; i < nhalo * chunks_per_row; i += kBinThreads) {
-      const int r = i / chunks_per_row, c = i - r * chunks_per_row;
+    for (int i = threadIdx.x; i < nhalo * cpr; i += kTileThreads) {
+      const int r = i / cpr, c = i - r * cpr;
       const int hx = r % HX, hy = (r / HX) % HY, hz = r / (HX * HY);
       const int32_t x = ox + hx, y = oy + hy, z = oz + hz;
       const bool in = x < sz[0] && y < sz[1] && z < sz[2];
       const int64_t key = in ? start + (static_cast<int64_t>(z) * sz[1] + y) * sz[0] + x : start;
       cp_async16(s_val + r * row_bytes + c * 16, vsrc + key * p.H * row_bytes + c * 16, in);
     }
-    for (int i = threadIdx.x; i < ntile_vox * C; i += kBinThreads) s_grad[i] = 0.0f;
+    float acc[kMaxUnitsPerThread][8];
+#pragma unroll
+    for (int k = 0; k < kMaxUnitsPerThread; ++k)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[k][e] = 0.0f;
     cp_async_wait_all();
     __syncthreads();
 
-    for (int32_t base = r0 + warp * slots_per_warp; base < r1; base += groups) {
-      const int32_t ri = base + slot;
+    for (int32_t c0 = r0; c0 < r1; c0 += R) {
+      // ---- A: records -> dots, staged a*grad_out, owned-corner pairs
+      const int32_t ri = c0 + slot;
       const bool active = ri < r1;
       const int32_t rec = active ? bb.records[ri] : 0;
       const bool secondary = rec & 1;
       const int32_t qp = rec >> 1;
-      const int64_t q = qp / p.P;
-      const int pp = qp - static_cast<int>(q * p.P);
+      const int32_t q = qp / static_cast<int32_t>(p.P);
+      const int pp = qp - q * static_cast<int32_t>(p.P);
       const int64_t row = (b * p.Q + q) * p.H + h;
       const int64_t s = row * LP + l * static_cast<int>(p.P) + pp;
-
       Point<NDIM> pt;
       float a = 0.0f;
       if (active) {
@@ -429,54 +452,69 @@ __global__ void __launch_bounds__(kBinThreads, 2)
             : raw_zero<16>();
         CK::unpack(rg, go);
       }
-      // Rotated copy for the shared-memory accumulation: at step e, the lanes
-      // of different record slots hit different banks.
-      float go_rot[EPV];
+      if (has) {
+        float4* dst = reinterpret_cast<float4*>(s_go + slot * C + j * EPV);
 #pragma unroll
-      for (int e = 0; e < EPV; ++e) go_rot[e] = go[e];
-      rotate_left<EPV>(go_rot, rot);
-
+        for (int e = 0; e < EPV; e += 4)
+          dst[e / 4] = make_float4(a * go[e], a * go[e + 1], a * go[e + 2], a * go[e + 3]);
+      }
+      // Per-axis corner data.
+      int32_t lo[3];
+      bool v0[3], v1[3];
+#pragma unroll
+      for (int ax = 0; ax < 3; ++ax) {
+        const int32_t o = ax == 0 ? ox : (ax == 1 ? oy : oz);
+        lo[ax] = pt.i0[ax] - o;
+        v0[ax] = pt.i0[ax] >= 0 && pt.i0[ax] < sz[ax];
+        v1[ax] = pt.i0[ax] + 1 >= 0 && pt.i0[ax] + 1 < sz[ax];
+      }
+      if (NDIM == 2) { lo[2] = 0; v0[2] = true; v1[2] = false; }
       float g_attn = 0.0f;
       float g_ix[3] = {0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
-        bool valid;
-        int32_t key;
-        float w;
-        corner_coords<NDIM>(pt, c, sz, start, valid, key, w);
-        (void)key;
-        const int32_t lx = pt.i0[0] + (c & 1) - ox;
-        const int32_t ly = pt.i0[1] + ((c >> 1) & 1) - oy;
-        const int32_t lz = (NDIM == 3) ? pt.i0[2] + ((c >> 2) & 1) - oz : 0;
+        const int bx = c & 1, by = (c >> 1) & 1, bz = (c >> 2) & 1;
+        const bool valid = (bx ? v1[0] : v0[0]) && (by ? v1[1] : v0[1]) && (bz ? v1[2] : v0[2]);
+        const int32_t lx = lo[0] + bx, ly = lo[1] + by, lz = lo[2] + bz;
+        const float wx = bx ? pt.f[0] : 1.0f - pt.f[0];
+        const float wy = by ? pt.f[1] : 1.0f - pt.f[1];
+        const float wz = (NDIM == 3) ? (bz ? pt.f[2] : 1.0f - pt.f[2]) : 1.0f;
+        const float w = wx * wy * wz;
         if (!secondary) {
-          // Dot product with the staged value row (all valid corners of a
-          // primary record lie in the tile + halo).
           float dot = 0.0f;
-          if (valid && has && lx >= 0 && lx <= TX && ly >= 0 && ly <= TY && lz >= 0 &&
-              lz < HZ) {
-            const int hr = (lz * HY + ly) * HX + lx;
+          if (valid && has && lx >= 0 && lx <= TX && ly >= 0 && ly <= TY && lz >= 0 && lz < HZ) {
             Raw<16> rv;
-            const uint4 u = *reinterpret_cast<const uint4*>(s_val + hr * row_bytes + j * 16);
+            const uint4 u = *reinterpret_cast<const uint4*>(
+                s_val + ((lz * HY + ly) * HX + lx) * row_bytes + j * 16);
             rv.w[0] = u.x; rv.w[1] = u.y; rv.w[2] = u.z; rv.w[3] = u.w;
             float x[EPV];
             CK::unpack(rv, x);
 #pragma unroll
             for (int e = 0; e < EPV; ++e) dot = fmaf(go[e], x[e], dot);
           }
-          float dw[3];
-          corner_dweights<NDIM>(pt, c, dw);
           g_attn = fmaf(w, dot, g_attn);
-#pragma unroll
-          for (int ax = 0; ax < NDIM; ++ax) g_ix[ax] = fmaf(dw[ax], dot, g_ix[ax]);
+          const float sx = bx ? 1.0f : -1.0f, sy = by ? 1.0f : -1.0f, sz_ = bz ? 1.0f : -1.0f;
+          g_ix[0] = fmaf(sx * wy * wz, dot, g_ix[0]);
+          g_ix[1] = fmaf(sy * wx * wz, dot, g_ix[1]);
+          if (NDIM == 3) g_ix[2] = fmaf(sz_ * wx * wy, dot, g_ix[2]);
         }
-        const bool owned = valid && has && lx >= 0 && lx < TX && ly >= 0 && ly < TY &&
-                           lz >= 0 && lz < TZ;
-        if (owned) {
-          const float aw = a * w;
-          float* gr = s_grad + ((lz * TY + ly) * TX + lx) * C + j * EPV;
-#pragma unroll
-          for (int e = 0; e < EPV; ++e) atomicAdd(gr + ((e + rot) & (EPV - 1)), aw * go_rot[e]);
+        // Corner c's pair is emitted by lane (c mod G) of the record.
+        if ((c & (G - 1)) == j) {
+          const bool owned = active && valid && lx >= 0 && lx < TX && ly >= 0 && ly < TY &&
+                             lz >= 0 && lz < TZ;
+          int32_t pv = -1;
+          if (owned) {
+            const int vox = (lz * TY + ly) * TX + lx;
+            const int rank = atomicAdd(&s_cnt[vox], 1);
+            pv = vox | (rank << 10);
+          }
+          s_pvr[slot * 8 + c] = pv;
+          s_pw[slot * 8 + c] = w;
         }
+      }
+      if (NC == 4 && j == 0) {  // 2D: the unused pair slots
+#pragma unroll
+        for (int c = 4; c < 8; ++c) s_pvr[slot * 8 + c] = -1;
       }
       for (int o = G >> 1; o > 0; o >>= 1) {
         g_attn += __shfl_xor_sync(0xffffffffu, g_attn, o);
@@ -492,29 +530,83 @@ __global__ void __launch_bounds__(kBinThreads, 2)
           gl[ax] = Elem<TS>::from_f(pt.pass[ax] ? gval : 0.0f);
         }
       }
-    }
-    __syncthreads();
-
-    // Flush the tile's value gradient.
-    for (int i = threadIdx.x; i < ntile_vox * (C / EPV); i += kBinThreads) {
-      const int v = i / static_cast<int>(C / EPV);
-      const int ck = i - v * static_cast<int>(C / EPV);
-      const int lx = v % TX, ly = (v / TX) % TY, lz = v / (TX * TY);
-      const int32_t x = ox + lx, y = oy + ly, z = oz + lz;
-      if (x >= sz[0] || y >= sz[1] || z >= sz[2]) continue;
-      const float* src = s_grad + v * C + ck * EPV;
-      float f[EPV];
+      __syncthreads();
+      // ---- B: exclusive scan of the per-voxel pair counts
+      for (int base = 0; base < V; base += kTileThreads) {
+        const int i = base + threadIdx.x;
+        const int32_t cnt = i < V ? s_cnt[i] : 0;
+        int32_t total;
+        const int32_t ex = block_exclusive_scan(cnt, s_warp, total);
+        const int32_t carry = base ? s_off[base] : 0;
+        if (i < V) {
+          s_off[i] = carry + ex;
+          s_cnt[i] = 0;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) s_off[min(base + kTileThreads, V)] = carry + total;
+        __syncthreads();
+      }
+      // ---- C: pairs into voxel order
+      for (int i = threadIdx.x; i < R * 8; i += kTileThreads) {
+        const int32_t pv = s_pvr[i];
+        if (pv >= 0) s_sorted[s_off[pv & 1023] + (pv >> 10)] = make_int2(i >> 3, __float_as_int(s_pw[i]));
+      }
+      __syncthreads();
+      // ---- D: owners accumulate in registers
 #pragma unroll
-      for (int e = 0; e < EPV; ++e) f[e] = src[e];
-      const int64_t key_in_level = (static_cast<int64_t>(z) * sz[1] + y) * sz[0] + x;
-      if (atomic_level) {
-        float* dst = bb.acc + ((b * bp.acc_keys + bp.acc_start[l] + key_in_level) * p.H + h) * C +
-                     ck * EPV;
-        red_add_f32<EPV>(dst, f);
-      } else {
-        char* dst = reinterpret_cast<char*>(grad_value) +
-                    ((b * p.K + start + key_in_level) * p.H + h) * row_bytes + ck * 16;
-        st_chunk<16>(dst, CK::pack(f));
+      for (int k = 0; k < kMaxUnitsPerThread; ++k) {
+        if (k < upt) {
+          const int u = threadIdx.x + k * kTileThreads;
+          if (u < nunits) {
+            const int vox = u / NU, g8 = u - vox * NU;
+            const int32_t e0 = s_off[vox], e1 = s_off[vox + 1];
+            for (int32_t e = e0; e < e1; ++e) {
+              const int2 sp = s_sorted[e];
+              const float w = __int_as_float(sp.y);
+              const float4* src = reinterpret_cast<const float4*>(s_go + sp.x * C + g8 * 8);
+              const float4 lo4 = src[0], hi4 = src[1];
+              acc[k][0] = fmaf(w, lo4.x, acc[k][0]);
+              acc[k][1] = fmaf(w, lo4.y, acc[k][1]);
+              acc[k][2] = fmaf(w, lo4.z, acc[k][2]);
+              acc[k][3] = fmaf(w, lo4.w, acc[k][3]);
+              acc[k][4] = fmaf(w, hi4.x, acc[k][4]);
+              acc[k][5] = fmaf(w, hi4.y, acc[k][5]);
+              acc[k][6] = fmaf(w, hi4.z, acc[k][6]);
+              acc[k][7] = fmaf(w, hi4.w, acc[k][7]);
+            }
+          }
+        }
+      }
+      __syncthreads();
+    }
+
+    // Flush the owned units: one write per gradient element (direct levels)
+    // or one vector reduction into the fp32 accumulator (atomic levels).
+#pragma unroll
+    for (int k = 0; k < kMaxUnitsPerThread; ++k) {
+      if (k < upt) {
+        const int u = threadIdx.x + k * kTileThreads;
+        if (u < nunits) {
+          const int vox = u / NU, g8 = u - vox * NU;
+          const int lx = vox % TX, ly = (vox / TX) % TY, lz = vox / (TX * TY);
+          const int32_t x = ox + lx, y = oy + ly, z = oz + lz;
+          if (x < sz[0] && y < sz[1] && z < sz[2]) {
+            const int64_t kil = (static_cast<int64_t>(z) * sz[1] + y) * sz[0] + x;
+            if (atomic_level) {
+              float* dst = bb.acc + ((b * bp.acc_keys + bp.acc_start[l] + kil) * p.H + h) * C + g8 * 8;
+              red_add_f32<8>(dst, acc[k]);
+            } else {
+              char* dst = reinterpret_cast<char*>(grad_value) +
+                          ((b * p.K + start + kil) * p.H + h) * row_bytes + g8 * 8 * sizeof(T);
+              if constexpr (sizeof(T) == 2) {
+                st_chunk<16>(dst, Chunk<T, 16>::pack(acc[k]));
+              } else {
+                st_chunk<16>(dst, Chunk<T, 16>::pack(acc[k]));
+                st_chunk<16>(dst + 16, Chunk<T, 16>::pack(acc[k] + 4));
+              }
+            }
+          }
+        }
       }
     }
     __syncthreads();

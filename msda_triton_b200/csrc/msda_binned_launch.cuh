@@ -86,11 +86,11 @@ cudaError_t launch_bwd_binned(const BinLaunch& bl, const Problem& p, const BinPl
   int dev = 0, nsm = 0, occ = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, main_k, kBinThreads,
+  if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, main_k, kTileThreads,
                                                            bl.smem_main)) != cudaSuccess)
     return err;
   if (occ < 1) occ = 1;
-  main_k<<<static_cast<unsigned>(nsm * occ), kBinThreads, bl.smem_main, st>>>(
+  main_k<<<static_cast<unsigned>(nsm * occ), kTileThreads, bl.smem_main, st>>>(
       p, bp, bb, static_cast<const T*>(grad_out), static_cast<T*>(grad_value),
       static_cast<TS*>(grad_loc), static_cast<TS*>(grad_attn));
   if ((err = cudaGetLastError()) != cudaSuccess) return err;

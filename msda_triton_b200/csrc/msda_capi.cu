@@ -277,6 +277,17 @@ int prepare_bwd(const Args& a, const void* go, const void* gv_like, void* gl, vo
   return MSDA_SUCCESS;
 }
 
+// The gather/scatter backward of 16-bit values reads 8-byte chunks (4
+// channels, one 16-byte fp32 vector reduction each): same lanes per row,
+// twice the chunks per lane.
+void bwd_gather_shape(const Args& a, const Problem& p, LaunchShape& ls) {
+  if (dtype_bytes(a.vdt) == 2 && ls.vb == 16) {
+    ls.vb = 8;
+    ls.vpl *= 2;
+  }
+  (void)p;
+}
+
 // Launch the scatter kernel (or zero-fill the per-sample gradients when
 // C == 0).  `gacc` receives += contributions; it is not cleared here.
 int launch_accumulate(const Args& a, const Problem& p, const LaunchShape& ls, const void* go,
@@ -322,7 +333,17 @@ struct BwdPlan {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
 
-bool choose_tile(int ndim, int64_t row_bytes, int64_t C, int budget, int32_t* tile, int* smem) {
+// Shared memory of the tile kernel for a tile shape: value tile + halo,
+// staged a*grad_out rows, pair lists and per-voxel counters of one chunk.
+int64_t tile_smem_bytes(int ndim, const int32_t* t, int64_t row_bytes, int64_t C, int G) {
+  const int64_t halo = int64_t{t[0] + 1} * (t[1] + 1) * (ndim == 3 ? t[2] + 1 : 1);
+  const int64_t vox = int64_t{t[0]} * t[1] * t[2];
+  const int64_t R = kTileThreads / G;
+  return halo * row_bytes + R * C * 4 + R * 8 * 4 * 2 + R * 8 * 8 + (2 * vox + 1) * 4;
+}
+
+bool choose_tile(int ndim, int64_t row_bytes, int64_t C, int G, int budget, int32_t* tile,
+                 int* smem) {
   static const int32_t c3[][3] = {{8, 8, 8}, {8, 8, 4}, {8, 4, 4}, {4, 4, 4}, {4, 4, 2}, {4, 2, 2}, {2, 2, 2}};
   static const int32_t c2[][3] = {{32, 16, 1}, {16, 16, 1}, {16, 8, 1}, {8, 8, 1}, {8, 4, 1}, {4, 4, 1}, {2, 2, 1}};
   const char* env = std::getenv("MSDA_BIN_TILE");
@@ -335,10 +356,10 @@ bool choose_tile(int ndim, int64_t row_bytes, int64_t C, int budget, int32_t* ti
   for (int i = -1; i < 7; ++i) {
     const int32_t* t = i < 0 ? forced : (ndim == 3 ? c3[i] : c2[i]);
     if (t[0] <= 0 || t[1] <= 0 || t[2] <= 0) continue;
-    const int64_t halo = int64_t{t[0] + 1} * (t[1] + 1) * (ndim == 3 ? t[2] + 1 : 1);
     const int64_t vox = int64_t{t[0]} * t[1] * t[2];
-    const int64_t bytes = halo * row_bytes + vox * C * 4;
-    if (bytes <= budget || (i < 0 && bytes <= 220 * 1024)) {
+    if (vox * C > int64_t{8} * 8 * kTileThreads || vox > 1024) continue;  // owner registers
+    const int64_t bytes = tile_smem_bytes(ndim, t, row_bytes, C, G);
+    if (bytes <= budget || (i < 0 && bytes <= 200 * 1024)) {
       tile[0] = t[0]; tile[1] = t[1]; tile[2] = t[2];
       *smem = static_cast<int>(bytes);
       return true;
@@ -358,7 +379,8 @@ void plan_bwd(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan& p
   const bool force_binned = env && std::strcmp(env, "binned") == 0;
   const bool force_gather = !force_binned;
   bool ok_binned = !force_gather && p.shapes_dev == nullptr && ls.vb == 16 && ls.vpl == 1 &&
-                   samples > 0 && a.C > 0 && (force_binned || samples >= kBinnedMinSamples) &&
+                   a.C % 8 == 0 && samples > 0 && a.C > 0 &&
+                   (force_binned || samples >= kBinnedMinSamples) &&
                    a.Q * a.P < (int64_t{1} << 30) && samples * (int64_t{1} << a.ndim) < INT32_MAX;
   for (int64_t l = 0; ok_binned && l < a.L; ++l)
     for (int ax = 0; ax < 3; ++ax) ok_binned = ok_binned && p.lv.size[l][ax] > 0;
@@ -367,7 +389,7 @@ void plan_bwd(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan& p
   if (ok_binned) {
     const char* sb = std::getenv("MSDA_BIN_SMEM_KB");
     const int budget = sb ? std::atoi(sb) * 1024 : kBinSmemBudget;
-    ok_binned = choose_tile(a.ndim, a.C * e, a.C, budget, bp.tile, &smem);
+    ok_binned = choose_tile(a.ndim, a.C * e, a.C, 1 << p.log2g, budget, bp.tile, &smem);
   }
   if (ok_binned) {
     int64_t ntl = 0;
@@ -491,6 +513,8 @@ int run_bwd(const Args& a, const void* go, void* gv, void* gl, void* ga, void* w
     err = cudaMemsetAsync(gacc, 0, static_cast<size_t>(nval) * sizeof(float), st);
     if (err != cudaSuccess) return cuda_fail(err, "zeroing the grad_value accumulator");
   }
+  bwd_gather_shape(a, p, ls);
+  p.nv = static_cast<int32_t>(a.C * dtype_bytes(a.vdt) / ls.vb);
   rc = launch_accumulate(a, p, ls, go, gacc, gl, ga, st);
   if (rc != MSDA_SUCCESS) return rc;
   if (a.vdt != MSDA_FLOAT32 && nval > 0) {
@@ -508,6 +532,8 @@ int run_bwd_accumulate(const Args& a, const void* go, float* gacc, void* gl, voi
   if (rc != MSDA_SUCCESS) return rc;
   if (a.B * a.K * a.H * a.C > 0 && !aligned(gacc, 16))
     return fail(MSDA_ERROR_MISALIGNED, "grad_value_accum must be 16-byte aligned");
+  bwd_gather_shape(a, p, ls);
+  p.nv = static_cast<int32_t>(a.C * dtype_bytes(a.vdt) / ls.vb);
   rc = launch_accumulate(a, p, ls, go, gacc, gl, ga, static_cast<cudaStream_t>(stream));
   return rc == MSDA_SUCCESS ? ok() : rc;
 }

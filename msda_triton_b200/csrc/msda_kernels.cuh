@@ -82,6 +82,75 @@ __device__ __forceinline__ Point<NDIM> load_point(const TS* lp, const int32_t* s
   return pt;
 }
 
+// A zero value row: invalid corners point here, so every lane loads finite
+// zeros instead of selecting per register (the widest row is 2048 bytes).
+static __device__ __align__(16) unsigned char g_zero_row[2048];
+
+// Per-level constants of the gather kernels.
+struct LevelGeom {
+  int32_t sz[3];
+  int32_t start;
+  int64_t dx, dy, dz;   // byte offsets of the +1 neighbour along x, y, z
+};
+
+__device__ __forceinline__ LevelGeom level_geom(const LevelSmem& lv, int l, int64_t key_bytes) {
+  LevelGeom g;
+  g.sz[0] = lv.size[l][0];
+  g.sz[1] = lv.size[l][1];
+  g.sz[2] = lv.size[l][2];
+  g.start = lv.start[l];
+  g.dx = key_bytes;
+  g.dy = key_bytes * g.sz[0];
+  g.dz = g.dy * g.sz[1];
+  return g;
+}
+
+// The 2^NDIM corners of one sample: row pointers (already offset to the lane's
+// channels; the zero row for corners outside the level), interpolation weights
+// (zero outside) and validity.
+template <int NDIM>
+struct Corners {
+  const char* ptr[1 << NDIM];
+  float w[1 << NDIM];
+  bool valid[1 << NDIM];
+};
+
+template <int NDIM>
+__device__ __forceinline__ Corners<NDIM> make_corners(const Point<NDIM>& pt, const LevelGeom& g,
+                                                      const char* vbase, int64_t key_bytes,
+                                                      int lane_off) {
+  Corners<NDIM> cs;
+  bool v[3][2];
+  float wt[3][2];
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+    if (a < NDIM) {
+      v[a][0] = static_cast<uint32_t>(pt.i0[a]) < static_cast<uint32_t>(g.sz[a]);
+      v[a][1] = static_cast<uint32_t>(pt.i0[a] + 1) < static_cast<uint32_t>(g.sz[a]);
+      wt[a][0] = __fsub_rn(1.0f, pt.f[a]);
+      wt[a][1] = pt.f[a];
+    } else {
+      v[a][0] = true; v[a][1] = false; wt[a][0] = 1.0f; wt[a][1] = 0.0f;
+    }
+  }
+  const int32_t zi = (NDIM == 3) ? pt.i0[2] : 0;
+  const int32_t key0 = g.start + (zi * g.sz[1] + pt.i0[1]) * g.sz[0] + pt.i0[0];
+  const char* p0 = vbase + static_cast<int64_t>(key0) * key_bytes + lane_off;
+  const char* zero = reinterpret_cast<const char*>(g_zero_row);
+#pragma unroll
+  for (int c = 0; c < (1 << NDIM); ++c) {
+    const int bx = c & 1, by = (c >> 1) & 1, bz = (c >> 2) & 1;
+    const bool ok = v[0][bx] && v[1][by] && v[2][bz];
+    const char* pc = p0 + (bx ? g.dx : 0) + (by ? g.dy : 0) + (bz ? g.dz : 0);
+    cs.ptr[c] = ok ? pc : zero;
+    float w = __fmul_rn(wt[0][bx], wt[1][by]);
+    if (NDIM == 3) w = __fmul_rn(w, wt[2][bz]);
+    cs.w[c] = ok ? w : 0.0f;
+    cs.valid[c] = ok;
+  }
+  return cs;
+}
+
 // ------------------------------------------------------------------ forward
 template <typename T, typename TS, int NDIM, int VB, int VPL>
 __global__ void __launch_bounds__(kThreads)
@@ -108,14 +177,9 @@ __global__ void __launch_bounds__(kThreads)
   const TS* lrow = static_cast<const TS*>(p.loc) + row * LP * NDIM;
   const TS* arow = static_cast<const TS*>(p.attn) + row * LP;
 
-  int off[VPL];
   bool has[VPL];
 #pragma unroll
-  for (int v = 0; v < VPL; ++v) {
-    const int chunk = j + v * G;
-    has[v] = chunk < p.nv;
-    off[v] = chunk * VB;
-  }
+  for (int v = 0; v < VPL; ++v) has[v] = j + v * G < p.nv;
 
   float acc[VPL][EPV];
 #pragma unroll
@@ -123,36 +187,30 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int e = 0; e < EPV; ++e) acc[v][e] = 0.0f;
 
+  const int P = static_cast<int>(p.P);
   for (int l = 0; l < p.L; ++l) {
-    const int32_t sz[3] = {lv.size[l][0], lv.size[l][1], lv.size[l][2]};
-    const int32_t start = lv.start[l];
-    for (int pp = 0; pp < p.P; ++pp) {
-      const int s = l * static_cast<int>(p.P) + pp;
-      const Point<NDIM> pt = load_point<TS, NDIM>(lrow + s * NDIM, sz, p);
+    const LevelGeom g = level_geom(lv, l, key_bytes);
+    for (int pp = 0; pp < P; ++pp) {
+      const int s = l * P + pp;
+      const Point<NDIM> pt = load_point<TS, NDIM>(lrow + s * NDIM, g.sz, p);
       const float a = Elem<TS>::to_f(arow[s]);
-
+      const Corners<NDIM> cs = make_corners<NDIM>(pt, g, vbase, key_bytes, j * VB);
       Raw<VB> raw[NC][VPL];
-      float cw[NC];
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        bool valid;
-        int32_t key;
-        float w;
-        corner_coords<NDIM>(pt, c, sz, start, valid, key, w);
-        cw[c] = valid ? a * w : 0.0f;
-        const char* kp = vbase + static_cast<int64_t>(key) * key_bytes;
+      for (int c = 0; c < NC; ++c)
 #pragma unroll
         for (int v = 0; v < VPL; ++v)
-          raw[c][v] = (valid && has[v]) ? ld_chunk<VB>(kp + off[v]) : raw_zero<VB>();
-      }
+          raw[c][v] = has[v] ? ld_chunk<VB>(cs.valid[c] ? cs.ptr[c] + v * G * VB : cs.ptr[c])
+                             : raw_zero<VB>();
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
+        const float cw = a * cs.w[c];
 #pragma unroll
         for (int v = 0; v < VPL; ++v) {
           float x[EPV];
           CK::unpack(raw[c][v], x);
 #pragma unroll
-          for (int e = 0; e < EPV; ++e) acc[v][e] = fmaf(cw[c], x[e], acc[v][e]);
+          for (int e = 0; e < EPV; ++e) acc[v][e] = fmaf(cw, x[e], acc[v][e]);
         }
       }
     }
@@ -161,7 +219,7 @@ __global__ void __launch_bounds__(kThreads)
   char* orow = reinterpret_cast<char*>(out) + row * p.C * static_cast<int64_t>(sizeof(T));
 #pragma unroll
   for (int v = 0; v < VPL; ++v)
-    if (has[v]) st_chunk<VB>(orow + off[v], CK::pack(acc[v]));
+    if (has[v]) st_chunk<VB>(orow + (j + v * G) * VB, CK::pack(acc[v]));
 }
 
 // ------------------------------------------------------------------ backward
@@ -190,7 +248,10 @@ __device__ __forceinline__ void red_add_f32(float* dst, const float* v) {
 // written with plain stores by the group's first lane (one owner per sample:
 // no atomics and no zero-fill).  grad_value is scattered with vector fp32
 // reductions into `gacc` (grad_value itself for fp32, else an fp32 workspace
-// that msda_cast_kernel rounds to the input dtype).
+// that msda_cast_kernel rounds to the input dtype).  For 16-bit inputs the
+// host picks 8-byte chunks (VB = 8): lane j then owns channel groups j, j+G,
+// ... of 4 channels, so one red.v4.f32 per group and the G lanes of a row
+// cover whole 32-byte sectors of the accumulator.
 template <typename T, typename TS, int NDIM, int VB, int VPL>
 __global__ void __launch_bounds__(kThreads)
     msda_bwd_kernel(const Problem p, const T* __restrict__ grad_out, float* __restrict__ gacc,
@@ -217,37 +278,35 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t key_bytes = HC * static_cast<int64_t>(sizeof(T));
   const char* vbase = static_cast<const char*>(p.value) +
                       (rc.b * p.K * p.H + rc.h) * p.C * static_cast<int64_t>(sizeof(T));
+  // fp32 accumulator row base, addressed with the same key offsets scaled.
   float* gbase = gacc + (rc.b * p.K * p.H + rc.h) * p.C;
   const int LP = static_cast<int>(p.L * p.P);
   const TS* lrow = static_cast<const TS*>(p.loc) + row * LP * NDIM;
   const TS* arow = static_cast<const TS*>(p.attn) + row * LP;
 
-  int chunk[VPL];
   bool has[VPL];
 #pragma unroll
-  for (int v = 0; v < VPL; ++v) {
-    chunk[v] = j + v * G;
-    has[v] = active && chunk[v] < p.nv;
-  }
+  for (int v = 0; v < VPL; ++v) has[v] = active && (j + v * G < p.nv);
 
   float go[VPL][EPV];
   const char* gorow = reinterpret_cast<const char*>(grad_out) +
                       row * p.C * static_cast<int64_t>(sizeof(T));
 #pragma unroll
   for (int v = 0; v < VPL; ++v) {
-    const Raw<VB> rg = has[v] ? ld_chunk<VB>(gorow + chunk[v] * VB) : raw_zero<VB>();
+    const Raw<VB> rg = has[v] ? ld_chunk<VB>(gorow + (j + v * G) * VB) : raw_zero<VB>();
     CK::unpack(rg, go[v]);
   }
 
+  const int P = static_cast<int>(p.P);
+  const char* vlane = vbase + j * VB;
   for (int l = 0; l < p.L; ++l) {
-    const int32_t sz[3] = {lv.size[l][0], lv.size[l][1], lv.size[l][2]};
-    const int32_t start = lv.start[l];
-    for (int pp = 0; pp < p.P; ++pp) {
-      const int s = l * static_cast<int>(p.P) + pp;
+    const LevelGeom g = level_geom(lv, l, key_bytes);
+    for (int pp = 0; pp < P; ++pp) {
+      const int s = l * P + pp;
       Point<NDIM> pt;
       float a = 0.0f;
       if (active) {
-        pt = load_point<TS, NDIM>(lrow + s * NDIM, sz, p);
+        pt = load_point<TS, NDIM>(lrow + s * NDIM, g.sz, p);
         a = Elem<TS>::to_f(arow[s]);
       } else {
 #pragma unroll
@@ -257,23 +316,16 @@ __global__ void __launch_bounds__(kThreads)
           pt.pass[ax] = false;
         }
       }
-
+      const Corners<NDIM> cs = make_corners<NDIM>(pt, g, vbase, key_bytes, j * VB);
       Raw<VB> raw[NC][VPL];
-      bool cvalid[NC];
-      int32_t ckey[NC];
-      float cw[NC];
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        corner_coords<NDIM>(pt, c, sz, start, cvalid[c], ckey[c], cw[c]);
-        const char* kp = vbase + static_cast<int64_t>(ckey[c]) * key_bytes;
+      for (int c = 0; c < NC; ++c)
 #pragma unroll
         for (int v = 0; v < VPL; ++v)
-          raw[c][v] = (cvalid[c] && has[v]) ? ld_chunk<VB>(kp + chunk[v] * VB)
-                                            : raw_zero<VB>();
-      }
+          raw[c][v] = has[v] ? ld_chunk<VB>(cs.valid[c] ? cs.ptr[c] + v * G * VB : cs.ptr[c])
+                             : raw_zero<VB>();
 
-      float g_attn = 0.0f;
-      float g_ix[3] = {0.0f, 0.0f, 0.0f};
+      float dots[NC];
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
         float dot = 0.0f;
@@ -284,28 +336,37 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
           for (int e = 0; e < EPV; ++e) dot = fmaf(go[v][e], x[e], dot);
         }
-        float dw[3];
-        corner_dweights<NDIM>(pt, c, dw);
-        g_attn = fmaf(cw[c], dot, g_attn);
-#pragma unroll
-        for (int ax = 0; ax < NDIM; ++ax) g_ix[ax] = fmaf(dw[ax], dot, g_ix[ax]);
-
-        if (cvalid[c]) {
-          const float aw = a * cw[c];
-          float* gk = gbase + static_cast<int64_t>(ckey[c]) * HC;
+        dots[c] = dot;
+        if (cs.valid[c]) {
+          const float aw = a * cs.w[c];
+          // The accumulator row of a corner sits at the value row's byte
+          // offset scaled by 4 / sizeof(T) (same key, fp32 elements).
+          const int64_t vo = cs.ptr[c] - vlane;
+          float* gk = reinterpret_cast<float*>(reinterpret_cast<char*>(gbase) +
+                                               vo * static_cast<int64_t>(4 / sizeof(T)));
 #pragma unroll
           for (int v = 0; v < VPL; ++v) {
             if (has[v]) {
               float t[EPV];
 #pragma unroll
               for (int e = 0; e < EPV; ++e) t[e] = aw * go[v][e];
-              red_add_f32<EPV>(gk + chunk[v] * EPV, t);
+              red_add_f32<EPV>(gk + (j + v * G) * EPV, t);
             }
           }
         }
       }
-
-      // Reduce the per-sample scalars over the G lanes of the group.
+      // Per-sample scalars: d out / d attn and d out / d (source index).
+      float g_attn = 0.0f;
+#pragma unroll
+      for (int c = 0; c < NC; ++c) g_attn = fmaf(cs.w[c], dots[c], g_attn);
+      float g_ix[3] = {0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {  // invalid corners read the zero row: dots[c] == 0
+        float dw[3];
+        corner_dweights<NDIM>(pt, c, dw);
+#pragma unroll
+        for (int ax = 0; ax < NDIM; ++ax) g_ix[ax] = fmaf(dw[ax], dots[c], g_ix[ax]);
+      }
       for (int o = G >> 1; o > 0; o >>= 1) {
         g_attn += __shfl_xor_sync(0xffffffffu, g_attn, o);
 #pragma unroll
@@ -316,7 +377,7 @@ __global__ void __launch_bounds__(kThreads)
         TS* gl = grad_loc + (row * LP + s) * NDIM;
 #pragma unroll
         for (int ax = 0; ax < NDIM; ++ax) {
-          const float gval = a * g_ix[ax] * static_cast<float>(sz[ax]);
+          const float gval = a * g_ix[ax] * static_cast<float>(g.sz[ax]);
           gl[ax] = Elem<TS>::from_f(pt.pass[ax] ? gval : 0.0f);
         }
       }

@@ -15,48 +15,56 @@ struct LaunchShape {
   int64_t grid;  // number of CTAs
 };
 
+// (chunk bytes, chunks per lane) pairs that are instantiated.  VB = 8 is the
+// backward's layout for 16-bit values (see msda_bwd_kernel).
+template <int VB, int VPL>
+constexpr bool kAllowed = (VB == 16 && (VPL == 1 || VPL == 2 || VPL == 4)) ||
+                          (VB == 8 && (VPL == 2 || VPL == 4 || VPL == 8)) ||
+                          ((VB == 4 || VB == 2) && (VPL == 1 || VPL == 8));
+
+template <typename T, typename TS, int NDIM, int VB, int VPL>
+static cudaError_t fwd_one(const LaunchShape& ls, const Problem& p, void* out, cudaStream_t st) {
+  if constexpr (kAllowed<VB, VPL> && VB != 8) {
+    msda_fwd_kernel<T, TS, NDIM, VB, VPL>
+        <<<dim3(static_cast<unsigned>(ls.grid)), kThreads, 0, st>>>(p, static_cast<T*>(out));
+    return cudaGetLastError();
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <typename T, typename TS, int NDIM, int VB, int VPL>
+static cudaError_t bwd_one(const LaunchShape& ls, const Problem& p, const void* grad_out,
+                           float* gacc, void* grad_loc, void* grad_attn, cudaStream_t st) {
+  if constexpr (kAllowed<VB, VPL> && (VB != 8 || sizeof(T) == 2)) {
+    msda_bwd_kernel<T, TS, NDIM, VB, VPL><<<dim3(static_cast<unsigned>(ls.grid)), kThreads, 0, st>>>(
+        p, static_cast<const T*>(grad_out), gacc, static_cast<TS*>(grad_loc),
+        static_cast<TS*>(grad_attn));
+    return cudaGetLastError();
+  }
+  return cudaErrorInvalidValue;
+}
+
 template <typename T, typename TS, int NDIM, int VB>
-static cudaError_t fwd_vpl(const LaunchShape& ls, const Problem& p, void* out,
-                           cudaStream_t st) {
-  const dim3 grid(static_cast<unsigned>(ls.grid));
-  T* o = static_cast<T*>(out);
+static cudaError_t fwd_vpl(const LaunchShape& ls, const Problem& p, void* out, cudaStream_t st) {
   switch (ls.vpl) {
-    case 1: msda_fwd_kernel<T, TS, NDIM, VB, 1><<<grid, kThreads, 0, st>>>(p, o); break;
-    case 2:
-      if constexpr (VB == 16) { msda_fwd_kernel<T, TS, NDIM, VB, 2><<<grid, kThreads, 0, st>>>(p, o); break; }
-      return cudaErrorInvalidValue;
-    case 4:
-      if constexpr (VB == 16) { msda_fwd_kernel<T, TS, NDIM, VB, 4><<<grid, kThreads, 0, st>>>(p, o); break; }
-      return cudaErrorInvalidValue;
-    case 8:
-      if constexpr (VB != 16) { msda_fwd_kernel<T, TS, NDIM, VB, 8><<<grid, kThreads, 0, st>>>(p, o); break; }
-      return cudaErrorInvalidValue;
+    case 1: return fwd_one<T, TS, NDIM, VB, 1>(ls, p, out, st);
+    case 2: return fwd_one<T, TS, NDIM, VB, 2>(ls, p, out, st);
+    case 4: return fwd_one<T, TS, NDIM, VB, 4>(ls, p, out, st);
+    case 8: return fwd_one<T, TS, NDIM, VB, 8>(ls, p, out, st);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 template <typename T, typename TS, int NDIM, int VB>
 static cudaError_t bwd_vpl(const LaunchShape& ls, const Problem& p, const void* grad_out,
                            float* gacc, void* grad_loc, void* grad_attn, cudaStream_t st) {
-  const dim3 grid(static_cast<unsigned>(ls.grid));
-  const T* go = static_cast<const T*>(grad_out);
-  TS* gl = static_cast<TS*>(grad_loc);
-  TS* ga = static_cast<TS*>(grad_attn);
   switch (ls.vpl) {
-    case 1: msda_bwd_kernel<T, TS, NDIM, VB, 1><<<grid, kThreads, 0, st>>>(p, go, gacc, gl, ga); break;
-    case 2:
-      if constexpr (VB == 16) { msda_bwd_kernel<T, TS, NDIM, VB, 2><<<grid, kThreads, 0, st>>>(p, go, gacc, gl, ga); break; }
-      return cudaErrorInvalidValue;
-    case 4:
-      if constexpr (VB == 16) { msda_bwd_kernel<T, TS, NDIM, VB, 4><<<grid, kThreads, 0, st>>>(p, go, gacc, gl, ga); break; }
-      return cudaErrorInvalidValue;
-    case 8:
-      if constexpr (VB != 16) { msda_bwd_kernel<T, TS, NDIM, VB, 8><<<grid, kThreads, 0, st>>>(p, go, gacc, gl, ga); break; }
-      return cudaErrorInvalidValue;
+    case 1: return bwd_one<T, TS, NDIM, VB, 1>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 2: return bwd_one<T, TS, NDIM, VB, 2>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 4: return bwd_one<T, TS, NDIM, VB, 4>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 8: return bwd_one<T, TS, NDIM, VB, 8>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 template <typename T, typename TS, int NDIM>
@@ -76,6 +84,10 @@ static cudaError_t bwd_vb(const LaunchShape& ls, const Problem& p, const void* g
                           float* gacc, void* grad_loc, void* grad_attn, cudaStream_t st) {
   switch (ls.vb) {
     case 16: return bwd_vpl<T, TS, NDIM, 16>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 8:
+      if constexpr (sizeof(T) == 2)
+        return bwd_vpl<T, TS, NDIM, 8>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+      return cudaErrorInvalidValue;
     case 4: return bwd_vpl<T, TS, NDIM, 4>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
     case 2:
       if constexpr (sizeof(T) == 2)
