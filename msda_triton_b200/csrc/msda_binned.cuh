@@ -107,7 +107,15 @@ __device__ __forceinline__ int sample_buckets(const Point<NDIM>& pt, const int32
 }
 
 // ---------------------------------------------------------------- binning
-// One CTA per (b, h, chunk of queries).  Pass 0 counts, pass 1 fills.
+// Record encoding: (q << 5) | (p << 1) | secondary  (P <= 16, Q < 2^26).
+__device__ __forceinline__ int32_t make_record(int32_t q, int pp, bool secondary) {
+  return (q << 5) | (pp << 1) | (secondary ? 1 : 0);
+}
+
+// One CTA per (b, h, chunk of queries).  Each thread keeps one (level, point)
+// index for the whole chunk and strides over the chunk's queries, so there is
+// no per-sample division.  FILL = false counts records per bucket; FILL = true
+// places them.
 template <typename TS, int NDIM, bool FILL>
 __global__ void __launch_bounds__(512)
     msda_bin_kernel(const Problem p, const BinPlan bp, BinBuffers bb) {
@@ -121,24 +129,27 @@ __global__ void __launch_bounds__(512)
   const int64_t chunk = blockIdx.x % bp.nchunk;
   const int64_t bh = blockIdx.x / bp.nchunk;
   const int64_t b = bh / p.H, h = bh % p.H;
-  const int64_t q0 = chunk * bp.rows_per_chunk;
-  int64_t q1 = q0 + bp.rows_per_chunk;
-  if (q1 > p.Q) q1 = p.Q;
+  const int32_t q0 = static_cast<int32_t>(chunk * bp.rows_per_chunk);
+  const int32_t q1 = min(static_cast<int32_t>(p.Q), q0 + bp.rows_per_chunk);
   const int LP = static_cast<int>(p.L * p.P);
-  const int64_t nsmp = (q1 - q0) * LP;
+  const int per_row = static_cast<int>(blockDim.x) / LP;   // host guarantees >= 1
+  const int lp = static_cast<int>(threadIdx.x) % LP;
+  const int roff = static_cast<int>(threadIdx.x) / LP;
+  const bool worker = roff < per_row;
+  const int l = lp / static_cast<int>(p.P);
+  const int pp = lp - l * static_cast<int>(p.P);
+  const int32_t sz[3] = {lv.size[l][0], lv.size[l][1], lv.size[l][2]};
   const TS* loc = static_cast<const TS*>(p.loc);
+  const int64_t row0 = (b * p.Q) * p.H + h;   // row of query 0 of this (b, h)
 
-  // Pass A: local histogram.
-  for (int64_t i = threadIdx.x; i < nsmp; i += blockDim.x) {
-    const int64_t q = q0 + i / LP;
-    const int lp = static_cast<int>(i % LP);
-    const int l = lp / static_cast<int>(p.P);
-    const int32_t sz[3] = {lv.size[l][0], lv.size[l][1], lv.size[l][2]};
-    const int64_t s = ((b * p.Q + q) * p.H + h) * LP + lp;
-    const Point<NDIM> pt = load_point<TS, NDIM>(loc + s * NDIM, sz, p);
-    int32_t lb[8];
-    const int n = sample_buckets<NDIM>(pt, sz, l, bp, lb);
-    for (int k = 0; k < n; ++k) atomicAdd(&s_hist[lb[k]], 1);
+  if (worker) {
+    for (int32_t q = q0 + roff; q < q1; q += per_row) {
+      const int64_t s = (row0 + static_cast<int64_t>(q) * p.H) * LP + lp;
+      const Point<NDIM> pt = load_point<TS, NDIM>(loc + s * NDIM, sz, p);
+      int32_t lb[8];
+      const int n = sample_buckets<NDIM>(pt, sz, l, bp, lb);
+      for (int k = 0; k < n; ++k) atomicAdd(&s_hist[lb[k]], 1);
+    }
   }
   __syncthreads();
   const int64_t gbase = bh * ntl;
@@ -155,20 +166,16 @@ __global__ void __launch_bounds__(512)
     s_hist[i] = 0;
   }
   __syncthreads();
-  for (int64_t i = threadIdx.x; i < nsmp; i += blockDim.x) {
-    const int64_t q = q0 + i / LP;
-    const int lp = static_cast<int>(i % LP);
-    const int l = lp / static_cast<int>(p.P);
-    const int pp = lp - l * static_cast<int>(p.P);
-    const int32_t sz[3] = {lv.size[l][0], lv.size[l][1], lv.size[l][2]};
-    const int64_t s = ((b * p.Q + q) * p.H + h) * LP + lp;
-    const Point<NDIM> pt = load_point<TS, NDIM>(loc + s * NDIM, sz, p);
-    int32_t lb[8];
-    const int n = sample_buckets<NDIM>(pt, sz, l, bp, lb);
-    const int32_t rec = static_cast<int32_t>((q * p.P + pp) << 1);
-    for (int k = 0; k < n; ++k) {
-      const int32_t pos = s_base[lb[k]] + atomicAdd(&s_hist[lb[k]], 1);
-      bb.records[pos] = rec | (k > 0 ? 1 : 0);
+  if (worker) {
+    for (int32_t q = q0 + roff; q < q1; q += per_row) {
+      const int64_t s = (row0 + static_cast<int64_t>(q) * p.H) * LP + lp;
+      const Point<NDIM> pt = load_point<TS, NDIM>(loc + s * NDIM, sz, p);
+      int32_t lb[8];
+      const int n = sample_buckets<NDIM>(pt, sz, l, bp, lb);
+      for (int k = 0; k < n; ++k) {
+        const int32_t pos = s_base[lb[k]] + atomicAdd(&s_hist[lb[k]], 1);
+        bb.records[pos] = make_record(q, pp, k > 0);
+      }
     }
   }
 }
@@ -306,31 +313,80 @@ __device__ __forceinline__ void rotate_left(float* x, int r) {
   }
 }
 
-// Work item: one tile of one (b, h, level), records [r0, r1).  VB = 16 only
-// (C * sizeof(T) % 16 == 0, C % 8 == 0).
-//
-// Records are processed in chunks of R = kTileThreads / G (G lanes per record,
-// each owning EPV channels):
-//   A. per record: corner weights, dot products against the staged value rows
-//      (primary records: write grad_attn / grad_loc), stage a*grad_out in
-//      shared memory, and emit one (voxel, weight) pair per corner the tile
-//      owns, counting pairs per voxel with an integer shared-memory atomic;
-//   B. exclusive scan of the per-voxel counts;
-//   C. scatter the pairs into voxel order;
-//   D. every thread owns fixed (voxel, 8-channel) units and adds
-//      w * a*grad_out for the voxel's pairs into registers.
-// The value gradient of the tile is never touched by an atomic: it lives in
-// the owners' registers until the item ends and is written once.
-constexpr int kTileThreads = 256;
-constexpr int kMaxUnitsPerThread = 8;
+// Dot product of EPV channels held as raw 16-byte chunks (8 x 16-bit or 4 x
+// fp32), fp32 accumulation.  16-bit inputs use sm_100's mixed-precision FMA
+// (fp16/bf16 multiplicands, fp32 addend) so no conversion is issued.
+template <typename T>
+__device__ __forceinline__ float chunk_dot(const uint4& x, const uint4& y, float acc);
+template <>
+__device__ __forceinline__ float chunk_dot<float>(const uint4& x, const uint4& y, float acc) {
+  acc = fmaf(__uint_as_float(x.x), __uint_as_float(y.x), acc);
+  acc = fmaf(__uint_as_float(x.y), __uint_as_float(y.y), acc);
+  acc = fmaf(__uint_as_float(x.z), __uint_as_float(y.z), acc);
+  acc = fmaf(__uint_as_float(x.w), __uint_as_float(y.w), acc);
+  return acc;
+}
+#define MSDA_MIXED_FMA(TYPE)                                                              \
+  __device__ __forceinline__ float mixed_fma_##TYPE(uint32_t a, uint32_t b, float acc) {  \
+    uint16_t al, ah, bl, bh;                                                              \
+    asm("mov.b32 {%0, %1}, %2;" : "=h"(al), "=h"(ah) : "r"(a));                          \
+    asm("mov.b32 {%0, %1}, %2;" : "=h"(bl), "=h"(bh) : "r"(b));                          \
+    asm("fma.rn.f32." #TYPE " %0, %1, %2, %0;" : "+f"(acc) : "h"(al), "h"(bl));          \
+    asm("fma.rn.f32." #TYPE " %0, %1, %2, %0;" : "+f"(acc) : "h"(ah), "h"(bh));          \
+    return acc;                                                                           \
+  }
+MSDA_MIXED_FMA(bf16)
+MSDA_MIXED_FMA(f16)
+#undef MSDA_MIXED_FMA
+template <>
+__device__ __forceinline__ float chunk_dot<__nv_bfloat16>(const uint4& x, const uint4& y,
+                                                           float acc) {
+  acc = mixed_fma_bf16(x.x, y.x, acc);
+  acc = mixed_fma_bf16(x.y, y.y, acc);
+  acc = mixed_fma_bf16(x.z, y.z, acc);
+  acc = mixed_fma_bf16(x.w, y.w, acc);
+  return acc;
+}
+template <>
+__device__ __forceinline__ float chunk_dot<__half>(const uint4& x, const uint4& y, float acc) {
+  acc = mixed_fma_f16(x.x, y.x, acc);
+  acc = mixed_fma_f16(x.y, y.y, acc);
+  acc = mixed_fma_f16(x.z, y.z, acc);
+  acc = mixed_fma_f16(x.w, y.w, acc);
+  return acc;
+}
 
+constexpr int kTileThreads = 256;
+constexpr int kTileCtasPerSm = 3;
+#ifndef MSDA_MIXED_PRECISION_DOT
+#define MSDA_MIXED_PRECISION_DOT 0
+#endif
+
+// Shared-memory fp32 reduction without a return value.
+__device__ __forceinline__ void red_shared_f32(float* addr, float v) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(addr));
+  asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+
+// Work item: one tile of one (b, h, level), records [r0, r1).  C * sizeof(T)
+// is a multiple of 16 and at most 512 bytes: G lanes per record own one
+// 16-byte chunk (EPV channels) each.
+//
+// Per record: corner weights from the sample's location; for a primary
+// record the dot products of grad_out with the staged corner rows give
+// grad_attn and grad_loc (written directly, one owner per sample); for every
+// corner inside the tile, a*w*grad_out is added to the tile's fp32 gradient
+// with shared-memory atomics.  Lanes of different record slots add their
+// elements in a rotated order so a warp's 32 atomics hit 32 banks.  At the end
+// of the item the tile gradient is written once (direct levels) or reduced
+// into the fp32 accumulator (atomic levels).
 template <typename T, typename TS, int NDIM>
-__global__ void __launch_bounds__(kTileThreads, 2)
+__global__ void __launch_bounds__(kTileThreads, kTileCtasPerSm)
     msda_bwd_binned_kernel(const Problem p, const BinPlan bp, const BinBuffers bb,
                            const T* __restrict__ grad_out, T* __restrict__ grad_value,
                            TS* __restrict__ grad_loc, TS* __restrict__ grad_attn) {
   using CK = Chunk<T, 16>;
-  constexpr int EPV = CK::EPV;      // channels per 16-byte chunk
+  constexpr int EPV = CK::EPV;      // channels per 16-byte chunk (8 or 4)
   constexpr int NC = 1 << NDIM;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ LevelSmem lv;
@@ -342,31 +398,32 @@ __global__ void __launch_bounds__(kTileThreads, 2)
   const int nhalo = HX * HY * HZ;
   const int V = TX * TY * TZ;
   const int C = static_cast<int>(p.C);
-  const int NU = C / 8;                       // 8-channel units per voxel
-  const int64_t row_bytes = static_cast<int64_t>(C) * sizeof(T);
-  const int G = 1 << p.log2g;
-  const int R = kTileThreads / G;             // records per chunk
-  // Shared memory carve-up (byte offsets are multiples of 16).
-  unsigned char* s_val = smem;                                                // nhalo rows
-  float* s_go = reinterpret_cast<float*>(smem + nhalo * row_bytes);           // R x C
-  int32_t* s_pvr = reinterpret_cast<int32_t*>(s_go + R * C);                  // R*8: voxel | rank<<10
-  float* s_pw = reinterpret_cast<float*>(s_pvr + R * 8);                      // R*8: weight
-  int2* s_sorted = reinterpret_cast<int2*>(s_pw + R * 8);                     // R*8: (slot, w)
-  int32_t* s_cnt = reinterpret_cast<int32_t*>(s_sorted + R * 8);              // V
-  int32_t* s_off = s_cnt + V;                                                 // V + 1
-  __shared__ int32_t s_warp[32];
+  const int row_bytes = C * static_cast<int>(sizeof(T));
+  unsigned char* s_val = smem;                                               // nhalo + 1 rows
+  float* s_grad = reinterpret_cast<float*>(smem + (nhalo + 1) * row_bytes);  // V x C
 
-  const int slot = threadIdx.x / G;           // record slot within the chunk
-  const int j = threadIdx.x & (G - 1);        // channel chunk of this lane
+  const int G = 1 << p.log2g;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int slot = lane / G;
+  const int j = lane & (G - 1);
+  const int spw = 32 / G;                              // record slots per warp
+  const int stride = (kTileThreads / 32) * spw;        // records per CTA pass
   const bool has = j < p.nv;
+  const int rot = slot & (EPV - 1);
   const int LP = static_cast<int>(p.L * p.P);
+  const int P = static_cast<int>(p.P);
   const int64_t NB = p.B * p.H * bp.ntl;
   const TS* loc = static_cast<const TS*>(p.loc);
   const TS* attn = static_cast<const TS*>(p.attn);
-  const int nunits = V * NU;
-  const int upt = (nunits + kTileThreads - 1) / kTileThreads;
+  // Element e of this lane's chunk goes to channel j*EPV + ((e + rot) & (EPV-1)).
+  int eoff[EPV];
+#pragma unroll
+  for (int e = 0; e < EPV; ++e) eoff[e] = j * EPV + ((e + rot) & (EPV - 1));
 
-  for (int i = threadIdx.x; i < V; i += kTileThreads) s_cnt[i] = 0;
+  // The zero row after the halo: corners outside the level read it.
+  for (int i = threadIdx.x; i < row_bytes / 16; i += kTileThreads)
+    reinterpret_cast<uint4*>(s_val + nhalo * row_bytes)[i] = make_uint4(0, 0, 0, 0);
 
   for (;;) {
     if (threadIdx.x == 0) {
@@ -395,7 +452,7 @@ __global__ void __launch_bounds__(kTileThreads, 2)
     while (l + 1 < p.L && lb >= bp.tile_base[l + 1]) ++l;
     const int32_t t = lb - bp.tile_base[l];
     const int32_t nx = bp.ntile[l][0], ny = bp.ntile[l][1];
-    const int32_t ox = (t % nx) * TX, oy = ((t / nx) % ny) * TY, oz = (t / (nx * ny)) * TZ;
+    const int32_t org[3] = {(t % nx) * TX, ((t / nx) % ny) * TY, (t / (nx * ny)) * TZ};
     const int32_t sz[3] = {lv.size[l][0], lv.size[l][1], lv.size[l][2]};
     const int32_t start = lv.start[l];
     const bool atomic_level = (bp.atomic_mask >> l) & 1;
@@ -406,115 +463,128 @@ __global__ void __launch_bounds__(kTileThreads, 2)
       r1 = min(r1, r0 + bp.s_max);
     }
 
-    // Stage the value tile + halo (zero outside the level).
-    const int cpr = static_cast<int>(row_bytes / 16);
+    // Stage the value tile + halo (zero outside the level); clear the grads.
+    const int cpr = row_bytes / 16;
     const char* vsrc = static_cast<const char*>(p.value) + (b * p.K * p.H + h) * row_bytes;
     for (int i = threadIdx.x; i < nhalo * cpr; i += kTileThreads) {
       const int r = i / cpr, c = i - r * cpr;
       const int hx = r % HX, hy = (r / HX) % HY, hz = r / (HX * HY);
-      const int32_t x = ox + hx, y = oy + hy, z = oz + hz;
+      const int32_t x = org[0] + hx, y = org[1] + hy, z = org[2] + hz;
       const bool in = x < sz[0] && y < sz[1] && z < sz[2];
       const int64_t key = in ? start + (static_cast<int64_t>(z) * sz[1] + y) * sz[0] + x : start;
       cp_async16(s_val + r * row_bytes + c * 16, vsrc + key * p.H * row_bytes + c * 16, in);
     }
-    float acc[kMaxUnitsPerThread][8];
-#pragma unroll
-    for (int k = 0; k < kMaxUnitsPerThread; ++k)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[k][e] = 0.0f;
+    for (int i = threadIdx.x; i < V * C / 4; i += kTileThreads)
+      reinterpret_cast<float4*>(s_grad)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     cp_async_wait_all();
     __syncthreads();
 
-    for (int32_t c0 = r0; c0 < r1; c0 += R) {
-      // ---- A: records -> dots, staged a*grad_out, owned-corner pairs
-      const int32_t ri = c0 + slot;
+    const int64_t row_b = b * p.Q * p.H + h;   // row of query 0
+    for (int32_t rb = r0 + warp * spw; rb < r1; rb += stride) {
+      const int32_t ri = rb + slot;
       const bool active = ri < r1;
-      const int32_t rec = active ? bb.records[ri] : 0;
+      const int32_t rec = active ? __ldg(bb.records + ri) : 0;
       const bool secondary = rec & 1;
-      const int32_t qp = rec >> 1;
-      const int32_t q = qp / static_cast<int32_t>(p.P);
-      const int pp = qp - q * static_cast<int32_t>(p.P);
-      const int64_t row = (b * p.Q + q) * p.H + h;
-      const int64_t s = row * LP + l * static_cast<int>(p.P) + pp;
+      const int32_t q = rec >> 5;
+      const int pp = (rec >> 1) & 15;
+      const int64_t row = row_b + static_cast<int64_t>(q) * p.H;
+      const int64_t s = row * LP + l * P + pp;
+
       Point<NDIM> pt;
       float a = 0.0f;
+      uint4 gor = make_uint4(0, 0, 0, 0);
       if (active) {
         pt = load_point<TS, NDIM>(loc + s * NDIM, sz, p);
         a = Elem<TS>::to_f(attn[s]);
+        if (has) gor = __ldg(reinterpret_cast<const uint4*>(
+                              reinterpret_cast<const char*>(grad_out) + row * row_bytes + j * 16));
       } else {
 #pragma unroll
         for (int ax = 0; ax < 3; ++ax) { pt.i0[ax] = -2; pt.f[ax] = 0.0f; pt.pass[ax] = false; }
       }
-      float go[EPV];
+      // grad_out in fp32 (dots) and a * grad_out rotated into this slot's
+      // accumulation order (value-gradient contributions).
+      float gof[EPV], ga[EPV];
       {
-        const Raw<16> rg = (active && has)
-            ? ld_chunk<16>(reinterpret_cast<const char*>(grad_out) + row * row_bytes + j * 16)
-            : raw_zero<16>();
-        CK::unpack(rg, go);
-      }
-      if (has) {
-        float4* dst = reinterpret_cast<float4*>(s_go + slot * C + j * EPV);
+        Raw<16> rg;
+        rg.w[0] = gor.x; rg.w[1] = gor.y; rg.w[2] = gor.z; rg.w[3] = gor.w;
+        CK::unpack(rg, gof);
 #pragma unroll
-        for (int e = 0; e < EPV; e += 4)
-          dst[e / 4] = make_float4(a * go[e], a * go[e + 1], a * go[e + 2], a * go[e + 3]);
+        for (int e = 0; e < EPV; ++e) ga[e] = a * gof[e];
+        rotate_left<EPV>(ga, rot);
       }
-      // Per-axis corner data.
+      // Per-axis: validity in the level, ownership by the tile, weights.
+      bool vv[3][2], ow[3][2];
+      float wt[3][2];
       int32_t lo[3];
-      bool v0[3], v1[3];
 #pragma unroll
       for (int ax = 0; ax < 3; ++ax) {
-        const int32_t o = ax == 0 ? ox : (ax == 1 ? oy : oz);
-        lo[ax] = pt.i0[ax] - o;
-        v0[ax] = pt.i0[ax] >= 0 && pt.i0[ax] < sz[ax];
-        v1[ax] = pt.i0[ax] + 1 >= 0 && pt.i0[ax] + 1 < sz[ax];
+        if (ax < NDIM) {
+          const int32_t i0 = pt.i0[ax];
+          const int32_t T_ = ax == 0 ? TX : (ax == 1 ? TY : TZ);
+          lo[ax] = i0 - org[ax];
+          vv[ax][0] = static_cast<uint32_t>(i0) < static_cast<uint32_t>(sz[ax]);
+          vv[ax][1] = static_cast<uint32_t>(i0 + 1) < static_cast<uint32_t>(sz[ax]);
+          ow[ax][0] = static_cast<uint32_t>(lo[ax]) < static_cast<uint32_t>(T_);
+          ow[ax][1] = static_cast<uint32_t>(lo[ax] + 1) < static_cast<uint32_t>(T_);
+          wt[ax][0] = __fsub_rn(1.0f, pt.f[ax]);
+          wt[ax][1] = pt.f[ax];
+        } else {
+          lo[ax] = 0;
+          vv[ax][0] = true; vv[ax][1] = false;
+          ow[ax][0] = true; ow[ax][1] = false;
+          wt[ax][0] = 1.0f; wt[ax][1] = 0.0f;
+        }
       }
-      if (NDIM == 2) { lo[2] = 0; v0[2] = true; v1[2] = false; }
-      float g_attn = 0.0f;
-      float g_ix[3] = {0.0f, 0.0f, 0.0f};
+      const int hbase = (lo[2] * HY + lo[1]) * HX + lo[0];
+      const int tbase = (lo[2] * TY + lo[1]) * TX + lo[0];
+      float dots[NC];
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
         const int bx = c & 1, by = (c >> 1) & 1, bz = (c >> 2) & 1;
-        const bool valid = (bx ? v1[0] : v0[0]) && (by ? v1[1] : v0[1]) && (bz ? v1[2] : v0[2]);
-        const int32_t lx = lo[0] + bx, ly = lo[1] + by, lz = lo[2] + bz;
-        const float wx = bx ? pt.f[0] : 1.0f - pt.f[0];
-        const float wy = by ? pt.f[1] : 1.0f - pt.f[1];
-        const float wz = (NDIM == 3) ? (bz ? pt.f[2] : 1.0f - pt.f[2]) : 1.0f;
-        const float w = wx * wy * wz;
+        const bool valid = vv[0][bx] && vv[1][by] && vv[2][bz];
+        float w = __fmul_rn(wt[0][bx], wt[1][by]);
+        if (NDIM == 3) w = __fmul_rn(w, wt[2][bz]);
+        w = valid ? w : 0.0f;
+        dots[c] = 0.0f;
         if (!secondary) {
-          float dot = 0.0f;
-          if (valid && has && lx >= 0 && lx <= TX && ly >= 0 && ly <= TY && lz >= 0 && lz < HZ) {
-            Raw<16> rv;
-            const uint4 u = *reinterpret_cast<const uint4*>(
-                s_val + ((lz * HY + ly) * HX + lx) * row_bytes + j * 16);
-            rv.w[0] = u.x; rv.w[1] = u.y; rv.w[2] = u.z; rv.w[3] = u.w;
-            float x[EPV];
-            CK::unpack(rv, x);
+          // All valid corners of a primary record lie in the tile + halo.
+          const int hidx = valid ? hbase + bx + by * HX + bz * HX * HY : nhalo;
+          const uint4 xv = *reinterpret_cast<const uint4*>(s_val + hidx * row_bytes + j * 16);
+#if MSDA_MIXED_PRECISION_DOT
+          dots[c] = chunk_dot<T>(gor, xv, 0.0f);
+#else
+          Raw<16> rv;
+          rv.w[0] = xv.x; rv.w[1] = xv.y; rv.w[2] = xv.z; rv.w[3] = xv.w;
+          float xf[EPV];
+          CK::unpack(rv, xf);
+          float d = 0.0f;
 #pragma unroll
-            for (int e = 0; e < EPV; ++e) dot = fmaf(go[e], x[e], dot);
-          }
-          g_attn = fmaf(w, dot, g_attn);
-          const float sx = bx ? 1.0f : -1.0f, sy = by ? 1.0f : -1.0f, sz_ = bz ? 1.0f : -1.0f;
-          g_ix[0] = fmaf(sx * wy * wz, dot, g_ix[0]);
-          g_ix[1] = fmaf(sy * wx * wz, dot, g_ix[1]);
-          if (NDIM == 3) g_ix[2] = fmaf(sz_ * wx * wy, dot, g_ix[2]);
+          for (int e = 0; e < EPV; ++e) d = fmaf(gof[e], xf[e], d);
+          dots[c] = d;
+#endif
         }
-        // Corner c's pair is emitted by lane (c mod G) of the record.
-        if ((c & (G - 1)) == j) {
-          const bool owned = active && valid && lx >= 0 && lx < TX && ly >= 0 && ly < TY &&
-                             lz >= 0 && lz < TZ;
-          int32_t pv = -1;
-          if (owned) {
-            const int vox = (lz * TY + ly) * TX + lx;
-            const int rank = atomicAdd(&s_cnt[vox], 1);
-            pv = vox | (rank << 10);
-          }
-          s_pvr[slot * 8 + c] = pv;
-          s_pw[slot * 8 + c] = w;
+        if (valid && ow[0][bx] && ow[1][by] && ow[2][bz] && has) {
+          float* gr = s_grad + (tbase + bx + by * TX + bz * TX * TY) * C;
+#pragma unroll
+          for (int e = 0; e < EPV; ++e) red_shared_f32(gr + eoff[e], w * ga[e]);
         }
       }
-      if (NC == 4 && j == 0) {  // 2D: the unused pair slots
+      // Per-sample scalars (d out / d attn, d out / d source index).
+      float g_attn = 0.0f, g_ix[3] = {0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int c = 4; c < 8; ++c) s_pvr[slot * 8 + c] = -1;
+      for (int c = 0; c < NC; ++c) {
+        const int bx = c & 1, by = (c >> 1) & 1, bz = (c >> 2) & 1;
+        const float wyz = (NDIM == 3) ? wt[1][by] * wt[2][bz] : wt[1][by];
+        const float wxz = (NDIM == 3) ? wt[0][bx] * wt[2][bz] : wt[0][bx];
+        const float d = dots[c];
+        g_attn = fmaf(wt[0][bx] * wyz, d, g_attn);
+        g_ix[0] = fmaf(bx ? wyz : -wyz, d, g_ix[0]);
+        g_ix[1] = fmaf(by ? wxz : -wxz, d, g_ix[1]);
+        if (NDIM == 3) {
+          const float wxy = wt[0][bx] * wt[1][by];
+          g_ix[2] = fmaf(bz ? wxy : -wxy, d, g_ix[2]);
+        }
       }
       for (int o = G >> 1; o > 0; o >>= 1) {
         g_attn += __shfl_xor_sync(0xffffffffu, g_attn, o);
@@ -530,83 +600,32 @@ __global__ void __launch_bounds__(kTileThreads, 2)
           gl[ax] = Elem<TS>::from_f(pt.pass[ax] ? gval : 0.0f);
         }
       }
-      __syncthreads();
-      // ---- B: exclusive scan of the per-voxel pair counts
-      for (int base = 0; base < V; base += kTileThreads) {
-        const int i = base + threadIdx.x;
-        const int32_t cnt = i < V ? s_cnt[i] : 0;
-        int32_t total;
-        const int32_t ex = block_exclusive_scan(cnt, s_warp, total);
-        const int32_t carry = base ? s_off[base] : 0;
-        if (i < V) {
-          s_off[i] = carry + ex;
-          s_cnt[i] = 0;
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) s_off[min(base + kTileThreads, V)] = carry + total;
-        __syncthreads();
-      }
-      // ---- C: pairs into voxel order
-      for (int i = threadIdx.x; i < R * 8; i += kTileThreads) {
-        const int32_t pv = s_pvr[i];
-        if (pv >= 0) s_sorted[s_off[pv & 1023] + (pv >> 10)] = make_int2(i >> 3, __float_as_int(s_pw[i]));
-      }
-      __syncthreads();
-      // ---- D: owners accumulate in registers
-#pragma unroll
-      for (int k = 0; k < kMaxUnitsPerThread; ++k) {
-        if (k < upt) {
-          const int u = threadIdx.x + k * kTileThreads;
-          if (u < nunits) {
-            const int vox = u / NU, g8 = u - vox * NU;
-            const int32_t e0 = s_off[vox], e1 = s_off[vox + 1];
-            for (int32_t e = e0; e < e1; ++e) {
-              const int2 sp = s_sorted[e];
-              const float w = __int_as_float(sp.y);
-              const float4* src = reinterpret_cast<const float4*>(s_go + sp.x * C + g8 * 8);
-              const float4 lo4 = src[0], hi4 = src[1];
-              acc[k][0] = fmaf(w, lo4.x, acc[k][0]);
-              acc[k][1] = fmaf(w, lo4.y, acc[k][1]);
-              acc[k][2] = fmaf(w, lo4.z, acc[k][2]);
-              acc[k][3] = fmaf(w, lo4.w, acc[k][3]);
-              acc[k][4] = fmaf(w, hi4.x, acc[k][4]);
-              acc[k][5] = fmaf(w, hi4.y, acc[k][5]);
-              acc[k][6] = fmaf(w, hi4.z, acc[k][6]);
-              acc[k][7] = fmaf(w, hi4.w, acc[k][7]);
-            }
-          }
-        }
-      }
-      __syncthreads();
     }
+    __syncthreads();
 
-    // Flush the owned units: one write per gradient element (direct levels)
-    // or one vector reduction into the fp32 accumulator (atomic levels).
+    // Flush: one write per gradient element (direct levels) or one vector
+    // reduction into the fp32 accumulator (atomic levels).
+    for (int i = threadIdx.x; i < V * (C / EPV); i += kTileThreads) {
+      const int v = i / (C / EPV);
+      const int ck = i - v * (C / EPV);
+      const int lx = v % TX, ly = (v / TX) % TY, lz = v / (TX * TY);
+      const int32_t x = org[0] + lx, y = org[1] + ly, z = org[2] + lz;
+      if (x >= sz[0] || y >= sz[1] || z >= sz[2]) continue;
+      const float* src = s_grad + v * C + ck * EPV;
+      float f[EPV];
 #pragma unroll
-    for (int k = 0; k < kMaxUnitsPerThread; ++k) {
-      if (k < upt) {
-        const int u = threadIdx.x + k * kTileThreads;
-        if (u < nunits) {
-          const int vox = u / NU, g8 = u - vox * NU;
-          const int lx = vox % TX, ly = (vox / TX) % TY, lz = vox / (TX * TY);
-          const int32_t x = ox + lx, y = oy + ly, z = oz + lz;
-          if (x < sz[0] && y < sz[1] && z < sz[2]) {
-            const int64_t kil = (static_cast<int64_t>(z) * sz[1] + y) * sz[0] + x;
-            if (atomic_level) {
-              float* dst = bb.acc + ((b * bp.acc_keys + bp.acc_start[l] + kil) * p.H + h) * C + g8 * 8;
-              red_add_f32<8>(dst, acc[k]);
-            } else {
-              char* dst = reinterpret_cast<char*>(grad_value) +
-                          ((b * p.K + start + kil) * p.H + h) * row_bytes + g8 * 8 * sizeof(T);
-              if constexpr (sizeof(T) == 2) {
-                st_chunk<16>(dst, Chunk<T, 16>::pack(acc[k]));
-              } else {
-                st_chunk<16>(dst, Chunk<T, 16>::pack(acc[k]));
-                st_chunk<16>(dst + 16, Chunk<T, 16>::pack(acc[k] + 4));
-              }
-            }
-          }
-        }
+      for (int e = 0; e < EPV; e += 4) {
+        const float4 t4 = *reinterpret_cast<const float4*>(src + e);
+        f[e] = t4.x; f[e + 1] = t4.y; f[e + 2] = t4.z; f[e + 3] = t4.w;
+      }
+      const int64_t kil = (static_cast<int64_t>(z) * sz[1] + y) * sz[0] + x;
+      if (atomic_level) {
+        float* dst = bb.acc + ((b * bp.acc_keys + bp.acc_start[l] + kil) * p.H + h) * C + ck * EPV;
+        red_add_f32<EPV>(dst, f);
+      } else {
+        char* dst = reinterpret_cast<char*>(grad_value) +
+                    ((b * p.K + start + kil) * p.H + h) * static_cast<int64_t>(row_bytes) + ck * 16;
+        st_chunk<16>(dst, CK::pack(f));
       }
     }
     __syncthreads();

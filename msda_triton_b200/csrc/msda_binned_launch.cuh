@@ -61,10 +61,12 @@ cudaError_t launch_bwd_binned(const BinLaunch& bl, const Problem& p, const BinPl
   auto count_k = bl.ndim == 2 ? msda_bin_kernel<TS, 2, false> : msda_bin_kernel<TS, 3, false>;
   auto fill_k = bl.ndim == 2 ? msda_bin_kernel<TS, 2, true> : msda_bin_kernel<TS, 3, true>;
   if (bin_smem * 2 > 48 * 1024) {
-    cudaFuncSetAttribute(count_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(bin_smem));
-    cudaFuncSetAttribute(fill_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(bin_smem * 2));
+    if ((err = cudaFuncSetAttribute(count_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(bin_smem))) != cudaSuccess)
+      return err;
+    if ((err = cudaFuncSetAttribute(fill_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(bin_smem * 2))) != cudaSuccess)
+      return err;
   }
   count_k<<<bin_grid, 512, bin_smem, st>>>(p, bp, bb);
   if ((err = cudaGetLastError()) != cudaSuccess) return err;

@@ -280,12 +280,21 @@ int prepare_bwd(const Args& a, const void* go, const void* gv_like, void* gl, vo
 // The gather/scatter backward of 16-bit values reads 8-byte chunks (4
 // channels, one 16-byte fp32 vector reduction each): same lanes per row,
 // twice the chunks per lane.
-void bwd_gather_shape(const Args& a, const Problem& p, LaunchShape& ls) {
+void bwd_gather_shape(const Args& a, Problem& p, LaunchShape& ls) {
   if (dtype_bytes(a.vdt) == 2 && ls.vb == 16) {
     ls.vb = 8;
-    ls.vpl *= 2;
+    // Twice the lanes per row (up to a warp) rather than twice the chunks per
+    // lane: each warp-wide reduction then covers whole 128-byte lines of the
+    // accumulator, one line touch per row instead of two.
+    const int64_t nv = a.C * 2 / 8;
+    if (p.log2g < 5 && (int64_t{1} << (p.log2g + 1)) <= nv && ls.vpl == 1 &&
+        std::getenv("MSDA_BWD_WIDE_ROWS") == nullptr) {
+      p.log2g += 1;
+      ls.grid *= 2;
+    } else {
+      ls.vpl *= 2;
+    }
   }
-  (void)p;
 }
 
 // Launch the scatter kernel (or zero-fill the per-sample gradients when
@@ -319,9 +328,9 @@ cudaError_t cast_from_f32(const float* src, void* dst, int dt, int64_t n, cudaSt
 // tile kernel (msda_binned.cuh) for large problems with host-resident shapes
 // and 16-byte channel rows.  The plan picks one and lays out the workspace.
 constexpr int64_t kBinnedMinSamples = int64_t{1} << 18;
-constexpr int kBinSmemBudget = 110 * 1024;   // two tile CTAs per SM
+constexpr int kBinSmemBudget = 72 * 1024;    // three tile CTAs per SM
 constexpr int64_t kAtomicLevelRecords = 8192;
-constexpr int kMaxTilesPerBh = 12288;
+constexpr int kMaxTilesPerBh = 24576;   // fill-pass histogram: 2 ints per tile in smem
 
 struct BwdPlan {
   bool binned = false;
@@ -333,13 +342,13 @@ struct BwdPlan {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
 
-// Shared memory of the tile kernel for a tile shape: value tile + halo,
-// staged a*grad_out rows, pair lists and per-voxel counters of one chunk.
+// Shared memory of the tile kernel for a tile shape: value tile + halo + one
+// zero row, and the tile's fp32 value gradient.
 int64_t tile_smem_bytes(int ndim, const int32_t* t, int64_t row_bytes, int64_t C, int G) {
   const int64_t halo = int64_t{t[0] + 1} * (t[1] + 1) * (ndim == 3 ? t[2] + 1 : 1);
   const int64_t vox = int64_t{t[0]} * t[1] * t[2];
-  const int64_t R = kTileThreads / G;
-  return halo * row_bytes + R * C * 4 + R * 8 * 4 * 2 + R * 8 * 8 + (2 * vox + 1) * 4;
+  (void)G;
+  return (halo + 1) * row_bytes + vox * C * 4;
 }
 
 bool choose_tile(int ndim, int64_t row_bytes, int64_t C, int G, int budget, int32_t* tile,
@@ -356,8 +365,6 @@ bool choose_tile(int ndim, int64_t row_bytes, int64_t C, int G, int budget, int3
   for (int i = -1; i < 7; ++i) {
     const int32_t* t = i < 0 ? forced : (ndim == 3 ? c3[i] : c2[i]);
     if (t[0] <= 0 || t[1] <= 0 || t[2] <= 0) continue;
-    const int64_t vox = int64_t{t[0]} * t[1] * t[2];
-    if (vox * C > int64_t{8} * 8 * kTileThreads || vox > 1024) continue;  // owner registers
     const int64_t bytes = tile_smem_bytes(ndim, t, row_bytes, C, G);
     if (bytes <= budget || (i < 0 && bytes <= 200 * 1024)) {
       tile[0] = t[0]; tile[1] = t[1]; tile[2] = t[2];
@@ -379,9 +386,9 @@ void plan_bwd(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan& p
   const bool force_binned = env && std::strcmp(env, "binned") == 0;
   const bool force_gather = !force_binned;
   bool ok_binned = !force_gather && p.shapes_dev == nullptr && ls.vb == 16 && ls.vpl == 1 &&
-                   a.C % 8 == 0 && samples > 0 && a.C > 0 &&
-                   (force_binned || samples >= kBinnedMinSamples) &&
-                   a.Q * a.P < (int64_t{1} << 30) && samples * (int64_t{1} << a.ndim) < INT32_MAX;
+                   samples > 0 && a.C > 0 && (force_binned || samples >= kBinnedMinSamples) &&
+                   a.P <= 16 && a.Q < (int64_t{1} << 26) && a.L * a.P <= 512 &&
+                   samples * (int64_t{1} << a.ndim) < INT32_MAX;
   for (int64_t l = 0; ok_binned && l < a.L; ++l)
     for (int ax = 0; ax < 3; ++ax) ok_binned = ok_binned && p.lv.size[l][ax] > 0;
   int smem = 0;

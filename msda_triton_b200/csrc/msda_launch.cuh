@@ -19,7 +19,7 @@ struct LaunchShape {
 // backward's layout for 16-bit values (see msda_bwd_kernel).
 template <int VB, int VPL>
 constexpr bool kAllowed = (VB == 16 && (VPL == 1 || VPL == 2 || VPL == 4)) ||
-                          (VB == 8 && (VPL == 2 || VPL == 4 || VPL == 8)) ||
+                          (VB == 8 && (VPL == 1 || VPL == 2 || VPL == 4 || VPL == 8)) ||
                           ((VB == 4 || VB == 2) && (VPL == 1 || VPL == 8));
 
 template <typename T, typename TS, int NDIM, int VB, int VPL>
