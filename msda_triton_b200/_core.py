@@ -204,6 +204,55 @@ def backward(
     return grad_value, grad_loc, grad_attn
 
 
+def backward_accumulate(
+    ndim: int,
+    value: torch.Tensor,
+    shapes: torch.Tensor,
+    on_dev: bool,
+    loc: torch.Tensor,
+    attn: torch.Tensor,
+    clamp_grid: bool,
+    clamp_eps: float,
+    grad_output: torch.Tensor,
+    grad_value_accum: torch.Tensor,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Backward scatter only: ADDS the value gradient (fp32) into
+    grad_value_accum and returns (grad_loc, grad_attn).  Used where partial
+    value gradients are summed before one final cast (query sharding)."""
+    if grad_value_accum.dtype != torch.float32 or grad_value_accum.shape != value.shape:
+        raise ValueError("grad_value_accum must be an fp32 tensor shaped like value")
+    go = grad_output
+    if go.dtype != value.dtype:
+        go = go.to(value.dtype)
+    go = go.contiguous()
+    grad_loc = torch.empty_like(loc)
+    grad_attn = torch.empty_like(attn)
+    lib = _lib.lib()
+    fn = lib.msda2d_bwd_accumulate if ndim == 2 else lib.msda3d_bwd_accumulate
+    with torch.cuda.device(value.device):
+        code = fn(
+            *_common_args(value, shapes, on_dev, loc, attn),
+            int(bool(clamp_grid)), float(clamp_eps),
+            go.data_ptr(), grad_value_accum.data_ptr(), grad_loc.data_ptr(), grad_attn.data_ptr(),
+            _stream_ptr(value.device),
+        )
+    check_status(code)
+    return grad_loc, grad_attn
+
+
+def cast_from_f32(src: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Round an fp32 tensor to `dtype` with the library's cast kernel."""
+    if dtype == torch.float32:
+        return src
+    src = src.contiguous()
+    dst = torch.empty(src.shape, device=src.device, dtype=dtype)
+    with torch.cuda.device(src.device):
+        code = _lib.lib().msda_cast_from_f32(src.data_ptr(), dst.data_ptr(), _DTYPE_CODE[dtype],
+                                             src.numel(), _stream_ptr(src.device))
+    check_status(code)
+    return dst
+
+
 def fwd_entry(ndim, value, value_spatial_shapes, sampling_locations, attention_weights,
               clamp_grid, clamp_eps) -> torch.Tensor:
     validate_inputs(ndim, value, value_spatial_shapes, sampling_locations, attention_weights)
