@@ -117,6 +117,7 @@ int prepare(const Args& a, const void* const* bufs, int nbufs, Problem& p, Launc
   p.loc = a.loc;
   p.attn = a.attn;
   p.B = a.B; p.K = a.K; p.H = a.H; p.C = a.C; p.Q = a.Q; p.L = a.L; p.P = a.P;
+  p.acc_keys = a.K;  // accumulator in value's key layout unless a plan compacts it
   p.clamp = a.clamp ? 1 : 0;
   p.lo = static_cast<float>(-1.0 + a.eps);
   p.hi = static_cast<float>(1.0 - a.eps);
@@ -332,13 +333,49 @@ constexpr int kBinSmemBudget = 72 * 1024;    // three tile CTAs per SM
 constexpr int64_t kAtomicLevelRecords = 8192;
 constexpr int kMaxTilesPerBh = 24576;   // fill-pass histogram: 2 ints per tile in smem
 
+// Gather path, 16-bit values: a level whose expected contributions per
+// grad_value element (2^d corners x Q x P samples / voxels) stay at or below
+// this bound reduces straight into grad_value in its own dtype -- the
+// reference accumulates every level that way -- so its fp32 accumulator rows,
+// their zero-fill and their cast disappear.  Busier levels keep fp32
+// accumulation, which bounds their rounding error.
+constexpr double kDirect16Contrib = 8.0;
+
 struct BwdPlan {
   bool binned = false;
   BinPlan bp{};
   BinLaunch bl{};
   size_t off[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // counts, starts, cursor, item_start, item_counter, scan_tmp, records, acc
   size_t ws_bytes = 0;
+  // gather path
+  int32_t direct16 = 0;   // levels reduced straight into grad_value
+  bool compact = false;   // fp32 accumulator holds only the other levels
+  int64_t acc_keys = 0;   // keys per batch entry in the fp32 accumulator
+  int32_t acc_start[kMaxLevels] = {};
 };
+
+// Gather-path value-gradient targets (see kDirect16Contrib).
+void plan_gather_targets(const Args& a, const Problem& p, BwdPlan& pl) {
+  pl.acc_keys = a.K;
+  if (dtype_bytes(a.vdt) != 2 || p.shapes_dev != nullptr || a.K == 0) return;
+  const char* env = std::getenv("MSDA_BWD_DIRECT16");
+  if (env && std::strcmp(env, "0") == 0) return;
+  int64_t keys = 0;
+  for (int64_t l = 0; l < a.L; ++l) {
+    const int64_t nvox = int64_t{p.lv.size[l][0]} * p.lv.size[l][1] * p.lv.size[l][2];
+    const double contrib = static_cast<double>(int64_t{1} << a.ndim) * a.Q * a.P /
+                           static_cast<double>(std::max<int64_t>(nvox, 1));
+    if (contrib <= kDirect16Contrib) {
+      pl.direct16 |= 1 << l;
+    } else {
+      pl.acc_start[l] = static_cast<int32_t>(keys);
+      keys += nvox;
+    }
+  }
+  if (pl.direct16 == 0) return;
+  pl.compact = true;
+  pl.acc_keys = keys;
+}
 
 size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
 
@@ -377,7 +414,6 @@ bool choose_tile(int ndim, int64_t row_bytes, int64_t C, int G, int budget, int3
 
 void plan_bwd(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan& pl) {
   const int64_t e = dtype_bytes(a.vdt);
-  const int64_t nval = a.B * a.K * a.H * a.C;
   const int64_t samples = a.B * a.Q * a.H * a.L * a.P;
   pl = BwdPlan{};
   const char* env = std::getenv("MSDA_BWD_PATH");
@@ -436,7 +472,9 @@ void plan_bwd(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan& p
   }
   if (!ok_binned) {
     pl.binned = false;
-    pl.ws_bytes = (a.vdt == MSDA_FLOAT32) ? 0 : static_cast<size_t>(nval) * sizeof(float);
+    plan_gather_targets(a, p, pl);
+    pl.ws_bytes = (a.vdt == MSDA_FLOAT32)
+                      ? 0 : static_cast<size_t>(a.B * pl.acc_keys * a.H * a.C) * sizeof(float);
     return;
   }
   pl.binned = true;
@@ -516,16 +554,37 @@ int run_bwd(const Args& a, const void* go, void* gv, void* gl, void* ga, void* w
   } else if (nval > 0) {
     gacc = static_cast<float*>(ws);
   }
-  if (nval > 0) {
-    err = cudaMemsetAsync(gacc, 0, static_cast<size_t>(nval) * sizeof(float), st);
+  p.direct16 = pl.direct16;
+  p.acc_compact = pl.compact ? 1 : 0;
+  p.acc_keys = pl.acc_keys;
+  for (int l = 0; l < kMaxLevels; ++l) p.acc_start[l] = pl.acc_start[l];
+  p.grad_value16 = pl.direct16 ? gv : nullptr;
+  const int64_t row_bytes = a.H * a.C * dtype_bytes(a.vdt);
+  const int64_t nacc = a.B * pl.acc_keys * a.H * a.C;
+  if (nacc > 0) {
+    err = cudaMemsetAsync(gacc, 0, static_cast<size_t>(nacc) * sizeof(float), st);
     if (err != cudaSuccess) return cuda_fail(err, "zeroing the grad_value accumulator");
+  }
+  // Direct levels: their grad_value rows (one span per batch entry) start at 0.
+  for (int64_t l = 0; l < a.L && nval > 0; ++l) {
+    if (!((pl.direct16 >> l) & 1)) continue;
+    const int64_t nvox = int64_t{p.lv.size[l][0]} * p.lv.size[l][1] * p.lv.size[l][2];
+    if (nvox == 0) continue;
+    err = cudaMemset2DAsync(static_cast<char*>(gv) + p.lv.start[l] * row_bytes,
+                            static_cast<size_t>(a.K * row_bytes), 0,
+                            static_cast<size_t>(nvox * row_bytes), static_cast<size_t>(a.B), st);
+    if (err != cudaSuccess) return cuda_fail(err, "zeroing grad_value rows");
   }
   bwd_gather_shape(a, p, ls);
   p.nv = static_cast<int32_t>(a.C * dtype_bytes(a.vdt) / ls.vb);
   rc = launch_accumulate(a, p, ls, go, gacc, gl, ga, st);
   if (rc != MSDA_SUCCESS) return rc;
   if (a.vdt != MSDA_FLOAT32 && nval > 0) {
-    err = cast_from_f32(gacc, gv, a.vdt, nval, st);
+    if (pl.compact)
+      err = a.vdt == MSDA_FLOAT16 ? launch_compact_cast<__half>(p, gacc, gv, st)
+                                  : launch_compact_cast<__nv_bfloat16>(p, gacc, gv, st);
+    else
+      err = cast_from_f32(gacc, gv, a.vdt, nval, st);
     if (err != cudaSuccess) return cuda_fail(err, "grad_value cast launch");
   }
   return ok();

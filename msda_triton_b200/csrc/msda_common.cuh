@@ -43,6 +43,17 @@ struct Problem {
   int32_t clamp;      // clamp_grid
   float lo, hi;       // clamp window in grid space
   LevelTable lv;      // host-resolved table (used when shapes_dev == nullptr)
+  // Backward value-gradient targets of the gather/scatter kernel (16-bit
+  // values).  Level l reduces straight into grad_value16 (same layout as
+  // value) when bit l of direct16 is set, else into the fp32 accumulator,
+  // whose rows are keys [0, acc_keys) per batch: with acc_compact the keys of
+  // level l start at acc_start[l] (only non-direct levels are stored), else
+  // the accumulator has value's own key layout (acc_keys == K).
+  int32_t direct16;
+  int32_t acc_compact;
+  int64_t acc_keys;
+  int32_t acc_start[kMaxLevels];
+  void* grad_value16;
 };
 
 // ---------------------------------------------------------------- types

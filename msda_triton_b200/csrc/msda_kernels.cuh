@@ -14,6 +14,8 @@
 // _bwd_kernel (src/msda_triton/triton/msda_3d.py:80-288, :291-653).
 #pragma once
 
+#include <type_traits>
+
 #include "msda_common.cuh"
 
 namespace msda {
@@ -242,6 +244,55 @@ __device__ __forceinline__ void red_add_f32(float* dst, const float* v) {
   }
 }
 
+// Vector reductions of N 16-bit channels straight into a bf16/fp16 tensor
+// (red.global.add.noftz.v{2,4}.{bf16x2,f16x2} is sm_90+).  Each pair of fp32
+// contributions is rounded to the element type once, then added by the L2.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_pair(float a, float b) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void red_add_16(T* dst, const float* v) {
+  constexpr bool kBf = std::is_same<T, __nv_bfloat16>::value;
+  if constexpr (N % 8 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 8) {
+      const uint32_t a = pack_pair<T>(v[i], v[i + 1]), b = pack_pair<T>(v[i + 2], v[i + 3]);
+      const uint32_t c = pack_pair<T>(v[i + 4], v[i + 5]), d = pack_pair<T>(v[i + 6], v[i + 7]);
+      if constexpr (kBf)
+        asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst + i),
+                     "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+      else
+        asm volatile("red.global.add.noftz.v4.f16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst + i),
+                     "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+    }
+  } else if constexpr (N == 4) {
+    const uint32_t a = pack_pair<T>(v[0], v[1]), b = pack_pair<T>(v[2], v[3]);
+    if constexpr (kBf)
+      asm volatile("red.global.add.noftz.v2.bf16x2 [%0], {%1, %2};" ::"l"(dst), "r"(a), "r"(b)
+                   : "memory");
+    else
+      asm volatile("red.global.add.noftz.v2.f16x2 [%0], {%1, %2};" ::"l"(dst), "r"(a), "r"(b)
+                   : "memory");
+  } else if constexpr (N == 2) {
+    const uint32_t a = pack_pair<T>(v[0], v[1]);
+    if constexpr (kBf)
+      asm volatile("red.global.add.noftz.bf16x2 [%0], %1;" ::"l"(dst), "r"(a) : "memory");
+    else
+      asm volatile("red.global.add.noftz.f16x2 [%0], %1;" ::"l"(dst), "r"(a) : "memory");
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) atomicAdd(dst + i, Elem<T>::from_f(v[i]));
+  }
+}
+
 // One pass produces all three gradients.  grad_out is read once per row
 // (the reference re-reads it for every (level, point), msda_3d.py:451-455).
 // grad_loc and grad_attn are reduced inside the lane group with shuffles and
@@ -251,7 +302,12 @@ __device__ __forceinline__ void red_add_f32(float* dst, const float* v) {
 // that msda_cast_kernel rounds to the input dtype).  For 16-bit inputs the
 // host picks 8-byte chunks (VB = 8): lane j then owns channel groups j, j+G,
 // ... of 4 channels, so one red.v4.f32 per group and the G lanes of a row
-// cover whole 32-byte sectors of the accumulator.
+// cover whole 32-byte sectors of the accumulator.  Levels flagged in
+// p.direct16 (few contributions per element) instead reduce with 16-bit
+// vector reductions straight into grad_value, as the reference's own
+// atomic_add into a grad_value of the input dtype does
+// (src/msda_triton/triton/msda_3d.py:477, :942); the other levels keep fp32
+// accumulation, possibly in a compacted accumulator (p.acc_start).
 template <typename T, typename TS, int NDIM, int VB, int VPL>
 __global__ void __launch_bounds__(kThreads)
     msda_bwd_kernel(const Problem p, const T* __restrict__ grad_out, float* __restrict__ gacc,
@@ -278,8 +334,6 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t key_bytes = HC * static_cast<int64_t>(sizeof(T));
   const char* vbase = static_cast<const char*>(p.value) +
                       (rc.b * p.K * p.H + rc.h) * p.C * static_cast<int64_t>(sizeof(T));
-  // fp32 accumulator row base, addressed with the same key offsets scaled.
-  float* gbase = gacc + (rc.b * p.K * p.H + rc.h) * p.C;
   const int LP = static_cast<int>(p.L * p.P);
   const TS* lrow = static_cast<const TS*>(p.loc) + row * LP * NDIM;
   const TS* arow = static_cast<const TS*>(p.attn) + row * LP;
@@ -299,8 +353,19 @@ __global__ void __launch_bounds__(kThreads)
 
   const int P = static_cast<int>(p.P);
   const char* vlane = vbase + j * VB;
+  // A corner's value row sits at byte offset vo from vlane (key * key_bytes).
+  // The same key's fp32 accumulator row is at vo * 4 / sizeof(T) from the
+  // level's accumulator base (keys shifted to the compacted layout), and its
+  // grad_value row (direct levels) at the same byte offset vo.
+  const int64_t vrow = (rc.b * p.K * p.H + rc.h) * p.C;
+  char* g16lane = static_cast<char*>(p.grad_value16) + vrow * static_cast<int64_t>(sizeof(T)) +
+                  j * VB;
   for (int l = 0; l < p.L; ++l) {
     const LevelGeom g = level_geom(lv, l, key_bytes);
+    const bool d16 = (sizeof(T) == 2) && ((p.direct16 >> l) & 1);
+    const int64_t kshift = p.acc_compact ? p.acc_start[l] - g.start : 0;
+    char* acc_lane = reinterpret_cast<char*>(
+        gacc + ((rc.b * p.acc_keys + kshift) * p.H + rc.h) * p.C + j * EPV);
     for (int pp = 0; pp < P; ++pp) {
       const int s = l * P + pp;
       Point<NDIM> pt;
@@ -339,18 +404,21 @@ __global__ void __launch_bounds__(kThreads)
         dots[c] = dot;
         if (cs.valid[c]) {
           const float aw = a * cs.w[c];
-          // The accumulator row of a corner sits at the value row's byte
-          // offset scaled by 4 / sizeof(T) (same key, fp32 elements).
           const int64_t vo = cs.ptr[c] - vlane;
-          float* gk = reinterpret_cast<float*>(reinterpret_cast<char*>(gbase) +
-                                               vo * static_cast<int64_t>(4 / sizeof(T)));
 #pragma unroll
           for (int v = 0; v < VPL; ++v) {
             if (has[v]) {
               float t[EPV];
 #pragma unroll
               for (int e = 0; e < EPV; ++e) t[e] = aw * go[v][e];
-              red_add_f32<EPV>(gk + (j + v * G) * EPV, t);
+              if constexpr (sizeof(T) == 2) {
+                if (d16) {
+                  red_add_16<T, EPV>(reinterpret_cast<T*>(g16lane + vo + v * G * VB), t);
+                  continue;
+                }
+              }
+              red_add_f32<EPV>(reinterpret_cast<float*>(acc_lane + vo * (4 / sizeof(T))) +
+                                   v * G * EPV, t);
             }
           }
         }
@@ -400,6 +468,42 @@ __global__ void __launch_bounds__(kThreads)
       dst[i + 3] = Elem<T>::from_f(v.w);
     } else {
       for (int64_t k = i; k < n; ++k) dst[k] = Elem<T>::from_f(src[k]);
+    }
+  }
+}
+
+// Compacted fp32 accumulator (the keys of the levels not in p.direct16,
+// p.acc_keys per batch entry) -> their grad_value rows in the input dtype.
+// V = 4: one float4 in, one 8-byte store out (16-bit T, H*C % 4 == 0,
+// grad_value 8-byte aligned); V = 1 otherwise.
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads)
+    msda_compact_cast_kernel(const Problem p, const float* __restrict__ acc, T* __restrict__ gv) {
+  const int64_t row = p.H * p.C;  // elements per key
+  const int64_t rv = row / V;
+  const int64_t n = p.B * p.acc_keys * rv;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t r = i / rv;
+    const int64_t e = (i - r * rv) * V;
+    const int64_t b = r / p.acc_keys;
+    const int64_t ak = r - b * p.acc_keys;
+    int64_t shift = 0;  // key - accumulator key of the level holding ak
+#pragma unroll
+    for (int k = 0; k < kMaxLevels; ++k)
+      if (k < p.L && !((p.direct16 >> k) & 1) && ak >= p.acc_start[k])
+        shift = static_cast<int64_t>(p.lv.start[k]) - p.acc_start[k];
+    T* dst = gv + (b * p.K + ak + shift) * row + e;
+    if constexpr (V == 4) {
+      const float4 v = *reinterpret_cast<const float4*>(acc + r * row + e);
+      struct alignas(8) Quad { T h[4]; } o;
+      o.h[0] = Elem<T>::from_f(v.x);
+      o.h[1] = Elem<T>::from_f(v.y);
+      o.h[2] = Elem<T>::from_f(v.z);
+      o.h[3] = Elem<T>::from_f(v.w);
+      *reinterpret_cast<Quad*>(dst) = o;
+    } else {
+      *dst = Elem<T>::from_f(acc[r * row + e]);
     }
   }
 }

@@ -118,6 +118,24 @@ cudaError_t launch_cast(const float* src, void* dst, int64_t n, cudaStream_t st)
   return cudaGetLastError();
 }
 
+// Compacted accumulator -> grad_value rows of the non-direct levels (16-bit T).
+template <typename T>
+cudaError_t launch_compact_cast(const Problem& p, const float* acc, void* gv, cudaStream_t st) {
+  const int64_t row = p.H * p.C;
+  const bool vec = row % 4 == 0 && reinterpret_cast<uintptr_t>(gv) % 8 == 0;
+  const int64_t n = p.B * p.acc_keys * (vec ? row / 4 : row);
+  if (n <= 0) return cudaSuccess;
+  int64_t blocks = (n + kThreads - 1) / kThreads;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (vec)
+    msda_compact_cast_kernel<T, 4><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
+        p, acc, static_cast<T*>(gv));
+  else
+    msda_compact_cast_kernel<T, 1><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
+        p, acc, static_cast<T*>(gv));
+  return cudaGetLastError();
+}
+
 // Explicit instantiations live in msda_inst_*.cu.
 #define MSDA_DECLARE_PAIR(T, TS)                                                              \
   extern template cudaError_t launch_fwd<T, TS>(const LaunchShape&, const Problem&, void*,     \

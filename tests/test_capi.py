@@ -48,12 +48,24 @@ def _ws(dtype, B, shapes, H, C, Q, P, on_dev=0):
                                                on_dev, len(shapes), Q, P)
 
 
-def test_workspace_bytes_gather_path():
-    # Small problems use the gather/scatter backward: an fp32 accumulator for
-    # half-precision values, nothing for fp32.
+def test_workspace_bytes_gather_path(monkeypatch):
+    # The gather/scatter backward: nothing for fp32; for 16-bit values an fp32
+    # accumulator over the keys of the levels with more than 8 expected
+    # contributions per element (2^d * Q * P / voxels) -- sparser levels
+    # reduce straight into grad_value.
     assert _ws(_lib.FLOAT32, 2, [(10, 10)], 8, 32, 50, 4) == 0
-    assert _ws(_lib.BFLOAT16, 2, [(10, 10)], 8, 32, 50, 4) == 2 * 100 * 8 * 32 * 4
+    # 4 * 50 * 4 / 100 = 8 contributions: direct, no workspace
+    assert _ws(_lib.BFLOAT16, 2, [(10, 10)], 8, 32, 50, 4) == 0
+    # 4 * 51 * 4 / 100 > 8: the whole level in fp32
+    assert _ws(_lib.BFLOAT16, 2, [(10, 10)], 8, 32, 51, 4) == 2 * 100 * 8 * 32 * 4
+    # two levels: only the coarse one (4 * 50 * 4 / 25 = 32) is accumulated
+    assert _ws(_lib.FLOAT16, 2, [(10, 10), (5, 5)], 8, 32, 50, 4) == 2 * 25 * 8 * 32 * 4
+    # 3D: 8 corners per sample
+    assert _ws(_lib.BFLOAT16, 1, [(8, 8, 8), (4, 4, 4)], 2, 16, 128, 4) == 64 * 2 * 16 * 4
     assert _ws(_lib.FLOAT16, 0, [(10, 10)], 8, 32, 50, 4) == 0
+    # the switch that keeps every level in fp32
+    monkeypatch.setenv("MSDA_BWD_DIRECT16", "0")
+    assert _ws(_lib.BFLOAT16, 2, [(10, 10), (5, 5)], 8, 32, 50, 4) == 2 * 125 * 8 * 32 * 4
 
 
 def test_workspace_bytes_binned_path(monkeypatch):
@@ -130,8 +142,9 @@ def test_empty_problem_is_a_noop():
 def test_bwd_requires_workspace_for_half_types():
     lib = _lib.lib()
     shp = np.array([[4, 5]], dtype=np.int32)
+    # Q=100, P=2 on 20 cells: 40 contributions per element, fp32 accumulation
     rc = lib.msda2d_bwd(FAKE, _lib.BFLOAT16, 1, 20, 2, 8, shp.ctypes.data, 0, 1, FAKE, FAKE,
-                        _lib.BFLOAT16, 3, 2, 1, 1e-4, FAKE, FAKE, FAKE, FAKE, None, 0, None)
+                        _lib.BFLOAT16, 100, 2, 1, 1e-4, FAKE, FAKE, FAKE, FAKE, None, 0, None)
     assert rc == _lib.ERROR_WORKSPACE
     assert "workspace" in _lib.last_error()
 

@@ -48,14 +48,15 @@ def test_static_scratch_matches_workspace_backward(ndim, dtype):
 
 
 def test_static_scratch_rejects_oversized_problem():
-    # 3 * 100000 * 8 * 32 fp32 accumulators = 307 MB > 32 MiB: rejected on the
-    # host before any launch.
+    # 4 corners * 25000 queries * 2 points on 20000 cells = 10 contributions per
+    # element: the level is accumulated in fp32, 3 * 20000 * 8 * 32 * 4 bytes =
+    # 61 MB > 32 MiB: rejected on the host before any launch.
     dev = torch.device("cuda", 0)
-    shapes = torch.tensor([[100, 1000]], dtype=torch.int32)
-    value = torch.zeros(3, 100000, 8, 32, device=dev, dtype=torch.bfloat16)
-    loc = torch.zeros(3, 4, 8, 1, 2, 2, device=dev, dtype=torch.bfloat16)
-    attn = torch.zeros(3, 4, 8, 1, 2, device=dev, dtype=torch.bfloat16)
-    go = torch.zeros(3, 4, 256, device=dev, dtype=torch.bfloat16)
+    shapes = torch.tensor([[100, 200]], dtype=torch.int32)
+    value = torch.zeros(3, 20000, 8, 32, device=dev, dtype=torch.bfloat16)
+    loc = torch.zeros(3, 25000, 8, 1, 2, 2, device=dev, dtype=torch.bfloat16)
+    attn = torch.zeros(3, 25000, 8, 1, 2, device=dev, dtype=torch.bfloat16)
+    go = torch.zeros(3, 25000, 256, device=dev, dtype=torch.bfloat16)
     rc, *_ = _call_static(2, value, shapes, loc, attn, go)
     assert rc == _lib.ERROR_WORKSPACE
     assert "static scratch holds" in _lib.last_error()
