@@ -78,12 +78,7 @@ def algorithmic_bytes(wl, B=None):
     smp = B * Q * H * L * P
     fwd = e * (B * K * H * C + smp * d + smp + B * Q * H * C)
     bwd = e * (2 * B * K * H * C + 2 * smp * (d + 1) + B * Q * H * C)
-    # The backward scatter kernel alone: reads value/loc/weights/grad_out,
-    # writes loc/weight grads and the fp32 value-gradient accumulator.
-    acc_bytes = 4 if e == 2 else e
-    bwd_kernel = e * (B * K * H * C + smp * (d + 1) + B * Q * H * C) + e * smp * (d + 1) \
-        + acc_bytes * B * K * H * C
-    return {"fwd": fwd, "bwd": bwd, "fwd_bwd": fwd + bwd, "bwd_kernel": bwd_kernel,
+    return {"fwd": fwd, "bwd": bwd, "fwd_bwd": fwd + bwd,
             "samples": smp}
 
 
@@ -174,13 +169,15 @@ def _peaks():
         return 6650.0, "fallback"
 
 
-def _traffic(workload, kernel):
-    """DRAM bytes per launch from the committed ncu summary, if any."""
+def _traffic(workload, kernel, batch):
+    """DRAM bytes per launch from the committed ncu summary (bytes per batch
+    entry, which the per-batch head-group schedule keeps proportional to B)."""
     try:
         with open(os.path.join(ROOT, "profiles", "dram_traffic.json")) as f:
-            return json.load(f).get(workload, {}).get(kernel)
+            ent = json.load(f).get(workload, {}).get(kernel)
     except (OSError, ValueError):
         return None
+    return None if ent is None else float(ent["bytes_per_batch"]) * batch
 
 
 def time_events(fn, iters, stream):
@@ -256,7 +253,7 @@ def run_ours(args, wl, rank, world, local_rank):
     args_c = _core._common_args(value.detach(), shp, on_dev, loc.detach(), attn.detach())
     out_buf = torch.empty(B, Q, H * C, device=dev, dtype=wl["dtype"])
     fwd_c = lib.msda3d_fwd if wl["ndim"] == 3 else lib.msda2d_fwd
-    acc_c = lib.msda3d_bwd_accumulate if wl["ndim"] == 3 else lib.msda2d_bwd_accumulate
+    bwd_c = lib.msda3d_bwd if wl["ndim"] == 3 else lib.msda2d_bwd
     sp = stream.cuda_stream
     kiters = max(3, min(args.steps, 10))
 
@@ -265,17 +262,25 @@ def run_ours(args, wl, rank, world, local_rank):
 
     fwd_times = time_events(k_fwd, kiters + 2, stream)[2:]
     kern = {"fwd": statistics.mean(fwd_times)}
+    bwd_launches = 0
     if not fwd_only:
-        gacc = torch.zeros(B, K, H, C, device=dev, dtype=torch.float32)
+        # The backward entry exactly as the autograd path calls it: zero-fill
+        # of the value-gradient targets, the scatter kernel and (16-bit
+        # values with an fp32 accumulator) the cast kernel.
+        ws_bytes = lib.msda_bwd_workspace_bytes(wl["ndim"], _core._DTYPE_CODE[wl["dtype"]], B, K,
+                                                H, C, shp.data_ptr(), int(on_dev), L, Q, P)
+        ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+        gv = torch.empty_like(value)
         gl = torch.empty_like(loc)
         ga = torch.empty_like(attn)
 
         def k_bwd():
-            _core.check_status(acc_c(*args_c, 1, 1e-4, go.data_ptr(), gacc.data_ptr(),
-                                     gl.data_ptr(), ga.data_ptr(), sp))
+            _core.check_status(bwd_c(*args_c, 1, 1e-4, go.data_ptr(), gv.data_ptr(),
+                                     gl.data_ptr(), ga.data_ptr(), ws.data_ptr(), ws_bytes, sp))
 
-        kern["bwd_kernel"] = statistics.mean(time_events(k_bwd, kiters + 2, stream)[2:])
-        del gacc
+        kern["bwd"] = statistics.mean(time_events(k_bwd, kiters + 2, stream)[2:])
+        bwd_launches = 1 + (1 if wl["dtype"] != torch.float32 and ws_bytes > 0 else 0)
+        del ws, gv, gl, ga
     if dist is not None:
         for k in list(kern):
             tt = torch.tensor([kern[k]], device=dev, dtype=torch.float64)
@@ -295,12 +300,12 @@ def run_ours(args, wl, rank, world, local_rank):
     per_pass = ab["fwd"] if fwd_only else ab["fwd_bwd"]
     samples = ab["samples"] * world
     peak, peak_kind = _peaks()
-    dom = "fwd" if fwd_only or kern["fwd"] >= kern.get("bwd_kernel", 0.0) else "bwd_kernel"
-    dom_bytes = ab["fwd"] if dom == "fwd" else ab["bwd_kernel"]
+    dom = "fwd" if fwd_only or kern["fwd"] >= kern.get("bwd", 0.0) else "bwd"
+    dom_bytes = ab[dom]
     achieved = dom_bytes / (kern[dom] * 1e-3) / 1e9
-    traffic = _traffic(args.workload, dom)
+    traffic = _traffic(args.workload, dom, B)
     pass_gbs = per_pass / (ms * 1e-3) / 1e9
-    launches_per_step = 1 if fwd_only else 3 if wl["dtype"] != torch.float32 else 2
+    launches_per_step = 1 + bwd_launches
     res = {
         "metric": "MSDA fwd+bwd Gsamples/s" if not fwd_only else "MSDA fwd Gsamples/s",
         "value": samples / (ms * 1e-3) / 1e9,
@@ -323,11 +328,12 @@ def run_ours(args, wl, rank, world, local_rank):
                   f" > {L2_BYTES / 1e6:.0f} MB); no flush",
         },
         "fwd_ms": kern["fwd"],
-        "bwd_kernel_ms": kern.get("bwd_kernel"),
+        "bwd_ms": kern.get("bwd"),
         "pass_bytes": per_pass,
         "pass_roofline_frac": pass_gbs / peak,
         "roofline": {
-            "kernel": "msda_fwd_kernel" if dom == "fwd" else "msda_bwd_kernel",
+            "kernel": "msda_fwd_kernel" if dom == "fwd" else
+                      "backward entry (zero-fill + msda_bwd_kernel + cast)",
             "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak, "peak_source": peak_kind,
             "algorithmic_bytes": dom_bytes, "traffic": traffic,
@@ -399,6 +405,92 @@ def run_e2e(args, wl, fn, dev, shapes, value, loc, attn, go, fwd_only, dist):
     del host_in, host_out
     return {"value": samples / (ms * 1e-3) / 1e9, "unit": "Gsamples/s", "ms_per_step": ms,
             "steps": iters, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+# ---------------------------------------------------------------- reference Triton arm
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def load_reference_triton():
+    """The unmodified reference package installed under baseline/_ref, or None."""
+    if not os.path.isdir(os.path.join(REF_DIR, "msda_triton")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import msda_triton
+
+    return msda_triton
+
+
+def run_reference_triton(args, wl, rank, world, local_rank):
+    """The reference's own Triton kernels on this GPU through its public API
+    (msda2d/msda3d with autograd), timed exactly like our arm: same inputs,
+    same step, CUDA events, max over ranks.  Informational comparison point."""
+    ref = load_reference_triton()
+    if ref is None:
+        return None if rank else {"impl": "reference-triton",
+                                  "unavailable": "reference not installed under baseline/_ref"}
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    fn = ref.msda3d if wl["ndim"] == 3 else ref.msda2d
+    value, shapes, loc, attn, go = make_inputs(wl, dev, seed=1234 + rank)
+    v, lo, a = (t.requires_grad_(True) for t in (value, loc, attn))
+    fwd_only = wl.get("fwd_only", False)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        out = fn(v, shapes, lo, a)
+        if not fwd_only:
+            torch.autograd.grad(out, (v, lo, a), go)
+
+    def fwd():
+        with torch.no_grad():
+            fn(v, shapes, lo, a)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / args.steps
+    fwd_ms = statistics.mean(time_events(fwd, max(3, min(args.steps, 10)) + 2, stream)[2:])
+    if dist is not None:
+        tt = torch.tensor([ms, fwd_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms, fwd_ms = (float(x) for x in tt.tolist())
+    e2e = run_e2e(args, wl, fn, dev, shapes, value, loc, attn, go, fwd_only, dist)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    B, K, H, C, Q, L, P = dims(wl)
+    samples = algorithmic_bytes(wl)["samples"] * world
+    return {
+        "impl": "reference-triton",
+        "metric": "MSDA fwd+bwd Gsamples/s" if not fwd_only else "MSDA fwd Gsamples/s",
+        "value": samples / (ms * 1e-3) / 1e9, "unit": "Gsamples/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "fwd_ms": fwd_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": DTYPE_NAME[wl["dtype"]], "data": "synthetic (same seeded inputs as our arm)",
+        "config": {"workload": args.workload, "batch_per_gpu": B, "global_batch": B * world,
+                   "num_queries": Q, "source": "unmodified reference from baseline/_ref "
+                   "(msda_triton " + getattr(ref, "__version__", "0.1.0") + ")"},
+        "e2e": e2e,
+    }
 
 
 # ---------------------------------------------------------------- CPU (oracle) arm
@@ -484,17 +576,23 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="3d_xl_bf16", choices=sorted(WORKLOADS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-triton"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="per-GPU batch override (a smaller case of the workload, for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.batch > 0:
+        wl["B"] = args.batch
     if args.impl == "reference":
         res = run_reference(args, wl, rank)
+    elif args.impl == "reference-triton":
+        res = run_reference_triton(args, wl, rank, world, local_rank)
     else:
         if args.no_cpu_baseline:
             globals()["cpu_baseline"] = lambda *a, **k: None
