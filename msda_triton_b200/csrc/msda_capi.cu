@@ -282,7 +282,8 @@ int prepare_bwd(const Args& a, const void* go, const void* gv_like, void* gl, vo
 // channels, one 16-byte fp32 vector reduction each): same lanes per row,
 // twice the chunks per lane.
 void bwd_gather_shape(const Args& a, Problem& p, LaunchShape& ls) {
-  if (dtype_bytes(a.vdt) == 2 && ls.vb == 16) {
+  // MSDA_BWD_CHUNK16 (tuning): keep the forward's 16-byte chunks.
+  if (dtype_bytes(a.vdt) == 2 && ls.vb == 16 && std::getenv("MSDA_BWD_CHUNK16") == nullptr) {
     ls.vb = 8;
     // Twice the lanes per row (up to a warp) rather than twice the chunks per
     // lane: each warp-wide reduction then covers whole 128-byte lines of the
@@ -360,12 +361,15 @@ void plan_gather_targets(const Args& a, const Problem& p, BwdPlan& pl) {
   if (dtype_bytes(a.vdt) != 2 || p.shapes_dev != nullptr || a.K == 0) return;
   const char* env = std::getenv("MSDA_BWD_DIRECT16");
   if (env && std::strcmp(env, "0") == 0) return;
+  // MSDA_BWD_DIRECT16_MAX (tuning): the contribution bound.
+  const char* mx = std::getenv("MSDA_BWD_DIRECT16_MAX");
+  const double bound = mx ? std::atof(mx) : kDirect16Contrib;
   int64_t keys = 0;
   for (int64_t l = 0; l < a.L; ++l) {
     const int64_t nvox = int64_t{p.lv.size[l][0]} * p.lv.size[l][1] * p.lv.size[l][2];
     const double contrib = static_cast<double>(int64_t{1} << a.ndim) * a.Q * a.P /
                            static_cast<double>(std::max<int64_t>(nvox, 1));
-    if (contrib <= kDirect16Contrib) {
+    if (contrib <= bound) {
       pl.direct16 |= 1 << l;
     } else {
       pl.acc_start[l] = static_cast<int32_t>(keys);
