@@ -10,10 +10,9 @@ from __future__ import annotations
 
 import torch
 
-from msda_triton_b200 import _core
+from msda_triton_b200 import _core, ops
 
 
-@torch.compiler.disable
 def msda3d_fwd(
     value: torch.Tensor,
     value_spatial_shapes: torch.Tensor,
@@ -45,6 +44,10 @@ def msda3d_fwd(
 
     Reference: triton/msda_3d.py:797-861.
     """
+    if torch.compiler.is_compiling():
+        with torch.no_grad():
+            return ops.msda_forward(value, value_spatial_shapes, sampling_locations,
+                                    attention_weights, 3, clamp_grid, clamp_eps)
     return _core.fwd_entry(3, value, value_spatial_shapes, sampling_locations,
                            attention_weights, clamp_grid, clamp_eps)
 
@@ -82,6 +85,10 @@ def msda3d(
     """
     if not value.is_cuda:
         raise ValueError("MSDA3D CUDA kernel requires CUDA tensors. Got CPU tensors instead.")
+    if torch.compiler.is_compiling():
+        # traced as one opaque op (msda_b200::msda_forward) instead of a graph break
+        return ops.msda_forward(value, value_spatial_shapes, sampling_locations,
+                                attention_weights, 3, clamp_grid, clamp_eps)
     return MSDA3DFn.apply(value, value_spatial_shapes, sampling_locations, attention_weights,
                           clamp_grid, clamp_eps)
 
