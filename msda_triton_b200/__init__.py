@@ -5,6 +5,7 @@ Drop-in replacement for the public API of mach9robotics/msda-triton
 
     from msda_triton_b200 import msda2d, msda2d_fwd, msda3d, msda3d_fwd
     from msda_triton_b200 import MSDA2DFn, MSDA3DFn
+    from msda_triton_b200 import MSDA2D, MSDA3D   # the nn.Modules (msda_triton.pytorch)
 
 The ops run in hand-written CUDA kernels (libmsda_b200.so, C ABI in
 include/msda_b200.h).  There is no CPU fallback: CPU tensors raise
@@ -17,6 +18,7 @@ __version__ = "0.1.0"
 
 from msda_triton_b200.msda_2d import MSDA2DFn, msda2d, msda2d_fwd
 from msda_triton_b200.msda_3d import MSDA3DFn, msda3d, msda3d_fwd
+from msda_triton_b200.modules import MSDA2D, MSDA3D
 
 __all__ = [
     "__version__",
@@ -26,4 +28,6 @@ __all__ = [
     "msda3d",
     "msda3d_fwd",
     "MSDA3DFn",
+    "MSDA2D",
+    "MSDA3D",
 ]
