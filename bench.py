@@ -50,6 +50,14 @@ WORKLOADS = {
     # BASELINE configs[2] (inference: forward only).
     "2d_dec_bf16": dict(ndim=2, B=8, Q=900, H=8, C=32, P=4, dtype=torch.bfloat16, shapes=SHAPES_2D,
                         fwd_only=True),
+    # The MSDA3D / MSDA2D nn.Modules (projections + sampling + output
+    # projection, init_weights() state, reference points U[0,1)) on the
+    # shapes of configs 4 and 1; informational, not the headline.
+    "module3d_xl_bf16": dict(ndim=3, B=8, Q=100000, H=8, C=32, P=4, dtype=torch.bfloat16,
+                             shapes=[(64, 128, 128), (32, 64, 64), (16, 32, 32), (8, 16, 16)],
+                             module=True),
+    "module2d_enc_bf16": dict(ndim=2, B=4, Q=19947, H=8, C=32, P=4, dtype=torch.bfloat16,
+                              shapes=SHAPES_2D, module=True),
 }
 DTYPE_NAME = {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}
 L2_BYTES = 126 * 1000 * 1000
@@ -519,6 +527,69 @@ def run_reference_triton(args, wl, rank, world, local_rank):
     }
 
 
+# ---------------------------------------------------------------- module workloads
+def run_module(args, wl, rank, world, local_rank):
+    """One fwd+bwd step of the nn.Module (ours, or the reference's own module
+    from baseline/_ref with --impl reference-triton) on one GPU: same seeded
+    parameters (init_weights) and inputs for both; CUDA events."""
+    if world > 1:
+        raise SystemExit("module workloads run on one GPU")
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if args.impl == "reference":
+        return {"impl": "reference", "unavailable": "module workloads have no CPU arm"}
+    if args.impl == "reference-triton":
+        ref = load_reference_triton()
+        if ref is None:
+            return {"impl": "reference-module", "unavailable": "reference not installed under baseline/_ref"}
+        from msda_triton.pytorch import MSDA2D, MSDA3D
+        impl = "reference-module (grid_sample)"
+    else:
+        from msda_triton_b200.modules import MSDA2D, MSDA3D
+        impl = "ours"
+    B, K, H, C, Q, L, P = dims(wl)
+    d, dt, E = wl["ndim"], wl["dtype"], H * C
+    torch.manual_seed(0)
+    m = (MSDA3D if d == 3 else MSDA2D)(embed_dims=E, num_heads=H, num_levels=L, num_points=P,
+                                       dropout=0.0, batch_first=True)
+    m.init_weights()
+    m = m.to(dev, dt)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    query = torch.randn(B, Q, E, generator=g, device=dev).to(dt).requires_grad_(True)
+    value = torch.randn(B, K, E, generator=g, device=dev).to(dt).requires_grad_(True)
+    refp = torch.rand(B, Q, L, d, generator=g, device=dev).to(dt).requires_grad_(True)
+    gout = torch.randn(B, Q, E, generator=g, device=dev).to(dt)
+    shapes = torch.tensor(wl["shapes"], dtype=torch.int64, device=dev)
+    wrt = [query, value, refp] + list(m.parameters())
+
+    def step():
+        out = m(query, value=value, reference_points=refp, spatial_shapes=shapes)
+        torch.autograd.grad(out, wrt, gout)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    with ClockSampler([local_rank]) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / args.steps
+    samples = algorithmic_bytes(wl)["samples"]
+    return {"impl": impl, "metric": "MSDA module fwd+bwd Gsamples/s",
+            "value": samples / (ms * 1e-3) / 1e9, "unit": "Gsamples/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": DTYPE_NAME[dt], "data": "synthetic (seeded; init_weights parameters)",
+            "config": {"workload": args.workload, "embed_dims": E, "batch": B, "num_queries": Q,
+                       "num_keys": K, "num_heads": H, "num_levels": L, "num_points": P},
+            "clocks": clk.summary()}
+
+
 # ---------------------------------------------------------------- CPU (oracle) arm
 def _cpu_sample(wl, target_s):
     """A bounded sample of the workload for the CPU: batch 1, and a query count
@@ -615,7 +686,9 @@ def main():
     wl = dict(WORKLOADS[args.workload])
     if args.batch > 0:
         wl["B"] = args.batch
-    if args.impl == "reference":
+    if wl.get("module"):
+        res = run_module(args, wl, rank, world, local_rank) if rank == 0 else None
+    elif args.impl == "reference":
         res = run_reference(args, wl, rank)
     elif args.impl == "reference-triton":
         res = run_reference_triton(args, wl, rank, world, local_rank)
