@@ -109,7 +109,11 @@ class _MSDAModule(nn.Module):
         num_value = value_in.shape[1]
         assert spatial_shapes is not None, "spatial_shapes is required"
         assert reference_points is not None, "reference_points is required"
-        total = spatial_shapes[:, :d].prod(-1).sum()
+        # The size check below needs the shapes on the host (the reference
+        # syncs here too); the kernels then get the host copy, which lets the
+        # backward plan its per-level value-gradient targets.
+        shapes_host = spatial_shapes.cpu() if spatial_shapes.is_cuda else spatial_shapes
+        total = shapes_host[:, :d].prod(-1).sum()
         assert total == num_value, (
             f"Spatial shapes product {total} doesn't match value size {num_value}")
 
@@ -136,12 +140,12 @@ class _MSDAModule(nn.Module):
             weights = weights.softmax(-1).view(bs, q1 - q0, H, L, P)
             loc = reference_points[:, q0:q1, None, :, None, :] + offsets / normalizer
             if hc == H:
-                chunks.append(self._run(v, spatial_shapes, loc, weights))
+                chunks.append(self._run(v, shapes_host, loc, weights))
                 continue
             out = q.new_zeros(bs, q1 - q0, self.embed_dims)
             for h0 in range(0, H, hc):
                 h1 = min(h0 + hc, H)
-                out[:, :, h0 * c:h1 * c] = self._run(v[:, :, h0:h1], spatial_shapes,
+                out[:, :, h0 * c:h1 * c] = self._run(v[:, :, h0:h1], shapes_host,
                                                      loc[:, :, h0:h1], weights[:, :, h0:h1])
             chunks.append(out)
         out = chunks[0] if len(chunks) == 1 else torch.cat(chunks, dim=1)
