@@ -63,7 +63,7 @@ extern "C" {
 #define MSDA_API
 #endif
 
-#define MSDA_B200_ABI_VERSION 2
+#define MSDA_B200_ABI_VERSION 3
 #define MSDA_MAX_LEVELS 16
 
 typedef enum msda_dtype {
@@ -155,12 +155,15 @@ MSDA_API int msda_cast_from_f32(const float* src, void* dst, int dst_dtype, int6
 
 /* Workspace bytes msda{2,3}d_bwd needs for this problem (it depends on the
  * level shapes, which must be the same pointer/residency as in the call).
- * Large problems with host-resident shapes use the binned backward (sample
- * bins + a small fp32 accumulator for coarse levels); others the
- * gather/scatter backward (B*K*H*C*4 bytes of fp32 accumulator for fp16/bf16
- * values, 0 for fp32).  The plan assumes value, grad_output and grad_value
- * are 16-byte aligned.  The reference allocates its gradient buffers with
- * torch.zeros_like (triton/msda_3d.py:941-944); here the caller allocates.
+ * fp32 values need none.  For fp16/bf16 values the gather/scatter backward
+ * reduces levels with at most 8 expected contributions per element
+ * (2^d*Q*P / voxels) straight into grad_value and accumulates the others in
+ * an fp32 buffer of B * (their keys) * H * C * 4 bytes; with device-resident
+ * shapes the host cannot plan levels and the buffer covers all K keys.  (The
+ * opt-in binned backward, MSDA_BWD_PATH=binned, needs sample bins instead.)
+ * The plan assumes value, grad_output and grad_value are 16-byte aligned.
+ * The reference allocates its gradient buffers with torch.zeros_like
+ * (triton/msda_3d.py:941-944); here the caller allocates.
  * Returns 0 when no workspace is needed or the arguments are invalid. */
 MSDA_API size_t msda_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batch,
                                          int64_t num_keys, int64_t num_heads, int64_t channels,
@@ -187,6 +190,63 @@ MSDA_API int msda_bwd_static_scratch(int ndim, const void* value, int value_dtyp
                int sampling_dtype, int64_t num_queries, int64_t num_points, int clamp_grid,
                double clamp_eps, const void* grad_output, void* grad_value,
                void* grad_sampling_locations, void* grad_attention_weights, void* stream);
+
+/* Fused prologue: MSDA from the raw outputs of a deformable-attention
+ * layer's two query projections instead of finished locations and weights
+ * (the MSDA2D / MSDA3D modules, src/msda_triton/pytorch/msda_2d.py:325-339,
+ * src/msda_triton/pytorch/msda_3d.py:325-350, compute them as separate
+ * tensors first):
+ *   reference_points  (B, Q, L, d) fp32, normalised
+ *   sampling_offsets  (B, Q, H, L, P, d) sampling_dtype, in cells of the level
+ *   attention_logits  (B, Q, H, L*P)     sampling_dtype
+ * location = reference_points[b,q,l] + sampling_offsets[b,q,h,l,p] / (W, H[, D])_l
+ * weight   = softmax over the L*P logits of row (b, q, h)
+ * and then exactly msda{2,3}d_fwd.  The backward writes grad_value,
+ * grad_sampling_offsets and grad_attention_logits (in the dtypes of their
+ * inputs) and grad_reference_partial, fp32 (B, Q, H, L, d): the sum over the
+ * row's points of the location gradient; the reference-point gradient is its
+ * sum over H (one small reduction by the caller).  Workspace: see
+ * msda_fused_bwd_workspace_bytes. */
+MSDA_API int msda2d_fused_fwd(const void* value, int value_dtype, int64_t batch,
+               int64_t num_keys, int64_t num_heads, int64_t channels,
+               const int32_t* spatial_shapes, int spatial_shapes_on_device, int64_t num_levels,
+               const float* reference_points, const void* sampling_offsets,
+               const void* attention_logits, int sampling_dtype, int64_t num_queries,
+               int64_t num_points, int clamp_grid, double clamp_eps, void* output, void* stream);
+
+MSDA_API int msda3d_fused_fwd(const void* value, int value_dtype, int64_t batch,
+               int64_t num_keys, int64_t num_heads, int64_t channels,
+               const int32_t* spatial_shapes, int spatial_shapes_on_device, int64_t num_levels,
+               const float* reference_points, const void* sampling_offsets,
+               const void* attention_logits, int sampling_dtype, int64_t num_queries,
+               int64_t num_points, int clamp_grid, double clamp_eps, void* output, void* stream);
+
+MSDA_API int msda2d_fused_bwd(const void* value, int value_dtype, int64_t batch,
+               int64_t num_keys, int64_t num_heads, int64_t channels,
+               const int32_t* spatial_shapes, int spatial_shapes_on_device, int64_t num_levels,
+               const float* reference_points, const void* sampling_offsets,
+               const void* attention_logits, int sampling_dtype, int64_t num_queries,
+               int64_t num_points, int clamp_grid, double clamp_eps, const void* grad_output,
+               void* grad_value, float* grad_reference_partial, void* grad_sampling_offsets,
+               void* grad_attention_logits, void* workspace, size_t workspace_bytes,
+               void* stream);
+
+MSDA_API int msda3d_fused_bwd(const void* value, int value_dtype, int64_t batch,
+               int64_t num_keys, int64_t num_heads, int64_t channels,
+               const int32_t* spatial_shapes, int spatial_shapes_on_device, int64_t num_levels,
+               const float* reference_points, const void* sampling_offsets,
+               const void* attention_logits, int sampling_dtype, int64_t num_queries,
+               int64_t num_points, int clamp_grid, double clamp_eps, const void* grad_output,
+               void* grad_value, float* grad_reference_partial, void* grad_sampling_offsets,
+               void* grad_attention_logits, void* workspace, size_t workspace_bytes,
+               void* stream);
+
+/* Workspace bytes of msda{2,3}d_fused_bwd (always the gather/scatter plan). */
+MSDA_API size_t msda_fused_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batch,
+                                               int64_t num_keys, int64_t num_heads,
+                                               int64_t channels, const int32_t* spatial_shapes,
+                                               int spatial_shapes_on_device, int64_t num_levels,
+                                               int64_t num_queries, int64_t num_points);
 
 /* Name of a status code ("MSDA_SUCCESS", ...). */
 MSDA_API const char* msda_status_string(int status);

@@ -31,7 +31,7 @@ FLOAT16 = 1
 BFLOAT16 = 2
 
 MAX_LEVELS = 16
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 EXPORTED_SYMBOLS = (
     "msda2d_fwd",
@@ -43,6 +43,11 @@ EXPORTED_SYMBOLS = (
     "msda_cast_from_f32",
     "msda_bwd_static_scratch",
     "msda_bwd_workspace_bytes",
+    "msda2d_fused_fwd",
+    "msda3d_fused_fwd",
+    "msda2d_fused_bwd",
+    "msda3d_fused_bwd",
+    "msda_fused_bwd_workspace_bytes",
     "msda_status_string",
     "msda_last_error",
     "msda_abi_version",
@@ -64,6 +69,19 @@ _FWD_ARGS = [
 ]
 _BWD_ARGS = _FWD_ARGS[:-2] + [
     _vp, _vp, _vp, _vp,                 # grad_output, grad_value, grad_loc, grad_attn
+    _vp, ctypes.c_size_t, _vp,          # workspace, workspace_bytes, stream
+]
+
+_FUSED_FWD_ARGS = [
+    _vp, _int, _i64, _i64, _i64, _i64,  # value, value_dtype, B, K, H, C
+    _vp, _int, _i64,                    # spatial_shapes, on_device, L
+    _vp, _vp, _vp, _int, _i64, _i64,    # reference_points (fp32), offsets, logits, sampling_dtype, Q, P
+    _int, ctypes.c_double,              # clamp_grid, clamp_eps
+    _vp, _vp,                           # output, stream
+]
+_FUSED_BWD_ARGS = _FUSED_FWD_ARGS[:-2] + [
+    _vp, _vp, _vp, _vp, _vp,            # grad_output, grad_value, grad_reference_partial (fp32),
+                                        # grad_sampling_offsets, grad_attention_logits
     _vp, ctypes.c_size_t, _vp,          # workspace, workspace_bytes, stream
 ]
 
@@ -104,6 +122,14 @@ def lib() -> ctypes.CDLL:
             handle.msda_cast_from_f32.restype = _int
             handle.msda_bwd_workspace_bytes.argtypes = [_int, _int, _i64, _i64, _i64, _i64, _vp, _int, _i64, _i64, _i64]
             handle.msda_bwd_workspace_bytes.restype = ctypes.c_size_t
+            handle.msda_fused_bwd_workspace_bytes.argtypes = handle.msda_bwd_workspace_bytes.argtypes
+            handle.msda_fused_bwd_workspace_bytes.restype = ctypes.c_size_t
+            for name in ("msda2d_fused_fwd", "msda3d_fused_fwd"):
+                getattr(handle, name).argtypes = _FUSED_FWD_ARGS
+                getattr(handle, name).restype = _int
+            for name in ("msda2d_fused_bwd", "msda3d_fused_bwd"):
+                getattr(handle, name).argtypes = _FUSED_BWD_ARGS
+                getattr(handle, name).restype = _int
             handle.msda_status_string.argtypes = [_int]
             handle.msda_status_string.restype = ctypes.c_char_p
             handle.msda_last_error.argtypes = []

@@ -76,6 +76,10 @@ struct Args {
   int64_t Q, P;
   int clamp;
   double eps;
+  // fused prologue: loc / attn are the raw offsets / logits, ref the fp32
+  // reference points (B, Q, L, d)
+  const float* ref = nullptr;
+  int fused = 0;
 };
 
 // Validate arguments, fill the Problem (except the launch shape) and pick
@@ -217,31 +221,55 @@ int cuda_fail(cudaError_t err, const char* what) {
   return fail(MSDA_ERROR_CUDA, "%s: %s", what, cudaGetErrorString(err));
 }
 
-cudaError_t dispatch_fwd(int vdt, int sdt, const LaunchShape& ls, const Problem& p, void* out,
-                         cudaStream_t st) {
+template <bool F>
+cudaError_t dispatch_fwd_mode(int vdt, int sdt, const LaunchShape& ls, const Problem& p,
+                              void* out, cudaStream_t st) {
   switch (vdt) {
-    case MSDA_FLOAT32: return launch_fwd<float, float>(ls, p, out, st);
+    case MSDA_FLOAT32: return launch_fwd<float, float, F>(ls, p, out, st);
     case MSDA_FLOAT16:
-      return sdt == MSDA_FLOAT32 ? launch_fwd<__half, float>(ls, p, out, st)
-                                 : launch_fwd<__half, __half>(ls, p, out, st);
+      return sdt == MSDA_FLOAT32 ? launch_fwd<__half, float, F>(ls, p, out, st)
+                                 : launch_fwd<__half, __half, F>(ls, p, out, st);
     default:
-      return sdt == MSDA_FLOAT32 ? launch_fwd<__nv_bfloat16, float>(ls, p, out, st)
-                                 : launch_fwd<__nv_bfloat16, __nv_bfloat16>(ls, p, out, st);
+      return sdt == MSDA_FLOAT32 ? launch_fwd<__nv_bfloat16, float, F>(ls, p, out, st)
+                                 : launch_fwd<__nv_bfloat16, __nv_bfloat16, F>(ls, p, out, st);
   }
 }
 
-cudaError_t dispatch_bwd(int vdt, int sdt, const LaunchShape& ls, const Problem& p,
-                         const void* go, float* gacc, void* gl, void* ga, cudaStream_t st) {
+cudaError_t dispatch_fwd(const Args& a, const LaunchShape& ls, const Problem& p, void* out,
+                         cudaStream_t st) {
+  return a.fused ? dispatch_fwd_mode<true>(a.vdt, a.sdt, ls, p, out, st)
+                 : dispatch_fwd_mode<false>(a.vdt, a.sdt, ls, p, out, st);
+}
+
+template <bool F>
+cudaError_t dispatch_bwd_mode(int vdt, int sdt, const LaunchShape& ls, const Problem& p,
+                              const void* go, float* gacc, void* gl, void* ga, cudaStream_t st) {
   switch (vdt) {
-    case MSDA_FLOAT32: return launch_bwd<float, float>(ls, p, go, gacc, gl, ga, st);
+    case MSDA_FLOAT32: return launch_bwd<float, float, F>(ls, p, go, gacc, gl, ga, st);
     case MSDA_FLOAT16:
-      return sdt == MSDA_FLOAT32 ? launch_bwd<__half, float>(ls, p, go, gacc, gl, ga, st)
-                                 : launch_bwd<__half, __half>(ls, p, go, gacc, gl, ga, st);
+      return sdt == MSDA_FLOAT32 ? launch_bwd<__half, float, F>(ls, p, go, gacc, gl, ga, st)
+                                 : launch_bwd<__half, __half, F>(ls, p, go, gacc, gl, ga, st);
     default:
-      return sdt == MSDA_FLOAT32 ? launch_bwd<__nv_bfloat16, float>(ls, p, go, gacc, gl, ga, st)
-                                 : launch_bwd<__nv_bfloat16, __nv_bfloat16>(ls, p, go, gacc, gl,
-                                                                            ga, st);
+      return sdt == MSDA_FLOAT32
+                 ? launch_bwd<__nv_bfloat16, float, F>(ls, p, go, gacc, gl, ga, st)
+                 : launch_bwd<__nv_bfloat16, __nv_bfloat16, F>(ls, p, go, gacc, gl, ga, st);
   }
+}
+
+cudaError_t dispatch_bwd(const Args& a, const LaunchShape& ls, const Problem& p, const void* go,
+                         float* gacc, void* gl, void* ga, cudaStream_t st) {
+  return a.fused ? dispatch_bwd_mode<true>(a.vdt, a.sdt, ls, p, go, gacc, gl, ga, st)
+                 : dispatch_bwd_mode<false>(a.vdt, a.sdt, ls, p, go, gacc, gl, ga, st);
+}
+
+// Fused prologue: the reference points are read by every row.
+int check_fused(const Args& a) {
+  if (!a.fused) return MSDA_SUCCESS;
+  if (a.B * a.Q * a.H * a.L * a.P > 0 && a.ref == nullptr)
+    return fail(MSDA_ERROR_INVALID_ARGUMENT, "reference_points pointer is NULL");
+  if (!aligned(a.ref, 4))
+    return fail(MSDA_ERROR_MISALIGNED, "reference_points must be 4-byte aligned (fp32)");
+  return MSDA_SUCCESS;
 }
 
 int run_fwd(const Args& a, void* out, void* stream) {
@@ -251,9 +279,11 @@ int run_fwd(const Args& a, void* out, void* stream) {
   Problem p;
   LaunchShape ls;
   int rc = prepare(a, bufs, 1, p, ls);
+  if (rc == MSDA_SUCCESS) rc = check_fused(a);
   if (rc != MSDA_SUCCESS) return rc;
   if (a.B * a.Q * a.H * a.C == 0) return ok();
-  const cudaError_t err = dispatch_fwd(a.vdt, a.sdt, ls, p, out, static_cast<cudaStream_t>(stream));
+  p.ref = a.ref;
+  const cudaError_t err = dispatch_fwd(a, ls, p, out, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "forward launch");
   return ok();
 }
@@ -310,9 +340,12 @@ int launch_accumulate(const Args& a, const Problem& p, const LaunchShape& ls, co
     const int64_t se = dtype_bytes(a.sdt);
     err = cudaMemsetAsync(gl, 0, static_cast<size_t>(nsmp * a.ndim * se), st);
     if (err == cudaSuccess) err = cudaMemsetAsync(ga, 0, static_cast<size_t>(nsmp * se), st);
+    if (err == cudaSuccess && a.fused)
+      err = cudaMemsetAsync(p.ref_partial, 0,
+                            static_cast<size_t>(a.B * a.Q * a.H * a.L * a.ndim) * sizeof(float), st);
     return err == cudaSuccess ? MSDA_SUCCESS : cuda_fail(err, "zeroing gradients");
   }
-  err = dispatch_bwd(a.vdt, a.sdt, ls, p, go, gacc, gl, ga, st);
+  err = dispatch_bwd(a, ls, p, go, gacc, gl, ga, st);
   return err == cudaSuccess ? MSDA_SUCCESS : cuda_fail(err, "backward launch");
 }
 
@@ -423,7 +456,7 @@ void plan_bwd(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan& p
   const char* env = std::getenv("MSDA_BWD_PATH");
   // The binned path is opt-in (MSDA_BWD_PATH=binned) until it outruns the
   // gather/scatter kernel on the benchmark shapes.
-  const bool force_binned = env && std::strcmp(env, "binned") == 0;
+  const bool force_binned = env && std::strcmp(env, "binned") == 0 && !a.fused;
   const bool force_gather = !force_binned;
   bool ok_binned = !force_gather && p.shapes_dev == nullptr && ls.vb == 16 && ls.vpl == 1 &&
                    samples > 0 && a.C > 0 && (force_binned || samples >= kBinnedMinSamples) &&
@@ -521,12 +554,21 @@ cudaError_t dispatch_bwd_binned(int vdt, int sdt, const BinLaunch& bl, const Pro
 }
 
 int run_bwd(const Args& a, const void* go, void* gv, void* gl, void* ga, void* ws,
-            size_t ws_bytes, void* stream) {
+            size_t ws_bytes, void* stream, float* ref_partial = nullptr) {
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   Problem p;
   LaunchShape ls;
   int rc = prepare_bwd(a, go, gv, gl, ga, p, ls);
+  if (rc == MSDA_SUCCESS) rc = check_fused(a);
   if (rc != MSDA_SUCCESS) return rc;
+  if (a.fused) {
+    if (a.B * a.Q * a.H * a.L * a.P > 0 && ref_partial == nullptr)
+      return fail(MSDA_ERROR_INVALID_ARGUMENT, "grad_reference_partial pointer is NULL");
+    if (!aligned(ref_partial, 4))
+      return fail(MSDA_ERROR_MISALIGNED, "grad_reference_partial must be 4-byte aligned");
+    p.ref = a.ref;
+    p.ref_partial = ref_partial;
+  }
   BwdPlan pl;
   plan_bwd(a, p, ls, pl);
   const int64_t nval = a.B * a.K * a.H * a.C;
@@ -696,6 +738,62 @@ int msda3d_bwd_accumulate(const void* value, int value_dtype, int64_t batch, int
                                   grad_attention_weights, stream);
 }
 
+#define MSDA_FUSED_ARGS(ND)                                                                \
+  Args a{ND,          value,           value_dtype,     batch,        num_keys,               \
+         num_heads,   channels,        spatial_shapes,  spatial_shapes_on_device, num_levels, \
+         sampling_offsets, attention_logits, sampling_dtype, num_queries, num_points,          \
+         clamp_grid,  clamp_eps,       reference_points, 1}
+
+int msda2d_fused_fwd(const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+                     int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+                     int spatial_shapes_on_device, int64_t num_levels,
+                     const float* reference_points, const void* sampling_offsets,
+                     const void* attention_logits, int sampling_dtype, int64_t num_queries,
+                     int64_t num_points, int clamp_grid, double clamp_eps, void* output,
+                     void* stream) {
+  MSDA_FUSED_ARGS(2);
+  return msda::run_fwd(a, output, stream);
+}
+
+int msda3d_fused_fwd(const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+                     int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+                     int spatial_shapes_on_device, int64_t num_levels,
+                     const float* reference_points, const void* sampling_offsets,
+                     const void* attention_logits, int sampling_dtype, int64_t num_queries,
+                     int64_t num_points, int clamp_grid, double clamp_eps, void* output,
+                     void* stream) {
+  MSDA_FUSED_ARGS(3);
+  return msda::run_fwd(a, output, stream);
+}
+
+int msda2d_fused_bwd(const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+                     int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+                     int spatial_shapes_on_device, int64_t num_levels,
+                     const float* reference_points, const void* sampling_offsets,
+                     const void* attention_logits, int sampling_dtype, int64_t num_queries,
+                     int64_t num_points, int clamp_grid, double clamp_eps,
+                     const void* grad_output, void* grad_value, float* grad_reference_partial,
+                     void* grad_sampling_offsets, void* grad_attention_logits, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  MSDA_FUSED_ARGS(2);
+  return msda::run_bwd(a, grad_output, grad_value, grad_sampling_offsets, grad_attention_logits,
+                       workspace, workspace_bytes, stream, grad_reference_partial);
+}
+
+int msda3d_fused_bwd(const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+                     int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+                     int spatial_shapes_on_device, int64_t num_levels,
+                     const float* reference_points, const void* sampling_offsets,
+                     const void* attention_logits, int sampling_dtype, int64_t num_queries,
+                     int64_t num_points, int clamp_grid, double clamp_eps,
+                     const void* grad_output, void* grad_value, float* grad_reference_partial,
+                     void* grad_sampling_offsets, void* grad_attention_logits, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  MSDA_FUSED_ARGS(3);
+  return msda::run_bwd(a, grad_output, grad_value, grad_sampling_offsets, grad_attention_logits,
+                       workspace, workspace_bytes, stream, grad_reference_partial);
+}
+
 int msda_cast_from_f32(const float* src, void* dst, int dst_dtype, int64_t count, void* stream) {
   if (count < 0 || msda::dtype_bytes(dst_dtype) == 0)
     return msda::fail(MSDA_ERROR_INVALID_ARGUMENT, "bad count or dtype");
@@ -709,15 +807,15 @@ int msda_cast_from_f32(const float* src, void* dst, int dst_dtype, int64_t count
   return err == cudaSuccess ? msda::ok() : msda::cuda_fail(err, "cast launch");
 }
 
-size_t msda_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batch, int64_t num_keys,
-                                int64_t num_heads, int64_t channels,
-                                const int32_t* spatial_shapes, int spatial_shapes_on_device,
-                                int64_t num_levels, int64_t num_queries, int64_t num_points) {
+static size_t workspace_bytes(int ndim, int value_dtype, int64_t batch, int64_t num_keys,
+                              int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+                              int spatial_shapes_on_device, int64_t num_levels,
+                              int64_t num_queries, int64_t num_points, int fused) {
   // Plan with 256-byte aligned stand-in pointers (never dereferenced).
   void* fake = reinterpret_cast<void*>(uintptr_t{256});
   Args a{ndim, fake, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,
          spatial_shapes_on_device, num_levels, fake, fake, value_dtype, num_queries, num_points,
-         1, 1e-4};
+         1, 1e-4, static_cast<const float*>(fake), fused};
   msda::Problem p;
   msda::LaunchShape ls;
   const void* bufs[2] = {fake, fake};
@@ -725,6 +823,23 @@ size_t msda_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batch, int64_
   msda::BwdPlan pl;
   msda::plan_bwd(a, p, ls, pl);
   return pl.ws_bytes;
+}
+
+size_t msda_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batch, int64_t num_keys,
+                                int64_t num_heads, int64_t channels,
+                                const int32_t* spatial_shapes, int spatial_shapes_on_device,
+                                int64_t num_levels, int64_t num_queries, int64_t num_points) {
+  return workspace_bytes(ndim, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,
+                         spatial_shapes_on_device, num_levels, num_queries, num_points, 0);
+}
+
+size_t msda_fused_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batch, int64_t num_keys,
+                                      int64_t num_heads, int64_t channels,
+                                      const int32_t* spatial_shapes, int spatial_shapes_on_device,
+                                      int64_t num_levels, int64_t num_queries,
+                                      int64_t num_points) {
+  return workspace_bytes(ndim, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,
+                         spatial_shapes_on_device, num_levels, num_queries, num_points, 1);
 }
 
 const char* msda_status_string(int status) {

@@ -54,6 +54,14 @@ struct Problem {
   int64_t acc_keys;
   int32_t acc_start[kMaxLevels];
   void* grad_value16;
+  // Fused prologue (kernels instantiated with FUSED): `loc` holds the raw
+  // sampling offsets and `attn` the raw weight logits (same shapes); the
+  // location is ref + offset / size per axis and the weight is the softmax
+  // of the row's L*P logits.  ref: fp32 reference points (B, Q, L, d).
+  // ref_partial (backward output): fp32 (B, Q, H, L, d), the sum over the
+  // row's points of each level's location gradient.
+  const float* ref;
+  float* ref_partial;
 };
 
 // ---------------------------------------------------------------- types

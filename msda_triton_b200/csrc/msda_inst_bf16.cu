@@ -3,6 +3,6 @@
 #include "msda_launch.cuh"
 
 namespace msda {
-MSDA_INSTANTIATE_PAIR(__nv_bfloat16, __nv_bfloat16)
+MSDA_INSTANTIATE_MODE(__nv_bfloat16, __nv_bfloat16, false)
 MSDA_INSTANTIATE_BINNED(__nv_bfloat16, __nv_bfloat16)
 }  // namespace msda

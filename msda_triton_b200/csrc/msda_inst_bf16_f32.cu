@@ -3,6 +3,6 @@
 #include "msda_launch.cuh"
 
 namespace msda {
-MSDA_INSTANTIATE_PAIR(__nv_bfloat16, float)
+MSDA_INSTANTIATE_MODE(__nv_bfloat16, float, false)
 MSDA_INSTANTIATE_BINNED(__nv_bfloat16, float)
 }  // namespace msda

@@ -3,6 +3,6 @@
 #include "msda_launch.cuh"
 
 namespace msda {
-MSDA_INSTANTIATE_PAIR(__half, __half)
+MSDA_INSTANTIATE_MODE(__half, __half, false)
 MSDA_INSTANTIATE_BINNED(__half, __half)
 }  // namespace msda

@@ -3,6 +3,6 @@
 #include "msda_launch.cuh"
 
 namespace msda {
-MSDA_INSTANTIATE_PAIR(__half, float)
+MSDA_INSTANTIATE_MODE(__half, float, false)
 MSDA_INSTANTIATE_BINNED(__half, float)
 }  // namespace msda

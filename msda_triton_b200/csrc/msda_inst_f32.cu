@@ -3,6 +3,6 @@
 #include "msda_launch.cuh"
 
 namespace msda {
-MSDA_INSTANTIATE_PAIR(float, float)
+MSDA_INSTANTIATE_MODE(float, float, false)
 MSDA_INSTANTIATE_BINNED(float, float)
 }  // namespace msda

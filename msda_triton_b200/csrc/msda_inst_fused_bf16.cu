@@ -1,0 +1,6 @@
+// Fused-prologue kernel instantiations for value dtype __nv_bfloat16, sampling dtype __nv_bfloat16.
+#include "msda_launch.cuh"
+
+namespace msda {
+MSDA_INSTANTIATE_MODE(__nv_bfloat16, __nv_bfloat16, true)
+}  // namespace msda

@@ -1,0 +1,6 @@
+// Fused-prologue kernel instantiations for value dtype __nv_bfloat16, sampling dtype float.
+#include "msda_launch.cuh"
+
+namespace msda {
+MSDA_INSTANTIATE_MODE(__nv_bfloat16, float, true)
+}  // namespace msda

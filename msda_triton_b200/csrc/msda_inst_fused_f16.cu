@@ -1,0 +1,6 @@
+// Fused-prologue kernel instantiations for value dtype __half, sampling dtype __half.
+#include "msda_launch.cuh"
+
+namespace msda {
+MSDA_INSTANTIATE_MODE(__half, __half, true)
+}  // namespace msda

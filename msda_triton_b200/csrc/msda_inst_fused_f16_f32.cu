@@ -1,0 +1,6 @@
+// Fused-prologue kernel instantiations for value dtype __half, sampling dtype float.
+#include "msda_launch.cuh"
+
+namespace msda {
+MSDA_INSTANTIATE_MODE(__half, float, true)
+}  // namespace msda

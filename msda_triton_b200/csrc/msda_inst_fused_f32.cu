@@ -1,0 +1,6 @@
+// Fused-prologue kernel instantiations for value dtype float, sampling dtype float.
+#include "msda_launch.cuh"
+
+namespace msda {
+MSDA_INSTANTIATE_MODE(float, float, true)
+}  // namespace msda

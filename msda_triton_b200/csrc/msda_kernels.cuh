@@ -84,6 +84,49 @@ __device__ __forceinline__ Point<NDIM> load_point(const TS* lp, const int32_t* s
   return pt;
 }
 
+// Fused prologue: the location of one sample from its raw offset and the
+// level's reference point, ref + offset / size per axis (size = W, H, D for
+// x, y, z), with the rounding of the separate `ref + offsets / normalizer`
+// expression (pytorch/msda_3d.py:336-339, pytorch/msda_2d.py:335-339).
+template <typename TS, int NDIM>
+__device__ __forceinline__ Point<NDIM> load_point_fused(const TS* off, const float* ref,
+                                                        const int32_t* sz, const Problem& p) {
+  Point<NDIM> pt;
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+    pt.i0[a] = 0;
+    pt.f[a] = 0.0f;
+    pt.pass[a] = true;
+  }
+#pragma unroll
+  for (int a = 0; a < NDIM; ++a) {
+    const float x =
+        __fadd_rn(ref[a], __fdiv_rn(Elem<TS>::to_f(off[a]), static_cast<float>(sz[a])));
+    resolve_axis(x, sz[a], p.clamp, p.lo, p.hi, pt.i0[a], pt.f[a], pt.pass[a]);
+  }
+  return pt;
+}
+
+// Softmax of one row's L*P weight logits: max and sum of exp(x - max); the
+// weight of a sample is exp(x - max) / sum.
+struct RowSoftmax {
+  float mx;
+  float sum;
+};
+
+template <typename TS>
+__device__ __forceinline__ RowSoftmax row_softmax(const TS* logits, int n) {
+  float mx = -INFINITY;
+  for (int i = 0; i < n; ++i) mx = fmaxf(mx, Elem<TS>::to_f(logits[i]));
+  float sum = 0.0f;
+  for (int i = 0; i < n; ++i) sum += expf(Elem<TS>::to_f(logits[i]) - mx);
+  return {mx, sum};
+}
+
+__device__ __forceinline__ float softmax_weight(float x, const RowSoftmax& sm) {
+  return __fdiv_rn(expf(x - sm.mx), sm.sum);
+}
+
 // A zero value row: invalid corners point here, so every lane loads finite
 // zeros instead of selecting per register (the widest row is 2048 bytes).
 static __device__ __align__(16) unsigned char g_zero_row[2048];
@@ -154,7 +197,7 @@ __device__ __forceinline__ Corners<NDIM> make_corners(const Point<NDIM>& pt, con
 }
 
 // ------------------------------------------------------------------ forward
-template <typename T, typename TS, int NDIM, int VB, int VPL>
+template <typename T, typename TS, int NDIM, int VB, int VPL, bool FUSED>
 __global__ void __launch_bounds__(kThreads)
     msda_fwd_kernel(const Problem p, T* __restrict__ out) {
   __shared__ LevelSmem lv;
@@ -183,6 +226,14 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
   for (int v = 0; v < VPL; ++v) has[v] = j + v * G < p.nv;
 
+  // FUSED: lrow / arow hold the raw offsets / logits of the row.
+  const float* rrow = nullptr;
+  RowSoftmax sm{0.0f, 1.0f};
+  if constexpr (FUSED) {
+    rrow = p.ref + (rc.b * p.Q + rc.q) * p.L * NDIM;
+    sm = row_softmax<TS>(arow, LP);
+  }
+
   float acc[VPL][EPV];
 #pragma unroll
   for (int v = 0; v < VPL; ++v)
@@ -194,8 +245,15 @@ __global__ void __launch_bounds__(kThreads)
     const LevelGeom g = level_geom(lv, l, key_bytes);
     for (int pp = 0; pp < P; ++pp) {
       const int s = l * P + pp;
-      const Point<NDIM> pt = load_point<TS, NDIM>(lrow + s * NDIM, g.sz, p);
-      const float a = Elem<TS>::to_f(arow[s]);
+      Point<NDIM> pt;
+      float a;
+      if constexpr (FUSED) {
+        pt = load_point_fused<TS, NDIM>(lrow + s * NDIM, rrow + l * NDIM, g.sz, p);
+        a = softmax_weight(Elem<TS>::to_f(arow[s]), sm);
+      } else {
+        pt = load_point<TS, NDIM>(lrow + s * NDIM, g.sz, p);
+        a = Elem<TS>::to_f(arow[s]);
+      }
       const Corners<NDIM> cs = make_corners<NDIM>(pt, g, vbase, key_bytes, j * VB);
       Raw<VB> raw[NC][VPL];
 #pragma unroll
@@ -308,7 +366,14 @@ __device__ __forceinline__ void red_add_16(T* dst, const float* v) {
 // atomic_add into a grad_value of the input dtype does
 // (src/msda_triton/triton/msda_3d.py:477, :942); the other levels keep fp32
 // accumulation, possibly in a compacted accumulator (p.acc_start).
-template <typename T, typename TS, int NDIM, int VB, int VPL>
+//
+// FUSED (prologue inside the kernel): grad_loc receives the offset gradient
+// (location gradient / size), p.ref_partial the per-level sums over points of
+// the location gradient (the reference-point gradient before the sum over
+// heads), and grad_attn the logit gradient: during the sample loop it holds
+// dL/dweight, and the row's last step turns it into the softmax backward
+// w * (dL/dw - sum(w * dL/dw)).
+template <typename T, typename TS, int NDIM, int VB, int VPL, bool FUSED>
 __global__ void __launch_bounds__(kThreads)
     msda_bwd_kernel(const Problem p, const T* __restrict__ grad_out, float* __restrict__ gacc,
                     TS* __restrict__ grad_loc, TS* __restrict__ grad_attn) {
@@ -342,6 +407,16 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
   for (int v = 0; v < VPL; ++v) has[v] = active && (j + v * G < p.nv);
 
+  // FUSED: lrow / arow hold the raw offsets / logits of the row (row 0's for
+  // the masked lanes past the end, which never store).
+  const float* rrow = nullptr;
+  RowSoftmax sm{0.0f, 1.0f};
+  float wdot = 0.0f;  // sum over the row's samples of weight * dL/dweight
+  if constexpr (FUSED) {
+    rrow = p.ref + (rc.b * p.Q + rc.q) * p.L * NDIM;
+    sm = row_softmax<TS>(arow, LP);
+  }
+
   float go[VPL][EPV];
   const char* gorow = reinterpret_cast<const char*>(grad_out) +
                       row * p.C * static_cast<int64_t>(sizeof(T));
@@ -363,6 +438,7 @@ __global__ void __launch_bounds__(kThreads)
   for (int l = 0; l < p.L; ++l) {
     const LevelGeom g = level_geom(lv, l, key_bytes);
     const bool d16 = (sizeof(T) == 2) && ((p.direct16 >> l) & 1);
+    float ref_sum[3] = {0.0f, 0.0f, 0.0f};  // FUSED: this level's location-gradient sum
     const int64_t kshift = p.acc_compact ? p.acc_start[l] - g.start : 0;
     char* acc_lane = reinterpret_cast<char*>(
         gacc + ((rc.b * p.acc_keys + kshift) * p.H + rc.h) * p.C + j * EPV);
@@ -371,8 +447,13 @@ __global__ void __launch_bounds__(kThreads)
       Point<NDIM> pt;
       float a = 0.0f;
       if (active) {
-        pt = load_point<TS, NDIM>(lrow + s * NDIM, g.sz, p);
-        a = Elem<TS>::to_f(arow[s]);
+        if constexpr (FUSED) {
+          pt = load_point_fused<TS, NDIM>(lrow + s * NDIM, rrow + l * NDIM, g.sz, p);
+          a = softmax_weight(Elem<TS>::to_f(arow[s]), sm);
+        } else {
+          pt = load_point<TS, NDIM>(lrow + s * NDIM, g.sz, p);
+          a = Elem<TS>::to_f(arow[s]);
+        }
       } else {
 #pragma unroll
         for (int ax = 0; ax < 3; ++ax) {
@@ -440,14 +521,38 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int ax = 0; ax < NDIM; ++ax) g_ix[ax] += __shfl_xor_sync(0xffffffffu, g_ix[ax], o);
       }
+      if constexpr (FUSED) wdot = fmaf(a, g_attn, wdot);
       if (active && j == 0) {
         grad_attn[row * LP + s] = Elem<TS>::from_f(g_attn);
         TS* gl = grad_loc + (row * LP + s) * NDIM;
 #pragma unroll
         for (int ax = 0; ax < NDIM; ++ax) {
-          const float gval = a * g_ix[ax] * static_cast<float>(g.sz[ax]);
-          gl[ax] = Elem<TS>::from_f(pt.pass[ax] ? gval : 0.0f);
+          const float size = static_cast<float>(g.sz[ax]);
+          const float gval = pt.pass[ax] ? a * g_ix[ax] * size : 0.0f;
+          if constexpr (FUSED) {
+            gl[ax] = Elem<TS>::from_f(__fdiv_rn(gval, size));
+            ref_sum[ax] += gval;
+          } else {
+            gl[ax] = Elem<TS>::from_f(gval);
+          }
         }
+      }
+    }
+    if constexpr (FUSED) {
+      if (active && j == 0) {
+        float* rp = p.ref_partial + (row * p.L + l) * NDIM;
+#pragma unroll
+        for (int ax = 0; ax < NDIM; ++ax) rp[ax] = ref_sum[ax];
+      }
+    }
+  }
+  if constexpr (FUSED) {
+    if (active && j == 0) {
+      // softmax backward over the row's L*P logits
+      TS* ga = grad_attn + row * LP;
+      for (int s = 0; s < LP; ++s) {
+        const float w = softmax_weight(Elem<TS>::to_f(arow[s]), sm);
+        ga[s] = Elem<TS>::from_f(w * (Elem<TS>::to_f(ga[s]) - wdot));
       }
     }
   }

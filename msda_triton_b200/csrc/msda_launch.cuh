@@ -22,21 +22,21 @@ constexpr bool kAllowed = (VB == 16 && (VPL == 1 || VPL == 2 || VPL == 4)) ||
                           (VB == 8 && (VPL == 1 || VPL == 2 || VPL == 4 || VPL == 8)) ||
                           ((VB == 4 || VB == 2) && (VPL == 1 || VPL == 8));
 
-template <typename T, typename TS, int NDIM, int VB, int VPL>
+template <typename T, typename TS, int NDIM, int VB, int VPL, bool F>
 static cudaError_t fwd_one(const LaunchShape& ls, const Problem& p, void* out, cudaStream_t st) {
   if constexpr (kAllowed<VB, VPL> && VB != 8) {
-    msda_fwd_kernel<T, TS, NDIM, VB, VPL>
+    msda_fwd_kernel<T, TS, NDIM, VB, VPL, F>
         <<<dim3(static_cast<unsigned>(ls.grid)), kThreads, 0, st>>>(p, static_cast<T*>(out));
     return cudaGetLastError();
   }
   return cudaErrorInvalidValue;
 }
 
-template <typename T, typename TS, int NDIM, int VB, int VPL>
+template <typename T, typename TS, int NDIM, int VB, int VPL, bool F>
 static cudaError_t bwd_one(const LaunchShape& ls, const Problem& p, const void* grad_out,
                            float* gacc, void* grad_loc, void* grad_attn, cudaStream_t st) {
   if constexpr (kAllowed<VB, VPL> && (VB != 8 || sizeof(T) == 2)) {
-    msda_bwd_kernel<T, TS, NDIM, VB, VPL><<<dim3(static_cast<unsigned>(ls.grid)), kThreads, 0, st>>>(
+    msda_bwd_kernel<T, TS, NDIM, VB, VPL, F><<<dim3(static_cast<unsigned>(ls.grid)), kThreads, 0, st>>>(
         p, static_cast<const T*>(grad_out), gacc, static_cast<TS*>(grad_loc),
         static_cast<TS*>(grad_attn));
     return cudaGetLastError();
@@ -44,69 +44,70 @@ static cudaError_t bwd_one(const LaunchShape& ls, const Problem& p, const void* 
   return cudaErrorInvalidValue;
 }
 
-template <typename T, typename TS, int NDIM, int VB>
+template <typename T, typename TS, int NDIM, int VB, bool F>
 static cudaError_t fwd_vpl(const LaunchShape& ls, const Problem& p, void* out, cudaStream_t st) {
   switch (ls.vpl) {
-    case 1: return fwd_one<T, TS, NDIM, VB, 1>(ls, p, out, st);
-    case 2: return fwd_one<T, TS, NDIM, VB, 2>(ls, p, out, st);
-    case 4: return fwd_one<T, TS, NDIM, VB, 4>(ls, p, out, st);
-    case 8: return fwd_one<T, TS, NDIM, VB, 8>(ls, p, out, st);
+    case 1: return fwd_one<T, TS, NDIM, VB, 1, F>(ls, p, out, st);
+    case 2: return fwd_one<T, TS, NDIM, VB, 2, F>(ls, p, out, st);
+    case 4: return fwd_one<T, TS, NDIM, VB, 4, F>(ls, p, out, st);
+    case 8: return fwd_one<T, TS, NDIM, VB, 8, F>(ls, p, out, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
-template <typename T, typename TS, int NDIM, int VB>
+template <typename T, typename TS, int NDIM, int VB, bool F>
 static cudaError_t bwd_vpl(const LaunchShape& ls, const Problem& p, const void* grad_out,
                            float* gacc, void* grad_loc, void* grad_attn, cudaStream_t st) {
   switch (ls.vpl) {
-    case 1: return bwd_one<T, TS, NDIM, VB, 1>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
-    case 2: return bwd_one<T, TS, NDIM, VB, 2>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
-    case 4: return bwd_one<T, TS, NDIM, VB, 4>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
-    case 8: return bwd_one<T, TS, NDIM, VB, 8>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 1: return bwd_one<T, TS, NDIM, VB, 1, F>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 2: return bwd_one<T, TS, NDIM, VB, 2, F>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 4: return bwd_one<T, TS, NDIM, VB, 4, F>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 8: return bwd_one<T, TS, NDIM, VB, 8, F>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
-template <typename T, typename TS, int NDIM>
+template <typename T, typename TS, int NDIM, bool F>
 static cudaError_t fwd_vb(const LaunchShape& ls, const Problem& p, void* out, cudaStream_t st) {
   switch (ls.vb) {
-    case 16: return fwd_vpl<T, TS, NDIM, 16>(ls, p, out, st);
-    case 4: return fwd_vpl<T, TS, NDIM, 4>(ls, p, out, st);
+    case 16: return fwd_vpl<T, TS, NDIM, 16, F>(ls, p, out, st);
+    case 4: return fwd_vpl<T, TS, NDIM, 4, F>(ls, p, out, st);
     case 2:
-      if constexpr (sizeof(T) == 2) return fwd_vpl<T, TS, NDIM, 2>(ls, p, out, st);
+      if constexpr (sizeof(T) == 2) return fwd_vpl<T, TS, NDIM, 2, F>(ls, p, out, st);
       return cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }
 
-template <typename T, typename TS, int NDIM>
+template <typename T, typename TS, int NDIM, bool F>
 static cudaError_t bwd_vb(const LaunchShape& ls, const Problem& p, const void* grad_out,
                           float* gacc, void* grad_loc, void* grad_attn, cudaStream_t st) {
   switch (ls.vb) {
-    case 16: return bwd_vpl<T, TS, NDIM, 16>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 16: return bwd_vpl<T, TS, NDIM, 16, F>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
     case 8:
       if constexpr (sizeof(T) == 2)
-        return bwd_vpl<T, TS, NDIM, 8>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+        return bwd_vpl<T, TS, NDIM, 8, F>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
       return cudaErrorInvalidValue;
-    case 4: return bwd_vpl<T, TS, NDIM, 4>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+    case 4: return bwd_vpl<T, TS, NDIM, 4, F>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
     case 2:
       if constexpr (sizeof(T) == 2)
-        return bwd_vpl<T, TS, NDIM, 2>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+        return bwd_vpl<T, TS, NDIM, 2, F>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
       return cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }
 
-template <typename T, typename TS>
+// F selects the fused-prologue kernels (see Problem::ref).
+template <typename T, typename TS, bool F>
 cudaError_t launch_fwd(const LaunchShape& ls, const Problem& p, void* out, cudaStream_t st) {
-  return ls.ndim == 2 ? fwd_vb<T, TS, 2>(ls, p, out, st) : fwd_vb<T, TS, 3>(ls, p, out, st);
+  return ls.ndim == 2 ? fwd_vb<T, TS, 2, F>(ls, p, out, st) : fwd_vb<T, TS, 3, F>(ls, p, out, st);
 }
 
-template <typename T, typename TS>
+template <typename T, typename TS, bool F>
 cudaError_t launch_bwd(const LaunchShape& ls, const Problem& p, const void* grad_out,
                        float* gacc, void* grad_loc, void* grad_attn, cudaStream_t st) {
-  return ls.ndim == 2 ? bwd_vb<T, TS, 2>(ls, p, grad_out, gacc, grad_loc, grad_attn, st)
-                      : bwd_vb<T, TS, 3>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
+  return ls.ndim == 2 ? bwd_vb<T, TS, 2, F>(ls, p, grad_out, gacc, grad_loc, grad_attn, st)
+                      : bwd_vb<T, TS, 3, F>(ls, p, grad_out, gacc, grad_loc, grad_attn, st);
 }
 
 template <typename T>
@@ -136,17 +137,19 @@ cudaError_t launch_compact_cast(const Problem& p, const float* acc, void* gv, cu
   return cudaGetLastError();
 }
 
-// Explicit instantiations live in msda_inst_*.cu.
-#define MSDA_DECLARE_PAIR(T, TS)                                                              \
-  extern template cudaError_t launch_fwd<T, TS>(const LaunchShape&, const Problem&, void*,     \
-                                                cudaStream_t);                                 \
-  extern template cudaError_t launch_bwd<T, TS>(const LaunchShape&, const Problem&,            \
-                                                const void*, float*, void*, void*,             \
-                                                cudaStream_t);
-#define MSDA_INSTANTIATE_PAIR(T, TS)                                                          \
-  template cudaError_t launch_fwd<T, TS>(const LaunchShape&, const Problem&, void*,            \
-                                         cudaStream_t);                                        \
-  template cudaError_t launch_bwd<T, TS>(const LaunchShape&, const Problem&, const void*,      \
-                                         float*, void*, void*, cudaStream_t);
+// Explicit instantiations live in msda_inst_*.cu (plain) and
+// msda_inst_fused_*.cu (fused prologue).
+#define MSDA_DECLARE_MODE(T, TS, F)                                                           \
+  extern template cudaError_t launch_fwd<T, TS, F>(const LaunchShape&, const Problem&, void*,  \
+                                                   cudaStream_t);                              \
+  extern template cudaError_t launch_bwd<T, TS, F>(const LaunchShape&, const Problem&,         \
+                                                   const void*, float*, void*, void*,          \
+                                                   cudaStream_t);
+#define MSDA_DECLARE_PAIR(T, TS) MSDA_DECLARE_MODE(T, TS, false) MSDA_DECLARE_MODE(T, TS, true)
+#define MSDA_INSTANTIATE_MODE(T, TS, F)                                                       \
+  template cudaError_t launch_fwd<T, TS, F>(const LaunchShape&, const Problem&, void*,         \
+                                            cudaStream_t);                                     \
+  template cudaError_t launch_bwd<T, TS, F>(const LaunchShape&, const Problem&, const void*,   \
+                                            float*, void*, void*, cudaStream_t);
 
 }  // namespace msda
