@@ -18,6 +18,7 @@ __version__ = "0.1.0"
 
 from msda_triton_b200.msda_2d import MSDA2DFn, msda2d, msda2d_fwd
 from msda_triton_b200.msda_3d import MSDA3DFn, msda3d, msda3d_fwd
+from msda_triton_b200.fused import msda2d_fused, msda3d_fused
 from msda_triton_b200.modules import MSDA2D, MSDA3D
 
 __all__ = [
@@ -30,4 +31,6 @@ __all__ = [
     "MSDA3DFn",
     "MSDA2D",
     "MSDA3D",
+    "msda2d_fused",
+    "msda3d_fused",
 ]

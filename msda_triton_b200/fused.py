@@ -1,0 +1,137 @@
+"""MSDA with the deformable-attention prologue inside the kernels.
+
+A deformable-attention layer (the reference's MSDA2D / MSDA3D modules,
+src/msda_triton/pytorch/msda_2d.py:325-339, src/msda_triton/pytorch/msda_3d.py:325-350)
+turns two query projections into the kernel's inputs with separate tensor
+ops:
+
+    loc     = reference_points[:, :, None, :, None, :] + offsets / (W, H[, D])_l
+    weights = softmax(logits over the L*P samples of each (b, q, h))
+
+msda2d_fused / msda3d_fused take reference_points, the raw offsets and the raw
+logits instead; the kernels form the locations and weights per sample in
+registers (fp32), so neither tensor is written or read from HBM, and the
+backward produces the offset, logit and reference-point gradients directly
+(the logit gradient is the softmax backward w * (dL/dw - sum w * dL/dw), the
+reference-point gradient the location gradient summed over heads and
+points).  Results equal msda{2,3}d on the separately computed loc / weights
+up to the softmax's summation order (fp32).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from msda_triton_b200 import _core, _lib
+
+
+def _prepare(ndim, value, spatial_shapes, reference_points, offsets, logits):
+    if logits.dim() == 4 and offsets.dim() == 6:
+        logits = logits.reshape(*offsets.shape[:5])
+    _core.validate_inputs(ndim, value, spatial_shapes, offsets, logits)
+    B, Q, H, L, P, _ = offsets.shape
+    if tuple(reference_points.shape) != (B, Q, L, ndim):
+        raise ValueError(f"reference_points must be (B, Q, L, {ndim}) = {(B, Q, L, ndim)}, "
+                         f"got {tuple(reference_points.shape)}")
+    if not reference_points.is_cuda or reference_points.device != value.device:
+        raise ValueError(f"reference_points must be a CUDA tensor on {value.device}, "
+                         f"got {reference_points.device}")
+    if not reference_points.dtype.is_floating_point:
+        raise ValueError(f"reference_points must be floating point, got {reference_points.dtype}")
+    shapes, on_dev = _core.prepare_spatial(spatial_shapes)
+    off, lg = _core.sampling_pair(value, offsets, logits)
+    ref = reference_points.detach().to(torch.float32).contiguous()
+    return shapes, on_dev, ref, off, lg
+
+
+def _args(value, shapes, on_dev, ref, off, lg):
+    B, K, H, C = value.shape
+    _, Q, _, L, P, _ = off.shape
+    return (value.data_ptr(), _core._DTYPE_CODE[value.dtype], B, K, H, C,
+            shapes.data_ptr(), int(on_dev), L, ref.data_ptr(), off.data_ptr(), lg.data_ptr(),
+            _core._DTYPE_CODE[off.dtype], Q, P)
+
+
+class MSDAFusedFn(torch.autograd.Function):
+    """Autograd Function of msda{2,3}d_fused; gradients flow to value,
+    reference_points, sampling_offsets and attention_logits."""
+
+    @staticmethod
+    def forward(ctx, ndim, value, spatial_shapes, reference_points, sampling_offsets,
+                attention_logits, clamp_grid=True, clamp_eps=1e-4):
+        shapes, on_dev, ref, off, lg = _prepare(ndim, value, spatial_shapes, reference_points,
+                                                sampling_offsets, attention_logits)
+        value_c = value.contiguous()
+        B, _, H, C = value_c.shape
+        out = torch.empty((B, off.shape[1], H * C), device=value.device, dtype=value.dtype)
+        fn = _lib.lib().msda2d_fused_fwd if ndim == 2 else _lib.lib().msda3d_fused_fwd
+        with torch.cuda.device(value.device):
+            code = fn(*_args(value_c, shapes, on_dev, ref, off, lg), int(bool(clamp_grid)),
+                      float(clamp_eps), out.data_ptr(), _core._stream_ptr(value.device))
+        _core.check_status(code)
+        ctx.save_for_backward(value_c, shapes, ref, off, lg)
+        ctx.meta = (ndim, on_dev, bool(clamp_grid), float(clamp_eps), reference_points.dtype,
+                    sampling_offsets.dtype, attention_logits.dtype, attention_logits.shape)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        value, shapes, ref, off, lg = ctx.saved_tensors
+        ndim, on_dev, clamp, eps, ref_dt, off_dt, lg_dt, lg_shape = ctx.meta
+        go = grad_output.to(value.dtype).contiguous()
+        B, K, H, C = value.shape
+        _, Q, _, L, P, _ = off.shape
+        lib = _lib.lib()
+        ws_bytes = lib.msda_fused_bwd_workspace_bytes(ndim, _core._DTYPE_CODE[value.dtype], B, K,
+                                                      H, C, shapes.data_ptr(), int(on_dev), L, Q,
+                                                      P)
+        ws = torch.empty((ws_bytes,), device=value.device, dtype=torch.uint8) if ws_bytes else None
+        g_value = torch.empty_like(value)
+        g_off = torch.empty_like(off)
+        g_lg = torch.empty_like(lg)
+        partial = torch.empty((B, Q, H, L, ndim), device=value.device, dtype=torch.float32)
+        fn = lib.msda2d_fused_bwd if ndim == 2 else lib.msda3d_fused_bwd
+        with torch.cuda.device(value.device):
+            code = fn(*_args(value, shapes, on_dev, ref, off, lg), int(clamp), eps,
+                      go.data_ptr(), g_value.data_ptr(), partial.data_ptr(), g_off.data_ptr(),
+                      g_lg.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes,
+                      _core._stream_ptr(value.device))
+        _core.check_status(code)
+        g_ref = partial.sum(dim=2).to(ref_dt)
+        return (None, g_value, None, g_ref, g_off.to(off_dt), g_lg.to(lg_dt).reshape(lg_shape),
+                None, None)
+
+
+def _fused(ndim, value, value_spatial_shapes, reference_points, sampling_offsets,
+           attention_logits, clamp_grid, clamp_eps):
+    if not value.is_cuda:
+        raise ValueError(f"MSDA{ndim}D CUDA kernel requires CUDA tensors. Got CPU tensors instead.")
+    return MSDAFusedFn.apply(ndim, value, value_spatial_shapes, reference_points,
+                             sampling_offsets, attention_logits, clamp_grid, clamp_eps)
+
+
+def msda2d_fused(value: torch.Tensor, value_spatial_shapes: torch.Tensor,
+                 reference_points: torch.Tensor, sampling_offsets: torch.Tensor,
+                 attention_logits: torch.Tensor, clamp_grid: bool = True,
+                 clamp_eps: float = 1e-4) -> torch.Tensor:
+    """2D MSDA from the layer's raw projections.
+
+    value (B, K, H, C); value_spatial_shapes (L, 2) as (H, W); reference_points
+    (B, Q, L, 2) normalised (x, y); sampling_offsets (B, Q, H, L, P, 2) in cells
+    of each level; attention_logits (B, Q, H, L, P) or (B, Q, H, L*P).
+    Returns (B, Q, H*C) in value's dtype, with autograd."""
+    return _fused(2, value, value_spatial_shapes, reference_points, sampling_offsets,
+                  attention_logits, clamp_grid, clamp_eps)
+
+
+def msda3d_fused(value: torch.Tensor, value_spatial_shapes: torch.Tensor,
+                 reference_points: torch.Tensor, sampling_offsets: torch.Tensor,
+                 attention_logits: torch.Tensor, clamp_grid: bool = True,
+                 clamp_eps: float = 1e-4) -> torch.Tensor:
+    """3D MSDA from the layer's raw projections (as msda2d_fused, with
+    (L, 3) shapes (D, H, W), (x, y, z) reference points and offsets)."""
+    return _fused(3, value, value_spatial_shapes, reference_points, sampling_offsets,
+                  attention_logits, clamp_grid, clamp_eps)
+
+
+__all__ = ["msda2d_fused", "msda3d_fused", "MSDAFusedFn"]

@@ -6,7 +6,10 @@ the same constructor arguments, parameter names and shapes (state_dicts load
 either way), init_weights() patterns and RNG use, forward signature,
 batch_first / query_pos / key_padding_mask / identity handling, query and
 head chunking, gradient checkpointing and errors.  The deformable sampling
-itself is msda2d / msda3d of this package.
+itself is msda2d / msda3d of this package; with fused_prologue=True (the
+default, an extra keyword the reference's modules ignore) the locations and
+softmax weights are formed inside the kernels from the raw projections
+(msda2d_fused / msda3d_fused) instead of as separate tensors.
 
 Forward, with q the (batch-first) query and v the projected value:
     offsets = Linear(q) -> (B, Q, H, L, P, d)
@@ -24,6 +27,7 @@ import torch
 from torch import nn
 from torch.utils.checkpoint import checkpoint
 
+from msda_triton_b200.fused import msda2d_fused, msda3d_fused
 from msda_triton_b200.msda_2d import msda2d
 from msda_triton_b200.msda_3d import msda3d
 
@@ -38,7 +42,7 @@ class _MSDAModule(nn.Module):
                  dropout: float = 0.1, batch_first: bool = False,
                  query_chunk_size: int | None = None, head_chunk_size: int | None = None,
                  use_checkpoint: bool = False, clamp_grid: bool = True,
-                 clamp_eps: float = 1e-4, **kwargs) -> None:
+                 clamp_eps: float = 1e-4, fused_prologue: bool = True, **kwargs) -> None:
         super().__init__()
         if embed_dims % num_heads != 0:
             raise ValueError(f"embed_dims must be divisible by num_heads, but got {embed_dims} "
@@ -54,6 +58,7 @@ class _MSDAModule(nn.Module):
         self.use_checkpoint = use_checkpoint
         self.clamp_grid = clamp_grid
         self.clamp_eps = clamp_eps
+        self.fused_prologue = fused_prologue
         samples = num_heads * num_levels * num_points
         # creation order fixes the default-init RNG draws (as in the reference)
         self.sampling_offsets = nn.Linear(embed_dims, samples * self.NDIM)
@@ -84,6 +89,9 @@ class _MSDAModule(nn.Module):
 
     # ------------------------------------------------------------- forward
     def _sample(self, value, spatial_shapes, loc, weights):
+        raise NotImplementedError
+
+    def _sample_fused(self, value, spatial_shapes, ref, offsets, logits):
         raise NotImplementedError
 
     def forward(self, query: torch.Tensor, key: torch.Tensor | None = None,
@@ -136,17 +144,25 @@ class _MSDAModule(nn.Module):
             q1 = min(q0 + qc, num_query)
             qq = q[:, q0:q1]
             offsets = self.sampling_offsets(qq).view(bs, q1 - q0, H, L, P, d)
-            weights = self.attention_weights(qq).view(bs, q1 - q0, H, L * P)
-            weights = weights.softmax(-1).view(bs, q1 - q0, H, L, P)
-            loc = reference_points[:, q0:q1, None, :, None, :] + offsets / normalizer
+            logits = self.attention_weights(qq).view(bs, q1 - q0, H, L, P)
+            if self.fused_prologue:
+                # (loc, weights) formed per sample inside the kernels
+                ref = reference_points[:, q0:q1]
+                run = lambda h0, h1: self._run(self._sample_fused, v[:, :, h0:h1], shapes_host,
+                                               ref, offsets[:, :, h0:h1], logits[:, :, h0:h1])
+            else:
+                weights = logits.view(bs, q1 - q0, H, L * P).softmax(-1)
+                weights = weights.view(bs, q1 - q0, H, L, P)
+                loc = reference_points[:, q0:q1, None, :, None, :] + offsets / normalizer
+                run = lambda h0, h1: self._run(self._sample, v[:, :, h0:h1], shapes_host,
+                                               loc[:, :, h0:h1], weights[:, :, h0:h1])
             if hc == H:
-                chunks.append(self._run(v, shapes_host, loc, weights))
+                chunks.append(run(0, H))
                 continue
             out = q.new_zeros(bs, q1 - q0, self.embed_dims)
             for h0 in range(0, H, hc):
                 h1 = min(h0 + hc, H)
-                out[:, :, h0 * c:h1 * c] = self._run(v[:, :, h0:h1], shapes_host,
-                                                     loc[:, :, h0:h1], weights[:, :, h0:h1])
+                out[:, :, h0 * c:h1 * c] = run(h0, h1)
             chunks.append(out)
         out = chunks[0] if len(chunks) == 1 else torch.cat(chunks, dim=1)
         out = self.output_proj(out)
@@ -154,10 +170,10 @@ class _MSDAModule(nn.Module):
             out = out.permute(1, 0, 2)
         return self.dropout(out) + identity
 
-    def _run(self, v, spatial_shapes, loc, weights):
+    def _run(self, fn, *args):
         if self.use_checkpoint and self.training:
-            return checkpoint(self._sample, v, spatial_shapes, loc, weights, use_reentrant=False)
-        return self._sample(v, spatial_shapes, loc, weights)
+            return checkpoint(fn, *args, use_reentrant=False)
+        return fn(*args)
 
 
 class MSDA3D(_MSDAModule):
@@ -181,6 +197,10 @@ class MSDA3D(_MSDAModule):
     def _sample(self, v, spatial_shapes, loc, weights):
         return msda3d(v, spatial_shapes, loc, weights, self.clamp_grid, self.clamp_eps)
 
+    def _sample_fused(self, v, spatial_shapes, ref, offsets, logits):
+        return msda3d_fused(v, spatial_shapes, ref, offsets, logits, self.clamp_grid,
+                            self.clamp_eps)
+
 
 class MSDA2D(_MSDAModule):
     """2D multi-scale deformable attention module (bilinear sampling in the
@@ -201,6 +221,10 @@ class MSDA2D(_MSDAModule):
 
     def _sample(self, v, spatial_shapes, loc, weights):
         return msda2d(v, spatial_shapes, loc, weights, self.clamp_grid, self.clamp_eps)
+
+    def _sample_fused(self, v, spatial_shapes, ref, offsets, logits):
+        return msda2d_fused(v, spatial_shapes, ref, offsets, logits, self.clamp_grid,
+                            self.clamp_eps)
 
 
 __all__ = ["MSDA2D", "MSDA3D"]

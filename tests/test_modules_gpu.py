@@ -40,9 +40,9 @@ def _load(path):
     return {k: z[k] for k in z.files}
 
 
-def _module(z):
+def _module(z, fused=True):
     kw = ast.literal_eval(str(z["module_kwargs"]))
-    m = (MSDA3D if int(z["ndim"]) == 3 else MSDA2D)(**kw)
+    m = (MSDA3D if int(z["ndim"]) == 3 else MSDA2D)(**kw, fused_prologue=fused)
     m.load_state_dict({k[6:]: torch.from_numpy(v) for k, v in z.items() if k.startswith("param/")})
     m.train(bool(kw.get("use_checkpoint")))   # the fixtures' chunked cases ran in training mode
     return m.to(DEV)
@@ -67,24 +67,26 @@ def _run(m, z, shapes_on_device):
     return res
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "unfused"])
 @pytest.mark.parametrize("shapes_on_device", [True, False])
 @pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p)[:-4] for p in GOLDEN])
-def test_module_matches_reference(path, shapes_on_device):
+def test_module_matches_reference(path, shapes_on_device, fused):
     z = _load(path)
-    got = _run(_module(z), z, shapes_on_device)
+    got = _run(_module(z, fused), z, shapes_on_device)
     for k, g in got.items():
         torch.testing.assert_close(g.detach().cpu(), torch.from_numpy(z[k]), rtol=1e-4, atol=1e-4,
                                    msg=lambda m, k=k: f"{os.path.basename(path)} {k}: {m}")
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "unfused"])
 @pytest.mark.parametrize("cls,d", [(MSDA2D, 2), (MSDA3D, 3)])
-def test_module_bf16_autocast(cls, d):
+def test_module_bf16_autocast(cls, d, fused):
     """Mixed precision: under autocast the projections run in bf16, the
     locations and softmax weights stay fp32 -- the kernels take the mixed
     pair.  The result stays within the half-precision bar of fp32."""
     torch.manual_seed(0)
     m = cls(embed_dims=64, num_heads=4, num_levels=2, num_points=4, dropout=0.0,
-            batch_first=True).to(DEV)
+            batch_first=True, fused_prologue=fused).to(DEV)
     m.init_weights()
     shapes = torch.tensor([[6] * d, [3] * d], dtype=torch.int64, device=DEV)
     K = 6 ** d + 3 ** d
