@@ -84,13 +84,43 @@ __device__ __forceinline__ Point<NDIM> load_point(const TS* lp, const int32_t* s
   return pt;
 }
 
+// x / n rounded to nearest for a level size n, given r = 1/n rounded to
+// nearest: the product x*r corrected once by its exact FMA residual
+// (Markstein's method), which reproduces the IEEE quotient of the separate
+// tensor division without a division per sample.
+__device__ __forceinline__ float div_by_size(float x, float n, float r) {
+  const float q = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-q, n, x);
+  return __fmaf_rn(e, r, q);
+}
+
+// Per-level sizes and their reciprocals for div_by_size.
+template <int NDIM>
+struct LevelRcp {
+  float n[3];
+  float r[3];
+};
+
+template <int NDIM>
+__device__ __forceinline__ LevelRcp<NDIM> level_rcp(const int32_t* sz) {
+  LevelRcp<NDIM> lr;
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+    lr.n[a] = static_cast<float>(sz[a]);
+    lr.r[a] = __frcp_rn(lr.n[a]);
+  }
+  return lr;
+}
+
 // Fused prologue: the location of one sample from its raw offset and the
 // level's reference point, ref + offset / size per axis (size = W, H, D for
 // x, y, z), with the rounding of the separate `ref + offsets / normalizer`
 // expression (pytorch/msda_3d.py:336-339, pytorch/msda_2d.py:335-339).
 template <typename TS, int NDIM>
 __device__ __forceinline__ Point<NDIM> load_point_fused(const TS* off, const float* ref,
-                                                        const int32_t* sz, const Problem& p) {
+                                                        const int32_t* sz,
+                                                        const LevelRcp<NDIM>& lr,
+                                                        const Problem& p) {
   Point<NDIM> pt;
 #pragma unroll
   for (int a = 0; a < 3; ++a) {
@@ -100,31 +130,50 @@ __device__ __forceinline__ Point<NDIM> load_point_fused(const TS* off, const flo
   }
 #pragma unroll
   for (int a = 0; a < NDIM; ++a) {
-    const float x =
-        __fadd_rn(ref[a], __fdiv_rn(Elem<TS>::to_f(off[a]), static_cast<float>(sz[a])));
+    const float x = __fadd_rn(ref[a], div_by_size(Elem<TS>::to_f(off[a]), lr.n[a], lr.r[a]));
     resolve_axis(x, sz[a], p.clamp, p.lo, p.hi, pt.i0[a], pt.f[a], pt.pass[a]);
   }
   return pt;
 }
 
-// Softmax of one row's L*P weight logits: max and sum of exp(x - max); the
-// weight of a sample is exp(x - max) / sum.
+// Softmax of one row's L*P weight logits, shared by the row's G lanes: lane
+// j takes logits j, j+G, ... in one pass (running maximum, the sum rescaled
+// whenever it rises), then the G partial (max, sum) pairs are merged with
+// butterfly shuffles, which leaves the same pair on every lane.  The weight
+// of a sample is exp(x - max) * (1 / sum).  -inf logits weigh 0.  All lanes
+// of the warp must call it.
 struct RowSoftmax {
   float mx;
-  float sum;
+  float inv;
 };
 
 template <typename TS>
-__device__ __forceinline__ RowSoftmax row_softmax(const TS* logits, int n) {
+__device__ __forceinline__ RowSoftmax row_softmax(const TS* logits, int n, int j, int G) {
   float mx = -INFINITY;
-  for (int i = 0; i < n; ++i) mx = fmaxf(mx, Elem<TS>::to_f(logits[i]));
   float sum = 0.0f;
-  for (int i = 0; i < n; ++i) sum += expf(Elem<TS>::to_f(logits[i]) - mx);
-  return {mx, sum};
+  for (int i = j; i < n; i += G) {
+    const float x = Elem<TS>::to_f(logits[i]);
+    if (x > mx) {
+      sum = fmaf(sum, expf(mx - x), 1.0f);
+      mx = x;
+    } else if (x != -INFINITY) {
+      sum += expf(x - mx);
+    }
+  }
+  for (int o = 1; o < G; o <<= 1) {
+    const float mo = __shfl_xor_sync(0xffffffffu, mx, o);
+    const float so = __shfl_xor_sync(0xffffffffu, sum, o);
+    const float m = fmaxf(mx, mo);
+    const float ta = sum == 0.0f ? 0.0f : sum * expf(mx - m);
+    const float tb = so == 0.0f ? 0.0f : so * expf(mo - m);
+    sum = ta + tb;
+    mx = m;
+  }
+  return {mx, __frcp_rn(sum)};
 }
 
 __device__ __forceinline__ float softmax_weight(float x, const RowSoftmax& sm) {
-  return __fdiv_rn(expf(x - sm.mx), sm.sum);
+  return expf(x - sm.mx) * sm.inv;
 }
 
 // A zero value row: invalid corners point here, so every lane loads finite
@@ -198,8 +247,7 @@ __device__ __forceinline__ Corners<NDIM> make_corners(const Point<NDIM>& pt, con
 
 // ------------------------------------------------------------------ forward
 template <typename T, typename TS, int NDIM, int VB, int VPL, bool FUSED>
-__global__ void __launch_bounds__(kThreads)
-    msda_fwd_kernel(const Problem p, T* __restrict__ out) {
+__device__ __forceinline__ void msda_fwd_body(const Problem p, T* __restrict__ out) {
   __shared__ LevelSmem lv;
   load_levels(p, lv, NDIM);
 
@@ -208,10 +256,18 @@ __global__ void __launch_bounds__(kThreads)
   constexpr int NC = 1 << NDIM;
 
   const uint64_t tid = static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  const uint64_t r = tid >> p.log2g;
+  uint64_t r = tid >> p.log2g;
   const int G = 1 << p.log2g;
   const int j = static_cast<int>(tid & static_cast<uint64_t>(G - 1));
-  if (r >= static_cast<uint64_t>(p.B * p.Q * p.H)) return;
+  bool active = true;
+  if constexpr (FUSED) {
+    // the fused prologue shuffles within lane groups: rows past the end stay
+    // (on row 0, storing nothing) instead of leaving the warp
+    active = r < static_cast<uint64_t>(p.B * p.Q * p.H);
+    if (!active) r = 0;
+  } else {
+    if (r >= static_cast<uint64_t>(p.B * p.Q * p.H)) return;
+  }
 
   const RowCoord rc = decode_row(static_cast<uint32_t>(r), p);
   const int64_t row = (rc.b * p.Q + rc.q) * p.H + rc.h;
@@ -224,14 +280,17 @@ __global__ void __launch_bounds__(kThreads)
 
   bool has[VPL];
 #pragma unroll
-  for (int v = 0; v < VPL; ++v) has[v] = j + v * G < p.nv;
+  for (int v = 0; v < VPL; ++v) has[v] = active && (j + v * G < p.nv);
 
-  // FUSED: lrow / arow hold the raw offsets / logits of the row.
+  // FUSED: lrow / arow hold the raw offsets / logits of the row.  Lane j
+  // computes the weight of every G-th sample; the others get it by shuffle.
   const float* rrow = nullptr;
   RowSoftmax sm{0.0f, 1.0f};
+  float wchunk = 0.0f;
+  const int gbase = static_cast<int>(threadIdx.x & 31u) & ~(G - 1);
   if constexpr (FUSED) {
     rrow = p.ref + (rc.b * p.Q + rc.q) * p.L * NDIM;
-    sm = row_softmax<TS>(arow, LP);
+    sm = row_softmax<TS>(arow, LP, j, G);
   }
 
   float acc[VPL][EPV];
@@ -243,13 +302,22 @@ __global__ void __launch_bounds__(kThreads)
   const int P = static_cast<int>(p.P);
   for (int l = 0; l < p.L; ++l) {
     const LevelGeom g = level_geom(lv, l, key_bytes);
+    LevelRcp<NDIM> lr;
+    float rl[3];
+    if constexpr (FUSED) {
+      lr = level_rcp<NDIM>(g.sz);
+#pragma unroll
+      for (int ax = 0; ax < NDIM; ++ax) rl[ax] = rrow[l * NDIM + ax];
+    }
     for (int pp = 0; pp < P; ++pp) {
       const int s = l * P + pp;
       Point<NDIM> pt;
       float a;
       if constexpr (FUSED) {
-        pt = load_point_fused<TS, NDIM>(lrow + s * NDIM, rrow + l * NDIM, g.sz, p);
-        a = softmax_weight(Elem<TS>::to_f(arow[s]), sm);
+        if ((s & (G - 1)) == 0)
+          wchunk = s + j < LP ? softmax_weight(Elem<TS>::to_f(arow[s + j]), sm) : 0.0f;
+        a = __shfl_sync(0xffffffffu, wchunk, gbase | (s & (G - 1)));
+        pt = load_point_fused<TS, NDIM>(lrow + s * NDIM, rl, g.sz, lr, p);
       } else {
         pt = load_point<TS, NDIM>(lrow + s * NDIM, g.sz, p);
         a = Elem<TS>::to_f(arow[s]);
@@ -280,6 +348,20 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
   for (int v = 0; v < VPL; ++v)
     if (has[v]) st_chunk<VB>(orow + (j + v * G) * VB, CK::pack(acc[v]));
+}
+
+template <typename T, typename TS, int NDIM, int VB, int VPL>
+__global__ void __launch_bounds__(kThreads)
+    msda_fwd_kernel(const Problem p, T* __restrict__ out) {
+  msda_fwd_body<T, TS, NDIM, VB, VPL, false>(p, out);
+}
+
+// The fused one-chunk-per-lane variants (the common row shapes) are held to
+// the occupancy of the plain kernels; wider rows would spill.
+template <typename T, typename TS, int NDIM, int VB, int VPL>
+__global__ void __launch_bounds__(kThreads, VPL == 1 ? 4 : 1)
+    msda_fwd_fused_kernel(const Problem p, T* __restrict__ out) {
+  msda_fwd_body<T, TS, NDIM, VB, VPL, true>(p, out);
 }
 
 // ------------------------------------------------------------------ backward
@@ -374,9 +456,9 @@ __device__ __forceinline__ void red_add_16(T* dst, const float* v) {
 // dL/dweight, and the row's last step turns it into the softmax backward
 // w * (dL/dw - sum(w * dL/dw)).
 template <typename T, typename TS, int NDIM, int VB, int VPL, bool FUSED>
-__global__ void __launch_bounds__(kThreads)
-    msda_bwd_kernel(const Problem p, const T* __restrict__ grad_out, float* __restrict__ gacc,
-                    TS* __restrict__ grad_loc, TS* __restrict__ grad_attn) {
+__device__ __forceinline__ void msda_bwd_body(const Problem p, const T* __restrict__ grad_out,
+                                              float* __restrict__ gacc, TS* __restrict__ grad_loc,
+                                              TS* __restrict__ grad_attn) {
   __shared__ LevelSmem lv;
   load_levels(p, lv, NDIM);
 
@@ -412,9 +494,11 @@ __global__ void __launch_bounds__(kThreads)
   const float* rrow = nullptr;
   RowSoftmax sm{0.0f, 1.0f};
   float wdot = 0.0f;  // sum over the row's samples of weight * dL/dweight
+  float wchunk = 0.0f;
+  const int gbase = static_cast<int>(threadIdx.x & 31u) & ~(G - 1);
   if constexpr (FUSED) {
     rrow = p.ref + (rc.b * p.Q + rc.q) * p.L * NDIM;
-    sm = row_softmax<TS>(arow, LP);
+    sm = row_softmax<TS>(arow, LP, j, G);
   }
 
   float go[VPL][EPV];
@@ -439,6 +523,13 @@ __global__ void __launch_bounds__(kThreads)
     const LevelGeom g = level_geom(lv, l, key_bytes);
     const bool d16 = (sizeof(T) == 2) && ((p.direct16 >> l) & 1);
     float ref_sum[3] = {0.0f, 0.0f, 0.0f};  // FUSED: this level's location-gradient sum
+    LevelRcp<NDIM> lr;
+    float rl[3];
+    if constexpr (FUSED) {
+      lr = level_rcp<NDIM>(g.sz);
+#pragma unroll
+      for (int ax = 0; ax < NDIM; ++ax) rl[ax] = rrow[l * NDIM + ax];
+    }
     const int64_t kshift = p.acc_compact ? p.acc_start[l] - g.start : 0;
     char* acc_lane = reinterpret_cast<char*>(
         gacc + ((rc.b * p.acc_keys + kshift) * p.H + rc.h) * p.C + j * EPV);
@@ -446,10 +537,16 @@ __global__ void __launch_bounds__(kThreads)
       const int s = l * P + pp;
       Point<NDIM> pt;
       float a = 0.0f;
+      if constexpr (FUSED) {
+        // every G-th weight per lane, shared by shuffle (all lanes take part)
+        if ((s & (G - 1)) == 0)
+          wchunk = s + j < LP ? softmax_weight(Elem<TS>::to_f(arow[s + j]), sm) : 0.0f;
+        a = __shfl_sync(0xffffffffu, wchunk, gbase | (s & (G - 1)));
+        if (!active) a = 0.0f;
+      }
       if (active) {
         if constexpr (FUSED) {
-          pt = load_point_fused<TS, NDIM>(lrow + s * NDIM, rrow + l * NDIM, g.sz, p);
-          a = softmax_weight(Elem<TS>::to_f(arow[s]), sm);
+          pt = load_point_fused<TS, NDIM>(lrow + s * NDIM, rl, g.sz, lr, p);
         } else {
           pt = load_point<TS, NDIM>(lrow + s * NDIM, g.sz, p);
           a = Elem<TS>::to_f(arow[s]);
@@ -530,7 +627,7 @@ __global__ void __launch_bounds__(kThreads)
           const float size = static_cast<float>(g.sz[ax]);
           const float gval = pt.pass[ax] ? a * g_ix[ax] * size : 0.0f;
           if constexpr (FUSED) {
-            gl[ax] = Elem<TS>::from_f(__fdiv_rn(gval, size));
+            gl[ax] = Elem<TS>::from_f(div_by_size(gval, lr.n[ax], lr.r[ax]));
             ref_sum[ax] += gval;
           } else {
             gl[ax] = Elem<TS>::from_f(gval);
@@ -547,15 +644,34 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   if constexpr (FUSED) {
-    if (active && j == 0) {
-      // softmax backward over the row's L*P logits
+    // softmax backward over the row's L*P logits, spread over the row's
+    // lanes (lane 0 stored dL/dw above; every lane holds wdot)
+    __syncwarp();
+    if (active) {
       TS* ga = grad_attn + row * LP;
-      for (int s = 0; s < LP; ++s) {
+      for (int s = j; s < LP; s += G) {
         const float w = softmax_weight(Elem<TS>::to_f(arow[s]), sm);
         ga[s] = Elem<TS>::from_f(w * (Elem<TS>::to_f(ga[s]) - wdot));
       }
     }
   }
+}
+
+template <typename T, typename TS, int NDIM, int VB, int VPL>
+__global__ void __launch_bounds__(kThreads)
+    msda_bwd_kernel(const Problem p, const T* __restrict__ grad_out, float* __restrict__ gacc,
+                    TS* __restrict__ grad_loc, TS* __restrict__ grad_attn) {
+  msda_bwd_body<T, TS, NDIM, VB, VPL, false>(p, grad_out, gacc, grad_loc, grad_attn);
+}
+
+// One-chunk rows are held to the plain kernel's occupancy (3 CTAs/SM for
+// 16-bit values, 2 for fp32); wider rows would spill.
+template <typename T, typename TS, int NDIM, int VB, int VPL>
+__global__ void __launch_bounds__(kThreads, VPL == 1 ? (sizeof(T) == 2 ? 3 : 2) : 1)
+    msda_bwd_fused_kernel(const Problem p, const T* __restrict__ grad_out,
+                          float* __restrict__ gacc, TS* __restrict__ grad_loc,
+                          TS* __restrict__ grad_attn) {
+  msda_bwd_body<T, TS, NDIM, VB, VPL, true>(p, grad_out, gacc, grad_loc, grad_attn);
 }
 
 // fp32 accumulation buffer -> grad_value in the input dtype.

@@ -25,8 +25,12 @@ constexpr bool kAllowed = (VB == 16 && (VPL == 1 || VPL == 2 || VPL == 4)) ||
 template <typename T, typename TS, int NDIM, int VB, int VPL, bool F>
 static cudaError_t fwd_one(const LaunchShape& ls, const Problem& p, void* out, cudaStream_t st) {
   if constexpr (kAllowed<VB, VPL> && VB != 8) {
-    msda_fwd_kernel<T, TS, NDIM, VB, VPL, F>
-        <<<dim3(static_cast<unsigned>(ls.grid)), kThreads, 0, st>>>(p, static_cast<T*>(out));
+    if constexpr (F)
+      msda_fwd_fused_kernel<T, TS, NDIM, VB, VPL>
+          <<<dim3(static_cast<unsigned>(ls.grid)), kThreads, 0, st>>>(p, static_cast<T*>(out));
+    else
+      msda_fwd_kernel<T, TS, NDIM, VB, VPL>
+          <<<dim3(static_cast<unsigned>(ls.grid)), kThreads, 0, st>>>(p, static_cast<T*>(out));
     return cudaGetLastError();
   }
   return cudaErrorInvalidValue;
@@ -36,9 +40,16 @@ template <typename T, typename TS, int NDIM, int VB, int VPL, bool F>
 static cudaError_t bwd_one(const LaunchShape& ls, const Problem& p, const void* grad_out,
                            float* gacc, void* grad_loc, void* grad_attn, cudaStream_t st) {
   if constexpr (kAllowed<VB, VPL> && (VB != 8 || sizeof(T) == 2)) {
-    msda_bwd_kernel<T, TS, NDIM, VB, VPL, F><<<dim3(static_cast<unsigned>(ls.grid)), kThreads, 0, st>>>(
-        p, static_cast<const T*>(grad_out), gacc, static_cast<TS*>(grad_loc),
-        static_cast<TS*>(grad_attn));
+    if constexpr (F)
+      msda_bwd_fused_kernel<T, TS, NDIM, VB, VPL>
+          <<<dim3(static_cast<unsigned>(ls.grid)), kThreads, 0, st>>>(
+              p, static_cast<const T*>(grad_out), gacc, static_cast<TS*>(grad_loc),
+              static_cast<TS*>(grad_attn));
+    else
+      msda_bwd_kernel<T, TS, NDIM, VB, VPL>
+          <<<dim3(static_cast<unsigned>(ls.grid)), kThreads, 0, st>>>(
+              p, static_cast<const T*>(grad_out), gacc, static_cast<TS*>(grad_loc),
+              static_cast<TS*>(grad_attn));
     return cudaGetLastError();
   }
   return cudaErrorInvalidValue;
