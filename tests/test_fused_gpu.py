@@ -122,3 +122,23 @@ def test_errors():
         M.msda3d_fused(value, shp, ref, off, logits)
     with pytest.raises(NotImplementedError):
         M.msda3d_fused(v.double(), shp, r, o, lg)
+
+
+@pytest.mark.parametrize("ndim", [2, 3])
+def test_location_bit_exact(ndim):
+    """One sample per row (L = P = 1): both paths weigh it exactly 1, so the
+    output and the offset gradient are bitwise equal iff the fused location
+    ref + offset / size rounds exactly like the separate tensor expression
+    (level sizes that are not powers of two, offsets of several cells)."""
+    shapes = [(37, 53)] if ndim == 2 else [(11, 19, 23)]
+    B, Q, H, C, P = 2, 4000, 4, 16, 1
+    value, shp, ref, off, logits, go = _inputs(ndim, B, Q, H, C, P, shapes, seed=11,
+                                               off_scale=7.0)
+    t = [x.to(DEV) for x in (value, ref, off, logits)]
+    fused = M.msda3d_fused if ndim == 3 else M.msda2d_fused
+    got = _run(lambda v, r, o, lg: fused(v, shp, r, o, lg, False, 1e-4), t, go.to(DEV))
+    want = _run(lambda v, r, o, lg: _unfused(ndim, v, shp, r, o, lg, False, 1e-4), t,
+                go.to(DEV))
+    assert torch.equal(got[0], want[0]), "output"
+    assert torch.equal(got[3], want[3]), "offset gradient"
+    torch.testing.assert_close(got[2], want[2], rtol=1e-5, atol=1e-5)
