@@ -695,18 +695,20 @@ __global__ void __launch_bounds__(kThreads)
 
 // Compacted fp32 accumulator (the keys of the levels not in p.direct16,
 // p.acc_keys per batch entry) -> their grad_value rows in the input dtype.
-// V = 4: one float4 in, one 8-byte store out (16-bit T, H*C % 4 == 0,
-// grad_value 8-byte aligned); V = 1 otherwise.
+// One warp per key row: the row's batch entry, level and destination key are
+// resolved once per row, then the lanes stream its H*C elements.
+// V = 4: float4 in, one 8-byte store out (16-bit T, H*C % 4 == 0, grad_value
+// 8-byte aligned); V = 1 otherwise.
 template <typename T, int V>
 __global__ void __launch_bounds__(kThreads)
     msda_compact_cast_kernel(const Problem p, const float* __restrict__ acc, T* __restrict__ gv) {
   const int64_t row = p.H * p.C;  // elements per key
   const int64_t rv = row / V;
-  const int64_t n = p.B * p.acc_keys * rv;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * kThreads) {
-    const int64_t r = i / rv;
-    const int64_t e = (i - r * rv) * V;
+  const int64_t nrows = p.B * p.acc_keys;
+  const int lane = static_cast<int>(threadIdx.x & 31u);
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / 32; r < nrows;
+       r += nwarps) {
     const int64_t b = r / p.acc_keys;
     const int64_t ak = r - b * p.acc_keys;
     int64_t shift = 0;  // key - accumulator key of the level holding ak
@@ -714,17 +716,20 @@ __global__ void __launch_bounds__(kThreads)
     for (int k = 0; k < kMaxLevels; ++k)
       if (k < p.L && !((p.direct16 >> k) & 1) && ak >= p.acc_start[k])
         shift = static_cast<int64_t>(p.lv.start[k]) - p.acc_start[k];
-    T* dst = gv + (b * p.K + ak + shift) * row + e;
-    if constexpr (V == 4) {
-      const float4 v = *reinterpret_cast<const float4*>(acc + r * row + e);
-      struct alignas(8) Quad { T h[4]; } o;
-      o.h[0] = Elem<T>::from_f(v.x);
-      o.h[1] = Elem<T>::from_f(v.y);
-      o.h[2] = Elem<T>::from_f(v.z);
-      o.h[3] = Elem<T>::from_f(v.w);
-      *reinterpret_cast<Quad*>(dst) = o;
-    } else {
-      *dst = Elem<T>::from_f(acc[r * row + e]);
+    const float* src = acc + r * row;
+    T* dst = gv + (b * p.K + ak + shift) * row;
+    for (int64_t e = lane; e < rv; e += 32) {
+      if constexpr (V == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(src + e * 4);
+        struct alignas(8) Quad { T h[4]; } o;
+        o.h[0] = Elem<T>::from_f(v.x);
+        o.h[1] = Elem<T>::from_f(v.y);
+        o.h[2] = Elem<T>::from_f(v.z);
+        o.h[3] = Elem<T>::from_f(v.w);
+        *reinterpret_cast<Quad*>(dst + e * 4) = o;
+      } else {
+        dst[e] = Elem<T>::from_f(src[e]);
+      }
     }
   }
 }

@@ -135,9 +135,9 @@ template <typename T>
 cudaError_t launch_compact_cast(const Problem& p, const float* acc, void* gv, cudaStream_t st) {
   const int64_t row = p.H * p.C;
   const bool vec = row % 4 == 0 && reinterpret_cast<uintptr_t>(gv) % 8 == 0;
-  const int64_t n = p.B * p.acc_keys * (vec ? row / 4 : row);
-  if (n <= 0) return cudaSuccess;
-  int64_t blocks = (n + kThreads - 1) / kThreads;
+  const int64_t nrows = p.B * p.acc_keys;  // one warp per key row
+  if (nrows <= 0 || row <= 0) return cudaSuccess;
+  int64_t blocks = (nrows + kThreads / 32 - 1) / (kThreads / 32);
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (vec)
     msda_compact_cast_kernel<T, 4><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(

@@ -78,34 +78,61 @@ class MSDAFusedFn(torch.autograd.Function):
     def backward(ctx, grad_output):
         value, shapes, ref, off, lg = ctx.saved_tensors
         ndim, on_dev, clamp, eps, ref_dt, off_dt, lg_dt, lg_shape = ctx.meta
-        go = grad_output.to(value.dtype).contiguous()
-        B, K, H, C = value.shape
-        _, Q, _, L, P, _ = off.shape
-        lib = _lib.lib()
-        ws_bytes = lib.msda_fused_bwd_workspace_bytes(ndim, _core._DTYPE_CODE[value.dtype], B, K,
-                                                      H, C, shapes.data_ptr(), int(on_dev), L, Q,
-                                                      P)
-        ws = torch.empty((ws_bytes,), device=value.device, dtype=torch.uint8) if ws_bytes else None
-        g_value = torch.empty_like(value)
-        g_off = torch.empty_like(off)
-        g_lg = torch.empty_like(lg)
-        partial = torch.empty((B, Q, H, L, ndim), device=value.device, dtype=torch.float32)
-        fn = lib.msda2d_fused_bwd if ndim == 2 else lib.msda3d_fused_bwd
-        with torch.cuda.device(value.device):
-            code = fn(*_args(value, shapes, on_dev, ref, off, lg), int(clamp), eps,
-                      go.data_ptr(), g_value.data_ptr(), partial.data_ptr(), g_off.data_ptr(),
-                      g_lg.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes,
-                      _core._stream_ptr(value.device))
-        _core.check_status(code)
-        g_ref = partial.sum(dim=2).to(ref_dt)
-        return (None, g_value, None, g_ref, g_off.to(off_dt), g_lg.to(lg_dt).reshape(lg_shape),
-                None, None)
+        g_value, g_ref, g_off, g_lg = _backward(ndim, grad_output, value, shapes, on_dev, ref,
+                                                off, lg, clamp, eps)
+        return (None, g_value, None, g_ref.to(ref_dt), g_off.to(off_dt),
+                g_lg.to(lg_dt).reshape(lg_shape), None, None)
+
+
+def _backward(ndim, grad_output, value, shapes, on_dev, ref, off, lg, clamp, eps):
+    """Launch the fused backward on prepared tensors; returns (grad_value,
+    grad_reference_points fp32, grad_offsets, grad_logits (B,Q,H,L,P))."""
+    go = grad_output.to(value.dtype).contiguous()
+    B, K, H, C = value.shape
+    _, Q, _, L, P, _ = off.shape
+    lib = _lib.lib()
+    ws_bytes = lib.msda_fused_bwd_workspace_bytes(ndim, _core._DTYPE_CODE[value.dtype], B, K,
+                                                  H, C, shapes.data_ptr(), int(on_dev), L, Q,
+                                                  P)
+    ws = torch.empty((ws_bytes,), device=value.device, dtype=torch.uint8) if ws_bytes else None
+    g_value = torch.empty_like(value)
+    g_off = torch.empty_like(off)
+    g_lg = torch.empty_like(lg)
+    partial = torch.empty((B, Q, H, L, ndim), device=value.device, dtype=torch.float32)
+    fn = lib.msda2d_fused_bwd if ndim == 2 else lib.msda3d_fused_bwd
+    with torch.cuda.device(value.device):
+        code = fn(*_args(value, shapes, on_dev, ref, off, lg), int(clamp), eps,
+                  go.data_ptr(), g_value.data_ptr(), partial.data_ptr(), g_off.data_ptr(),
+                  g_lg.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes,
+                  _core._stream_ptr(value.device))
+    _core.check_status(code)
+    return g_value, partial.sum(dim=2), g_off, g_lg
+
+
+def fused_backward(ndim, grad_output, value, spatial_shapes, reference_points, sampling_offsets,
+                   attention_logits, clamp_grid, clamp_eps):
+    """The backward of msda{2,3}d_fused as a function of its inputs (the
+    torch.library op's implementation): gradients in the inputs' dtypes and
+    shapes."""
+    shapes, on_dev, ref, off, lg = _prepare(ndim, value, spatial_shapes, reference_points,
+                                            sampling_offsets, attention_logits)
+    g_value, g_ref, g_off, g_lg = _backward(ndim, grad_output, value.contiguous(), shapes, on_dev,
+                                            ref, off, lg, bool(clamp_grid), float(clamp_eps))
+    return (g_value, g_ref.to(reference_points.dtype), g_off.to(sampling_offsets.dtype),
+            g_lg.to(attention_logits.dtype).reshape(attention_logits.shape))
 
 
 def _fused(ndim, value, value_spatial_shapes, reference_points, sampling_offsets,
            attention_logits, clamp_grid, clamp_eps):
     if not value.is_cuda:
         raise ValueError(f"MSDA{ndim}D CUDA kernel requires CUDA tensors. Got CPU tensors instead.")
+    if torch.compiler.is_compiling():
+        from msda_triton_b200 import ops
+
+        # traced as one opaque op (msda_b200::msda_fused_forward), no graph break
+        return ops.msda_fused_forward(value, value_spatial_shapes, reference_points,
+                                      sampling_offsets, attention_logits, ndim, clamp_grid,
+                                      clamp_eps)
     return MSDAFusedFn.apply(ndim, value, value_spatial_shapes, reference_points,
                              sampling_offsets, attention_logits, clamp_grid, clamp_eps)
 

@@ -80,3 +80,64 @@ msda_forward.register_autograd(_backward, setup_context=_setup_context)
 
 
 __all__ = ["msda_forward", "msda_backward"]
+
+
+# ---------------------------------------------------------------- fused prologue
+@torch.library.custom_op("msda_b200::msda_fused_forward", mutates_args=())
+def msda_fused_forward(value: Tensor, spatial_shapes: Tensor, reference_points: Tensor,
+                       sampling_offsets: Tensor, attention_logits: Tensor, ndim: int,
+                       clamp_grid: bool, clamp_eps: float) -> Tensor:
+    """(B, Q, H*C) output of msda{2,3}d_fused (locations and weights formed in the kernels)."""
+    from msda_triton_b200 import fused
+
+    with torch.no_grad():
+        return fused.MSDAFusedFn.apply(ndim, value, spatial_shapes, reference_points,
+                                       sampling_offsets, attention_logits, clamp_grid, clamp_eps)
+
+
+@msda_fused_forward.register_fake
+def _msda_fused_forward_fake(value, spatial_shapes, reference_points, sampling_offsets,
+                             attention_logits, ndim, clamp_grid, clamp_eps):
+    B, _, H, C = value.shape
+    return value.new_empty((B, sampling_offsets.shape[1], H * C))
+
+
+@torch.library.custom_op("msda_b200::msda_fused_backward", mutates_args=())
+def msda_fused_backward(grad_output: Tensor, value: Tensor, spatial_shapes: Tensor,
+                        reference_points: Tensor, sampling_offsets: Tensor,
+                        attention_logits: Tensor, ndim: int, clamp_grid: bool,
+                        clamp_eps: float) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """(grad_value, grad_reference_points, grad_sampling_offsets,
+    grad_attention_logits), each in the dtype and shape of its input."""
+    from msda_triton_b200 import fused
+
+    return fused.fused_backward(ndim, grad_output, value, spatial_shapes, reference_points,
+                                sampling_offsets, attention_logits, clamp_grid, clamp_eps)
+
+
+@msda_fused_backward.register_fake
+def _msda_fused_backward_fake(grad_output, value, spatial_shapes, reference_points,
+                              sampling_offsets, attention_logits, ndim, clamp_grid, clamp_eps):
+    fmt = torch.contiguous_format
+    return tuple(torch.empty_like(t, memory_format=fmt)
+                 for t in (value, reference_points, sampling_offsets, attention_logits))
+
+
+def _fused_setup_context(ctx, inputs, output):
+    value, spatial_shapes, ref, off, logits, ndim, clamp_grid, clamp_eps = inputs
+    ctx.save_for_backward(value, spatial_shapes, ref, off, logits)
+    ctx.ndim = ndim
+    ctx.clamp_grid = clamp_grid
+    ctx.clamp_eps = clamp_eps
+
+
+def _fused_backward(ctx, grad_output):
+    value, spatial_shapes, ref, off, logits = ctx.saved_tensors
+    gv, gr, go, gl = msda_fused_backward(grad_output.contiguous(), value, spatial_shapes, ref,
+                                         off, logits, ctx.ndim, ctx.clamp_grid, ctx.clamp_eps)
+    return gv, None, gr, go, gl, None, None, None
+
+
+msda_fused_forward.register_autograd(_fused_backward, setup_context=_fused_setup_context)
+
+__all__ += ["msda_fused_forward", "msda_fused_backward"]

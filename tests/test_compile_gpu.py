@@ -102,3 +102,31 @@ def test_cuda_graph_capture_and_replay(ndim, dtype):
         assert torch.equal(static[i], eager[i])
     tol = 1e-5 if dtype == torch.float32 else 1e-2
     torch.testing.assert_close(static[1], eager[1], rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("ndim", [2, 3])
+def test_fused_opcheck_and_compile(ndim):
+    """The fused-prologue ops: opcheck, and a compiled module-like step with
+    fullgraph=True against eager."""
+    value, shp, loc, attn, go = _inputs(ndim, seed=9)
+    B, Q, H, L, P, _ = loc.shape
+    g = torch.Generator(device=DEV).manual_seed(1)
+    ref = torch.rand(B, Q, L, ndim, generator=g, device=DEV)
+    off = torch.randn(B, Q, H, L, P, ndim, generator=g, device=DEV)
+    logits = torch.randn(B, Q, H, L * P, generator=g, device=DEV)
+    args = [t.clone().requires_grad_(True) for t in (value, ref, off, logits)]
+    torch.library.opcheck(ops.msda_fused_forward, (args[0], shp, *args[1:], ndim, True, 1e-4))
+    fused = M.msda3d_fused if ndim == 3 else M.msda2d_fused
+
+    def step(v, r, o, lg):
+        return (fused(v, shp, r, o, lg) * go).sum()
+
+    def grads(f):
+        xs = [t.clone().requires_grad_(True) for t in (value, ref, off, logits)]
+        loss = f(*xs)
+        return [loss.detach(), *torch.autograd.grad(loss, xs)]
+
+    eager = grads(step)
+    compiled = grads(torch.compile(step, fullgraph=True, backend="aot_eager"))
+    for e, c in zip(eager, compiled):
+        torch.testing.assert_close(c, e, rtol=1e-5, atol=1e-5)

@@ -12,8 +12,8 @@ import msda_triton_b200.ops  # noqa: F401  (registers the ops)
 
 
 def test_ops_registered():
-    assert hasattr(torch.ops.msda_b200, "msda_forward")
-    assert hasattr(torch.ops.msda_b200, "msda_backward")
+    for name in ("msda_forward", "msda_backward", "msda_fused_forward", "msda_fused_backward"):
+        assert hasattr(torch.ops.msda_b200, name)
 
 
 @pytest.mark.parametrize("ndim", [2, 3])
@@ -33,3 +33,22 @@ def test_fake_shapes(ndim, vdt, sdt):
                                                        1e-4)
         for g, ref in ((gv, value), (gl, loc), (ga, attn)):
             assert g.shape == ref.shape and g.dtype == ref.dtype and g.is_contiguous()
+
+
+@pytest.mark.parametrize("ndim", [2, 3])
+def test_fused_fake_shapes(ndim):
+    B, K, H, C, Q, L, P = 2, 84, 4, 16, 37, 2, 3
+    with FakeTensorMode():
+        value = torch.empty(B, K, H, C, device="cuda", dtype=torch.bfloat16)
+        shapes = torch.empty(L, ndim, dtype=torch.int64)
+        ref = torch.empty(B, Q, L, ndim, device="cuda", dtype=torch.float32)
+        off = torch.empty(B, Q, H, L, P, ndim, device="cuda", dtype=torch.bfloat16)
+        logits = torch.empty(B, Q, H, L * P, device="cuda", dtype=torch.bfloat16)
+        out = torch.ops.msda_b200.msda_fused_forward(value, shapes, ref, off, logits, ndim, True,
+                                                     1e-4)
+        assert out.shape == (B, Q, H * C) and out.dtype == torch.bfloat16
+        go = torch.empty(B, Q, H * C, device="cuda", dtype=torch.bfloat16)
+        grads = torch.ops.msda_b200.msda_fused_backward(go, value, shapes, ref, off, logits, ndim,
+                                                        True, 1e-4)
+        for g, t in zip(grads, (value, ref, off, logits)):
+            assert g.shape == t.shape and g.dtype == t.dtype
