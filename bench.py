@@ -527,6 +527,75 @@ def run_reference_triton(args, wl, rank, world, local_rank):
     }
 
 
+# ---------------------------------------------------------------- query sharding
+def run_query_sharded(args, wl, rank, world, local_rank):
+    """BASELINE config 4 at a batch smaller than the GPU count: every rank holds
+    the whole value and a block of the queries; the backward sums the fp32
+    partial value gradients with an NCCL reduce-scatter and gathers the
+    rounded shards (all-gather in value's dtype).  Total work is fixed
+    (strong scaling); time is the max over ranks of CUDA-event times."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from msda_triton_b200.sharding import msda_query_sharded, query_shard
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    else:  # one rank: no collective, the rest of the path is the same
+        dist.init_process_group("nccl", init_method="tcp://127.0.0.1:29533", rank=0,
+                                world_size=1, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+    value, shapes, loc, attn, go = make_inputs(wl, dev, seed=1234)  # the same on every rank
+    sl = query_shard(wl["Q"], rank, world)
+    v = value.requires_grad_(True)
+    lo = loc[:, sl].contiguous().requires_grad_(True)
+    a = attn[:, sl].contiguous().requires_grad_(True)
+    g = go[:, sl].contiguous()
+    group = dist.group.WORLD
+
+    def step():
+        out = msda_query_sharded(wl["ndim"], v, shapes, lo, a, group=group)
+        torch.autograd.grad(out, (v, lo, a), g)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return None
+    B, K, H, C, Q, L, P = dims(wl)
+    samples = algorithmic_bytes(wl)["samples"]
+    return {"metric": "MSDA fwd+bwd Gsamples/s", "value": samples / (ms * 1e-3) / 1e9,
+            "unit": "Gsamples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": DTYPE_NAME[wl["dtype"]], "data": "synthetic (seeded)",
+            "config": {"workload": args.workload, "batch": B, "num_queries": Q,
+                       "parallelism": f"query-sharded over {world} GPU(s), value replicated; "
+                                      "grad_value: fp32 NCCL reduce-scatter + all-gather in "
+                                      "the value dtype",
+                       "collective_bytes_per_rank": (
+                           B * K * H * C * (4 + value.element_size()) * (world - 1) // world)}}
+
+
 # ---------------------------------------------------------------- module workloads
 def run_module(args, wl, rank, world, local_rank):
     """One fwd+bwd step of the nn.Module (ours, or the reference's own module
@@ -675,6 +744,9 @@ def main():
     ap.add_argument("--workload", default="3d_xl_bf16", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-triton"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard", default="batch", choices=["batch", "query"],
+                    help="batch: one instance of the workload per GPU (weak scaling); query: "
+                         "one instance split by queries across the GPUs (strong scaling)")
     ap.add_argument("--batch", type=int, default=0,
                     help="per-GPU batch override (a smaller case of the workload, for profiling)")
     args = ap.parse_args()
@@ -686,7 +758,9 @@ def main():
     wl = dict(WORKLOADS[args.workload])
     if args.batch > 0:
         wl["B"] = args.batch
-    if wl.get("module"):
+    if args.shard == "query" and args.impl == "ours" and not wl.get("module"):
+        res = run_query_sharded(args, wl, rank, world, local_rank)
+    elif wl.get("module"):
         res = run_module(args, wl, rank, world, local_rank) if rank == 0 else None
     elif args.impl == "reference":
         res = run_reference(args, wl, rank)

@@ -1,7 +1,7 @@
 """Multi-GPU runs of the CUDA path (NCCL, one process per GPU): needs >= 2 GPUs.
 
 * query sharding: every rank holds the whole value and a block of queries;
-  its output block, its location/weight gradient block and the all-reduced
+  its output block, its location/weight gradient block and the reduced
   value gradient must match one single-GPU run of the whole problem;
 * batch sharding: independent slices -- the concatenated outputs equal the
   single-GPU run bitwise.

@@ -2,7 +2,8 @@
 
 The compute is injected: a CPU backend built on the oracle stands in for the
 CUDA kernels, so these tests check what the sharding layer itself does --
-query/batch partition, the fp32 all_reduce of the partial value gradients,
+query/batch partition, the fp32 reduce-scatter and all-gather of the partial
+value gradients,
 gradient routing through autograd -- against a single-process oracle run.
 They also check that a rank that disappears turns into an error on the
 surviving rank (process-group timeout), not a hang.
@@ -146,7 +147,7 @@ def _lost_rank_worker(rank, world, port, q):
         out = msda_query_sharded(2, v, shp, loc[:, sl], attn[:, sl], backend=OracleBackend)
         if rank == 1:
             # This rank fails between steps: it never joins the backward's
-            # all_reduce and exits.
+            # collectives and exits.
             _report_and_exit(q, rank, "left")
         try:
             out.backward(go[:, sl])
