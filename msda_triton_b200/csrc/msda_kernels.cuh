@@ -27,26 +27,6 @@ struct Point {
   bool pass[3];
 };
 
-template <int NDIM>
-__device__ __forceinline__ void corner_coords(const Point<NDIM>& pt, int c, const int32_t* sz,
-                                              int32_t start, bool& valid, int32_t& key,
-                                              float& w) {
-  const int32_t xi = pt.i0[0] + (c & 1);
-  const int32_t yi = pt.i0[1] + ((c >> 1) & 1);
-  const int32_t zi = (NDIM == 3) ? pt.i0[2] + ((c >> 2) & 1) : 0;
-  valid = static_cast<uint32_t>(xi) < static_cast<uint32_t>(sz[0]) &&
-          static_cast<uint32_t>(yi) < static_cast<uint32_t>(sz[1]);
-  if (NDIM == 3) valid = valid && static_cast<uint32_t>(zi) < static_cast<uint32_t>(sz[2]);
-  key = start + (zi * sz[1] + yi) * sz[0] + xi;
-  const float wx = (c & 1) ? pt.f[0] : __fsub_rn(1.0f, pt.f[0]);
-  const float wy = (c & 2) ? pt.f[1] : __fsub_rn(1.0f, pt.f[1]);
-  w = __fmul_rn(wx, wy);
-  if (NDIM == 3) {
-    const float wz = (c & 4) ? pt.f[2] : __fsub_rn(1.0f, pt.f[2]);
-    w = __fmul_rn(w, wz);
-  }
-}
-
 // d(weight of corner c)/d(source index) along each axis.
 template <int NDIM>
 __device__ __forceinline__ void corner_dweights(const Point<NDIM>& pt, int c, float* dw) {
