@@ -26,6 +26,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import torch
@@ -116,7 +117,7 @@ class ClockSampler:
     def __init__(self, gpus):
         self.gpus = gpus
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        self.path = os.path.join(tempfile.gettempdir(), f"msda_bench_clocks_{os.getpid()}.csv")
 
     def __enter__(self):
         try:
