@@ -351,7 +351,8 @@ def run_ours(args, wl, rank, world, local_rank):
         "clocks": clk.summary(),
         "e2e": e2e,
     }
-    res["cpu_baseline"] = cpu_baseline(args, wl)
+    # the CPU baseline is a single-GPU figure: rank 0 at N=1 only
+    res["cpu_baseline"] = cpu_baseline(args, wl) if world == 1 else None
     return res
 
 
