@@ -376,12 +376,18 @@ def run_e2e(args, wl, fn, dev, shapes, value, loc, attn, go, fwd_only, dist):
     kernels of step i, with two device slots for the inputs; CUDA events
     order every copy against the compute that reads or writes its buffer."""
     n_in = 3 if fwd_only else 4
-    host_in = [t.detach().cpu().pin_memory() for t in (value, loc, attn, go)[:n_in]]
+    # pinned host copies made directly (no pageable intermediate: 8 ranks on
+    # one host each hold these)
+    host_in = []
+    for t in (value, loc, attn, go)[:n_in]:
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        h.copy_(t.detach())
+        host_in.append(h)
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     B, K, H, C, Q, L, P = dims(wl)
     outs_shape = [(B, Q, H * C)] + ([] if fwd_only else [tuple(value.shape), tuple(loc.shape),
                                                          tuple(attn.shape)])
-    host_out = [torch.empty(s, dtype=wl["dtype"]).pin_memory() for s in outs_shape]
+    host_out = [torch.empty(s, dtype=wl["dtype"], pin_memory=True) for s in outs_shape]
     d2h = sum(t.numel() * t.element_size() for t in host_out)
     comp = torch.cuda.current_stream(dev)
     s_in = torch.cuda.Stream(dev)
