@@ -203,6 +203,7 @@ template <> struct Chunk<__half, 2> {
 struct LevelSmem {
   int32_t size[kMaxLevels][3];
   int32_t start[kMaxLevels];
+  float rcp[kMaxLevels][3];  // 1 / size rounded to nearest (fused prologue only)
 };
 
 // Fill the CTA's level table.  Host-resolved tables are copied.  Device
@@ -238,6 +239,14 @@ __device__ __forceinline__ void load_levels(const Problem& p, LevelSmem& s, int 
       }
     }
   }
+  __syncthreads();
+}
+
+// The reciprocals of the level sizes for the fused prologue's divisions,
+// once per CTA (after load_levels).
+__device__ __forceinline__ void load_level_rcps(const Problem& p, LevelSmem& s) {
+  const int t = static_cast<int>(threadIdx.x);
+  if (t < p.L * 3) s.rcp[t / 3][t % 3] = __frcp_rn(static_cast<float>(s.size[t / 3][t % 3]));
   __syncthreads();
 }
 

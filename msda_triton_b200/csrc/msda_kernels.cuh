@@ -82,12 +82,12 @@ struct LevelRcp {
 };
 
 template <int NDIM>
-__device__ __forceinline__ LevelRcp<NDIM> level_rcp(const int32_t* sz) {
+__device__ __forceinline__ LevelRcp<NDIM> level_rcp(const int32_t* sz, const float* rcp) {
   LevelRcp<NDIM> lr;
 #pragma unroll
   for (int a = 0; a < 3; ++a) {
     lr.n[a] = static_cast<float>(sz[a]);
-    lr.r[a] = __frcp_rn(lr.n[a]);
+    lr.r[a] = rcp[a];
   }
   return lr;
 }
@@ -230,6 +230,7 @@ template <typename T, typename TS, int NDIM, int VB, int VPL, bool FUSED>
 __device__ __forceinline__ void msda_fwd_body(const Problem p, T* __restrict__ out) {
   __shared__ LevelSmem lv;
   load_levels(p, lv, NDIM);
+  if constexpr (FUSED) load_level_rcps(p, lv);
 
   using CK = Chunk<T, VB>;
   constexpr int EPV = CK::EPV;
@@ -285,7 +286,7 @@ __device__ __forceinline__ void msda_fwd_body(const Problem p, T* __restrict__ o
     LevelRcp<NDIM> lr;
     float rl[3];
     if constexpr (FUSED) {
-      lr = level_rcp<NDIM>(g.sz);
+      lr = level_rcp<NDIM>(g.sz, lv.rcp[l]);
 #pragma unroll
       for (int ax = 0; ax < NDIM; ++ax) rl[ax] = rrow[l * NDIM + ax];
     }
@@ -441,6 +442,7 @@ __device__ __forceinline__ void msda_bwd_body(const Problem p, const T* __restri
                                               TS* __restrict__ grad_attn) {
   __shared__ LevelSmem lv;
   load_levels(p, lv, NDIM);
+  if constexpr (FUSED) load_level_rcps(p, lv);
 
   using CK = Chunk<T, VB>;
   constexpr int EPV = CK::EPV;
@@ -506,7 +508,7 @@ __device__ __forceinline__ void msda_bwd_body(const Problem p, const T* __restri
     LevelRcp<NDIM> lr;
     float rl[3];
     if constexpr (FUSED) {
-      lr = level_rcp<NDIM>(g.sz);
+      lr = level_rcp<NDIM>(g.sz, lv.rcp[l]);
 #pragma unroll
       for (int ax = 0; ax < NDIM; ++ax) rl[ax] = rrow[l * NDIM + ax];
     }
