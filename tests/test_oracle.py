@@ -108,3 +108,52 @@ def test_oracle_rejects_inconsistent_k():
     value, shp, loc, attn, _ = make_inputs(1, 2, 1, 4, 1, [(4, 4)], seed=1)
     with pytest.raises(ValueError):
         msda_fwd_oracle(value[:, :15], shp, loc, attn)
+
+
+@pytest.mark.parametrize("ndim,shapes", [(2, [(6, 7), (3, 4)]), (3, [(4, 5, 6), (2, 3, 3)])])
+def test_gradients_are_derivatives_of_the_forward(ndim, shapes):
+    """Central differences of the oracle's forward against its backward, a
+    check independent of the golden vectors: with S(x) = <grad_out, out(x)>,
+    every gradient the backward returns must be dS/dx.  Locations sit at
+    cell fractions in [0.25, 0.75] so each +-h step stays inside its cell,
+    where the interpolation is linear along the stepped axis."""
+    rng = np.random.default_rng(17)
+    B, Q, H, C, P = 1, 4, 2, 3, 2
+    L = len(shapes)
+    K = int(sum(np.prod(s) for s in shapes))
+    value = rng.standard_normal((B, K, H, C)).astype(np.float32)
+    attn = rng.uniform(0.2, 1.0, (B, Q, H, L, P)).astype(np.float32)
+    go = rng.standard_normal((B, Q, H * C)).astype(np.float32)
+    loc = np.empty((B, Q, H, L, P, ndim), dtype=np.float32)
+    for lvl, s in enumerate(shapes):
+        for ax in range(ndim):
+            n = s[ndim - 1 - ax]  # axis 0 is x (W-indexed), the last shapes entry
+            cell = rng.integers(0, n - 1, (B, Q, H, P))
+            frac = rng.uniform(0.25, 0.75, (B, Q, H, P))
+            loc[:, :, :, lvl, :, ax] = (cell + frac + 0.5) / n  # ix = loc * n - 0.5
+    shp = np.array(shapes, dtype=np.int64)
+    gv, gl, ga = msda_bwd_oracle(value, shp, loc, attn, go)
+
+    def score(v=value, lo=loc, a=attn):
+        return float(np.dot(msda_fwd_oracle(v, shp, lo, a).ravel().astype(np.float64),
+                            go.ravel().astype(np.float64)))
+
+    def central(array, idx, h, **which):
+        up, dn = array.copy(), array.copy()
+        up[idx] += h
+        dn[idx] -= h
+        key = next(iter(which))
+        return (score(**{key: up}) - score(**{key: dn})) / (2 * h)
+
+    for _ in range(8):
+        b, q, hh, lvl, p = (int(rng.integers(0, m)) for m in (B, Q, H, L, P))
+        for ax in range(ndim):
+            n = shapes[lvl][ndim - 1 - ax]
+            idx = (b, q, hh, lvl, p, ax)
+            fd = central(loc, idx, 0.1 / n, lo=loc)
+            np.testing.assert_allclose(gl[idx], fd, rtol=2e-2, atol=2e-3)
+        idx = (b, q, hh, lvl, p)
+        np.testing.assert_allclose(ga[idx], central(attn, idx, 0.05, a=attn), rtol=1e-2, atol=1e-3)
+        idx = (0, int(rng.integers(0, K)), hh, int(rng.integers(0, C)))
+        np.testing.assert_allclose(gv[idx], central(value, idx, 0.05, v=value), rtol=1e-2,
+                                   atol=1e-3)
