@@ -10,7 +10,6 @@ gradients 1e-4, fp16/bf16 2e-2 against an fp32 reference on the same
 
 from __future__ import annotations
 
-import numpy as np
 import pytest
 import torch
 
