@@ -565,7 +565,8 @@ def run_query_sharded(args, wl, rank, world, local_rank):
     group = dist.group.WORLD
 
     def step():
-        out = msda_query_sharded(wl["ndim"], v, shapes, lo, a, group=group)
+        out = msda_query_sharded(wl["ndim"], v, shapes, lo, a, group=group,
+                                 reduce_dtype=args.reduce_dtype)
         torch.autograd.grad(out, (v, lo, a), g)
 
     stream = torch.cuda.current_stream(dev)
@@ -592,16 +593,22 @@ def run_query_sharded(args, wl, rank, world, local_rank):
         return None
     B, K, H, C, Q, L, P = dims(wl)
     samples = algorithmic_bytes(wl)["samples"]
+    e = value.element_size()
+    if args.reduce_dtype == "value":
+        how = f"grad_value: one NCCL all_reduce of the partial gradients in {DTYPE_NAME[wl['dtype']]}"
+        coll = 2 * B * K * H * C * e * (world - 1) // world
+    else:
+        how = ("grad_value: fp32 NCCL reduce-scatter + all-gather in the value dtype")
+        coll = B * K * H * C * (4 + e) * (world - 1) // world
     return {"metric": "MSDA fwd+bwd Gsamples/s", "value": samples / (ms * 1e-3) / 1e9,
             "unit": "Gsamples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": DTYPE_NAME[wl["dtype"]], "data": "synthetic (seeded)",
             "config": {"workload": args.workload, "batch": B, "num_queries": Q,
                        "parallelism": f"query-sharded over {world} GPU(s), value replicated; "
-                                      "grad_value: fp32 NCCL reduce-scatter + all-gather in "
-                                      "the value dtype",
-                       "collective_bytes_per_rank": (
-                           B * K * H * C * (4 + value.element_size()) * (world - 1) // world)}}
+                                      + how,
+                       "reduce_dtype": args.reduce_dtype,
+                       "collective_bytes_per_rank": coll}}
 
 
 # ---------------------------------------------------------------- module workloads
@@ -755,6 +762,9 @@ def main():
     ap.add_argument("--shard", default="batch", choices=["batch", "query"],
                     help="batch: one instance of the workload per GPU (weak scaling); query: "
                          "one instance split by queries across the GPUs (strong scaling)")
+    ap.add_argument("--reduce-dtype", default="float32", choices=["float32", "value"],
+                    help="--shard query: sum the partial value gradients in fp32 (reduce-scatter "
+                         "+ all-gather, one rounding) or in the value dtype (one all_reduce)")
     ap.add_argument("--batch", type=int, default=0,
                     help="per-GPU batch override (a smaller case of the workload, for profiling)")
     args = ap.parse_args()

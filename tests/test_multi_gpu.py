@@ -68,6 +68,18 @@ def _worker(rank, world, port, ndim, dtype_name, q):
         torch.testing.assert_close(ga, ga_ref[:, sl], rtol=tol, atol=tol)
         torch.testing.assert_close(gv.float(), gv_ref.float(), rtol=tol, atol=tol)
 
+        # query sharding, partial value gradients in value's dtype summed by
+        # one all_reduce: the same bar (one extra rounding per rank)
+        v3 = value.clone().requires_grad_(True)
+        lo3 = loc[:, sl].clone().requires_grad_(True)
+        a3 = attn[:, sl].clone().requires_grad_(True)
+        out3 = msda_query_sharded(ndim, v3, shp, lo3, a3, reduce_dtype="value")
+        gv3, gl3, ga3 = torch.autograd.grad(out3, (v3, lo3, a3), go[:, sl])
+        assert torch.equal(out3, out_ref[:, sl]), "query-sharded forward differs"
+        torch.testing.assert_close(gl3, gl_ref[:, sl], rtol=tol, atol=tol)
+        torch.testing.assert_close(ga3, ga_ref[:, sl], rtol=tol, atol=tol)
+        torch.testing.assert_close(gv3.float(), gv_ref.float(), rtol=tol, atol=tol)
+
         # batch sharding: each rank runs its slice; gather and compare bitwise
         bs = batch_shard(B, rank, world)
         out_b = fn(value[bs], shp, loc[bs], attn[bs])

@@ -41,6 +41,14 @@ class OracleBackend:
                                                 clamp, eps))
 
     @staticmethod
+    def backward(ndim, value, shapes, on_dev, loc, attn, clamp, eps, go):
+        gv, gl, ga = msda_bwd_oracle(value.detach().numpy(), shapes.numpy(),
+                                     loc.detach().numpy(), attn.detach().numpy(),
+                                     go.detach().numpy(), clamp, eps)
+        return (torch.from_numpy(gv).to(value.dtype), torch.from_numpy(gl),
+                torch.from_numpy(ga))
+
+    @staticmethod
     def backward_accumulate(ndim, value, shapes, on_dev, loc, attn, clamp, eps, go, acc):
         gv, gl, ga = msda_bwd_oracle(value.detach().numpy(), shapes.numpy(),
                                      loc.detach().numpy(), attn.detach().numpy(),
@@ -66,7 +74,7 @@ def _init(rank, world, port, timeout_s=60):
                             timeout=datetime.timedelta(seconds=timeout_s))
 
 
-def _query_sharded_worker(rank, world, port, ndim, q):
+def _query_sharded_worker(rank, world, port, ndim, reduce_dtype, q):
     try:
         _init(rank, world, port)
         shapes = [(12, 20), (6, 10)] if ndim == 2 else [(6, 8, 10), (3, 4, 5)]
@@ -76,7 +84,8 @@ def _query_sharded_worker(rank, world, port, ndim, q):
         v = value.clone().requires_grad_(True)
         lo = loc[:, sl].clone().requires_grad_(True)
         a = attn[:, sl].clone().requires_grad_(True)
-        out = msda_query_sharded(ndim, v, shp, lo, a, backend=OracleBackend)
+        out = msda_query_sharded(ndim, v, shp, lo, a, backend=OracleBackend,
+                                 reduce_dtype=reduce_dtype)
         out.backward(go[:, sl])
         # Reference: the whole problem in one process.
         ref_out = msda_fwd_oracle(value, shp, loc, attn)
@@ -110,10 +119,17 @@ def _run(target, args, world=2, timeout=120):
     return results
 
 
+@pytest.mark.parametrize("reduce_dtype", ["float32", "value"])
 @pytest.mark.parametrize("ndim", [2, 3])
-def test_query_sharded_matches_single_process(ndim):
-    results = _run(_query_sharded_worker, (ndim,))
+def test_query_sharded_matches_single_process(ndim, reduce_dtype):
+    # fp32 values: both reductions sum fp32 partials, so both match one process
+    results = _run(_query_sharded_worker, (ndim, reduce_dtype))
     assert results == {0: "ok", 1: "ok"}, results
+
+
+def test_query_sharded_rejects_unknown_reduce_dtype():
+    with pytest.raises(ValueError, match="reduce_dtype"):
+        msda_query_sharded(3, torch.zeros(1), None, None, None, reduce_dtype="fp8")
 
 
 def test_shard_slices_cover_everything():
