@@ -156,3 +156,41 @@ def test_shape_row_order(ndim):
     K = int(np.prod(shapes[0]))
     assert _fwd(ndim=ndim, K=K, shapes=shapes, Q=0) == _lib.SUCCESS
     assert _fwd(ndim=ndim, K=K + 1, shapes=shapes, Q=0) == _lib.ERROR_SHAPE_MISMATCH
+
+
+def _fused_fwd(ndim=3, ref=FAKE, Q=3, **kw):
+    lib = _lib.lib()
+    shapes = kw.get("shapes", ((2, 3, 4),) if ndim == 3 else ((4, 5),))
+    shp = np.ascontiguousarray(np.array(shapes, dtype=np.int32))
+    K = int(sum(np.prod(s) for s in shapes))
+    fn = lib.msda3d_fused_fwd if ndim == 3 else lib.msda2d_fused_fwd
+    return fn(FAKE, _lib.BFLOAT16, 1, K, 2, 8, shp.ctypes.data, 0, len(shapes), ref, FAKE, FAKE,
+              _lib.BFLOAT16, Q, 2, 1, 1e-4, FAKE, None)
+
+
+@pytest.mark.parametrize("ndim", [2, 3])
+def test_fused_entries_validate_reference_points(ndim):
+    assert _fused_fwd(ndim, ref=None) == _lib.ERROR_INVALID_ARGUMENT
+    assert "reference_points" in _lib.last_error()
+    assert _fused_fwd(ndim, ref=FAKE + 2) == _lib.ERROR_MISALIGNED
+    assert _fused_fwd(ndim, ref=None, Q=0) == _lib.SUCCESS  # nothing to sample: no pointer needed
+
+
+def test_fused_workspace_is_the_gather_plan(monkeypatch):
+    # The fused backward always takes the gather/scatter path, so its
+    # workspace is the gather plan's, whatever MSDA_BWD_PATH says.
+    lib = _lib.lib()
+    B, H, C, Q, P = 2, 8, 32, 20000, 4
+    shapes = [(32, 64, 64), (16, 32, 32), (8, 16, 16)]
+    shp = np.ascontiguousarray(np.array(shapes, dtype=np.int32))
+    K = int(sum(np.prod(s) for s in shapes))
+
+    def fused():
+        return lib.msda_fused_bwd_workspace_bytes(3, _lib.BFLOAT16, B, K, H, C, shp.ctypes.data,
+                                                  0, len(shapes), Q, P)
+
+    gather = _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P)
+    assert fused() == gather
+    monkeypatch.setenv("MSDA_BWD_PATH", "binned")
+    assert _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P) != gather  # the plain entry switches
+    assert fused() == gather
