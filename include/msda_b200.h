@@ -40,7 +40,8 @@
  * nothing; the backward needs a workspace of msda_bwd_workspace_bytes() bytes
  * (256-byte aligned).  Every call is asynchronous
  * on `stream` (a cudaStream_t; NULL = legacy default stream) and keeps no
- * state between calls, so calls on different streams may run concurrently.
+ * state between calls, so calls on different streams may run concurrently
+ * (except msda_bwd_static_scratch, whose calls share one scratch array).
  * grad_* buffers need no initialisation: they are fully overwritten.
  *
  * Errors: every entry point returns MSDA_SUCCESS (0) or an msda_status code;
