@@ -2,7 +2,8 @@
 
 The library is built in-tree by `python -m msda_triton_b200.build` (or
 __graft_entry__.build()).  There is no fallback: if the library is missing
-or fails to load, every op raises RuntimeError.
+or fails to load, every op raises RuntimeError.  MSDA_B200_LIB=<path>
+selects another build of the same ABI (e.g. the bounds-checked one).
 """
 
 from __future__ import annotations
@@ -11,7 +12,8 @@ import ctypes
 import os
 import threading
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libmsda_b200.so")
+LIB_PATH = os.environ.get("MSDA_B200_LIB") or os.path.join(
+    os.path.dirname(os.path.abspath(__file__)), "_lib", "libmsda_b200.so")
 
 # Status codes (msda_status in include/msda_b200.h).
 SUCCESS = 0

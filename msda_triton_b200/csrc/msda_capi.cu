@@ -7,6 +7,9 @@
 #include <cstring>
 
 #include "../../include/msda_b200.h"
+#ifdef MSDA_CHECKED
+#include "../../include/msda_b200_checked.h"
+#endif
 #include "msda_binned_launch.cuh"
 #include "msda_launch.cuh"
 
@@ -61,6 +64,22 @@ const char* dtype_name(int dt) {
 bool aligned(const void* p, int64_t a) {
   return (reinterpret_cast<uintptr_t>(p) % static_cast<uintptr_t>(a)) == 0;
 }
+
+#ifdef MSDA_CHECKED
+// Checked build: the device word the kernels' bounds checks report into
+// (Problem::check_flag), one per device, looked up once.
+__device__ unsigned int g_check_word;
+unsigned int* check_word() {
+  static unsigned int* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (addr[dev] == nullptr) {
+    void* a = nullptr;
+    if (cudaGetSymbolAddress(&a, g_check_word) == cudaSuccess) addr[dev] = static_cast<unsigned int*>(a);
+  }
+  return addr[dev];
+}
+#endif
 
 struct Args {
   int ndim;
@@ -126,6 +145,11 @@ int prepare(const Args& a, const void* const* bufs, int nbufs, Problem& p, Launc
   p.lo = static_cast<float>(-1.0 + a.eps);
   p.hi = static_cast<float>(1.0 - a.eps);
   p.shapes_dev = nullptr;
+#ifdef MSDA_CHECKED
+  p.check_flag = check_word();
+  if (p.check_flag == nullptr)
+    return fail(MSDA_ERROR_CUDA, "checked build: bounds-check word not available");
+#endif
   if (a.shapes_dev) {
     p.shapes_dev = a.shapes;
   } else {
@@ -861,5 +885,20 @@ const char* msda_status_string(int status) {
 const char* msda_last_error(void) { return msda::g_last_error; }
 
 int msda_abi_version(void) { return MSDA_B200_ABI_VERSION; }
+
+#ifdef MSDA_CHECKED
+// Checked build only (include/msda_b200_checked.h): the bounds-check bits
+// recorded on the current device since the last clear; waits for the device.
+MSDA_API unsigned int msda_checked_violations(int clear) {
+  unsigned int* w = msda::check_word();
+  if (w == nullptr) return 0xffffffffu;
+  unsigned int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return 0xffffffffu;
+  if (clear && cudaMemset(w, 0, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+  return v;
+}
+#endif
 
 }  // extern "C"

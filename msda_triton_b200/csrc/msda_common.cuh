@@ -62,6 +62,10 @@ struct Problem {
   // row's points of each level's location gradient.
   const float* ref;
   float* ref_partial;
+  // Checked build (MSDA_CHECKED): device word whose bits record the gather
+  // and scatter addresses that fell outside their buffers (never set
+  // otherwise; nullptr in the normal build).
+  unsigned int* check_flag;
 };
 
 // ---------------------------------------------------------------- types

@@ -160,6 +160,38 @@ __device__ __forceinline__ float softmax_weight(float x, const RowSoftmax& sm) {
 // zeros instead of selecting per register (the widest row is 2048 bytes).
 static __device__ __align__(16) unsigned char g_zero_row[2048];
 
+// Checked build (-DMSDA_CHECKED): every value gather and value-gradient
+// scatter address is tested against the buffer it must stay inside.  A
+// violation sets a bit in *p.check_flag (1: value gather, 2: 16-bit
+// grad_value scatter, 4: fp32 accumulator scatter) and the access is skipped;
+// nothing traps.  The normal build compiles the plain accesses.
+#ifdef MSDA_CHECKED
+__device__ __forceinline__ bool msda_within(const void* a, int n, const void* base,
+                                            int64_t bytes) {
+  const char* c = static_cast<const char*>(a);
+  const char* b = static_cast<const char*>(base);
+  return b != nullptr && c >= b && c + n <= b + bytes;
+}
+template <typename T>
+__device__ __forceinline__ int64_t msda_value_bytes(const Problem& p) {
+  return p.B * p.K * p.H * p.C * static_cast<int64_t>(sizeof(T));
+}
+template <int VB, typename T>
+__device__ __forceinline__ Raw<VB> checked_ld_value(const char* a, const Problem& p) {
+  if (msda_within(a, VB, p.value, msda_value_bytes<T>(p)) ||
+      msda_within(a, VB, g_zero_row, sizeof(g_zero_row)))
+    return ld_chunk<VB>(a);
+  atomicOr(p.check_flag, 1u);
+  return raw_zero<VB>();
+}
+#define MSDA_LD_VALUE(VB, a) checked_ld_value<VB, T>((a), p)
+#define MSDA_SCATTER_OK(a, n, base, bytes, bit) \
+  (msda_within((a), (n), (base), (bytes)) || (atomicOr(p.check_flag, (bit)), false))
+#else
+#define MSDA_LD_VALUE(VB, a) ld_chunk<VB>(a)
+#define MSDA_SCATTER_OK(a, n, base, bytes, bit) true
+#endif
+
 // Per-level constants of the gather kernels.
 struct LevelGeom {
   int32_t sz[3];
@@ -309,7 +341,7 @@ __device__ __forceinline__ void msda_fwd_body(const Problem p, T* __restrict__ o
       for (int c = 0; c < NC; ++c)
 #pragma unroll
         for (int v = 0; v < VPL; ++v)
-          raw[c][v] = has[v] ? ld_chunk<VB>(cs.valid[c] ? cs.ptr[c] + v * G * VB : cs.ptr[c])
+          raw[c][v] = has[v] ? MSDA_LD_VALUE(VB, cs.valid[c] ? cs.ptr[c] + v * G * VB : cs.ptr[c])
                              : raw_zero<VB>();
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
@@ -547,7 +579,7 @@ __device__ __forceinline__ void msda_bwd_body(const Problem p, const T* __restri
       for (int c = 0; c < NC; ++c)
 #pragma unroll
         for (int v = 0; v < VPL; ++v)
-          raw[c][v] = has[v] ? ld_chunk<VB>(cs.valid[c] ? cs.ptr[c] + v * G * VB : cs.ptr[c])
+          raw[c][v] = has[v] ? MSDA_LD_VALUE(VB, cs.valid[c] ? cs.ptr[c] + v * G * VB : cs.ptr[c])
                              : raw_zero<VB>();
 
       float dots[NC];
@@ -573,12 +605,18 @@ __device__ __forceinline__ void msda_bwd_body(const Problem p, const T* __restri
               for (int e = 0; e < EPV; ++e) t[e] = aw * go[v][e];
               if constexpr (sizeof(T) == 2) {
                 if (d16) {
-                  red_add_16<T, EPV>(reinterpret_cast<T*>(g16lane + vo + v * G * VB), t);
+                  T* dst16 = reinterpret_cast<T*>(g16lane + vo + v * G * VB);
+                  if (MSDA_SCATTER_OK(dst16, EPV * static_cast<int>(sizeof(T)), p.grad_value16,
+                                      p.B * p.K * p.H * p.C * static_cast<int64_t>(sizeof(T)), 2u))
+                    red_add_16<T, EPV>(dst16, t);
                   continue;
                 }
               }
-              red_add_f32<EPV>(reinterpret_cast<float*>(acc_lane + vo * (4 / sizeof(T))) +
-                                   v * G * EPV, t);
+              float* dst32 = reinterpret_cast<float*>(acc_lane + vo * (4 / sizeof(T))) +
+                             v * G * EPV;
+              if (MSDA_SCATTER_OK(dst32, EPV * 4, gacc,
+                                  p.B * p.acc_keys * p.H * p.C * int64_t{4}, 4u))
+                red_add_f32<EPV>(dst32, t);
             }
           }
         }
