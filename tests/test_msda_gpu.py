@@ -233,6 +233,20 @@ def test_empty_queries(ndim):
 
 
 @pytest.mark.parametrize("ndim", [2, 3])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_zero_points_sample_nothing(ndim, dtype):
+    # P = 0: every row is an empty sum -- zero output, zero value gradient,
+    # empty location/weight gradients (as the oracle gives).
+    value, shp, loc, attn, go = make_inputs(2, 30, 4, 16, 0, SHAPES[ndim][:2], seed=7, dtype=dtype)
+    got = cuda_fwd_bwd(ndim, value, shp, loc, attn, go)
+    assert got[0].shape == (2, 30, 64) and torch.count_nonzero(got[0]) == 0
+    assert got[1].shape == value.shape and torch.count_nonzero(got[1]) == 0
+    assert got[2].numel() == 0 and got[3].numel() == 0
+    ref = msda_fwd_oracle(value.float(), shp, loc.float(), attn.float())
+    assert not ref.any()
+
+
+@pytest.mark.parametrize("ndim", [2, 3])
 @pytest.mark.parametrize("dtype,C", [(torch.float32, 3), (torch.float32, 6), (torch.float32, 256),
                                      (torch.float32, 200), (torch.bfloat16, 5), (torch.bfloat16, 6),
                                      (torch.bfloat16, 512), (torch.float16, 96), (torch.float16, 1)])
