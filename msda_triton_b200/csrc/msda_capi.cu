@@ -10,8 +10,8 @@
 #ifdef MSDA_CHECKED
 #include "../../include/msda_b200_checked.h"
 #endif
-#include "msda_binned_launch.cuh"
 #include "msda_launch.cuh"
+#include "msda_sorted_launch.cuh"
 
 namespace msda {
 
@@ -20,11 +20,11 @@ MSDA_DECLARE_PAIR(__half, __half)
 MSDA_DECLARE_PAIR(__half, float)
 MSDA_DECLARE_PAIR(__nv_bfloat16, __nv_bfloat16)
 MSDA_DECLARE_PAIR(__nv_bfloat16, float)
-MSDA_DECLARE_BINNED(float, float)
-MSDA_DECLARE_BINNED(__half, __half)
-MSDA_DECLARE_BINNED(__half, float)
-MSDA_DECLARE_BINNED(__nv_bfloat16, __nv_bfloat16)
-MSDA_DECLARE_BINNED(__nv_bfloat16, float)
+MSDA_DECLARE_SORTED(float, float)
+MSDA_DECLARE_SORTED(__half, __half)
+MSDA_DECLARE_SORTED(__half, float)
+MSDA_DECLARE_SORTED(__nv_bfloat16, __nv_bfloat16)
+MSDA_DECLARE_SORTED(__nv_bfloat16, float)
 
 namespace {
 
@@ -99,6 +99,9 @@ struct Args {
   // reference points (B, Q, L, d)
   const float* ref = nullptr;
   int fused = 0;
+  // keep the backward on the gather/scatter plan (the static-scratch entry:
+  // its workspace bound was set for that plan)
+  bool scatter_only = false;
 };
 
 // Validate arguments, fill the Problem (except the launch shape) and pick
@@ -382,42 +385,196 @@ cudaError_t cast_from_f32(const float* src, void* dst, int dt, int64_t n, cudaSt
 }
 
 // ------------------------------------------------------------ backward plan
-// The backward has two implementations: the gather/scatter kernel (any
-// shape; fp32 atomics into grad_value or an fp32 workspace) and the binned
-// tile kernel (msda_binned.cuh) for large problems with host-resident shapes
-// and 16-byte channel rows.  The plan picks one and lays out the workspace.
-constexpr int64_t kBinnedMinSamples = int64_t{1} << 18;
-constexpr int kBinSmemBudget = 72 * 1024;    // three tile CTAs per SM
-constexpr int64_t kAtomicLevelRecords = 8192;
-constexpr int kMaxTilesPerBh = 24576;   // fill-pass histogram: 2 ints per tile in smem
+// The backward has two implementations: the cell-sorted pipeline
+// (msda_sorted.cuh; host-resident shapes, large problems) and the
+// gather/scatter kernel (any shape; vector reductions into grad_value or an
+// fp32 workspace).  The plan picks one and lays out the workspace.
 
-// Gather path, 16-bit values: a level whose expected contributions per
-// grad_value element (2^d corners x Q x P samples / voxels) stay at or below
-// this bound reduces straight into grad_value in its own dtype -- the
-// reference accumulates every level that way -- so its fp32 accumulator rows,
-// their zero-fill and their cast disappear.  Busier levels keep fp32
-// accumulation, which bounds their rounding error.
+// Gather path, 16-bit values, opt-in (MSDA_BWD_DIRECT16=1): a level whose
+// expected contributions per grad_value element (2^d corners x Q x P samples
+// / voxels) stay at or below this bound reduces straight into grad_value in
+// its own dtype, as the reference does for every level, instead of through
+// the fp32 accumulator.  The bound assumes uniformly spread locations:
+// clustered samples (a module's points around their reference points) can put
+// hundreds of 16-bit roundings on one element, so the default accumulates
+// every level in fp32 and rounds once.
 constexpr double kDirect16Contrib = 8.0;
 
 struct BwdPlan {
-  bool binned = false;
-  BinPlan bp{};
-  BinLaunch bl{};
-  size_t off[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // counts, starts, cursor, item_start, item_counter, scan_tmp, records, acc
   size_t ws_bytes = 0;
   // gather path
   int32_t direct16 = 0;   // levels reduced straight into grad_value
   bool compact = false;   // fp32 accumulator holds only the other levels
   int64_t acc_keys = 0;   // keys per batch entry in the fp32 accumulator
   int32_t acc_start[kMaxLevels] = {};
+  // cell-sorted path (msda_sorted.cuh)
+  bool sorted = false;
+  SortPlan sp{};          // per-chunk sizes; pointers are set per call
+  int64_t chunk_b = 0;    // batch entries per chunk
+  int64_t smp_per_b = 0;  // samples per batch entry
+  int64_t keys_per_b = 0; // bucket keys per batch entry
+  size_t soff[4] = {};    // bucket counts (one leading zero), bsum, srec, acc
 };
+
+size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
+
+// ------------------------------------------------------------ sorted plan
+// The cell-sorted backward runs when the level shapes are on the host and the
+// problem is large enough to amortise its nine launches.  Per level it
+// picks how the value gradient is formed: gathered per value row (levels
+// with at most kVoxelMaxDensity samples per cell and (b, h): each sample is
+// read by its 2^d corner rows) or aggregated per cell in registers and
+// flushed with fp32 reductions (denser levels: one flush per cell).  The
+// break-even follows from the measured B200 rates of 64-byte row gathers
+// (250 G rows/s) and 128-byte fp32 reductions (47 G rows/s).
+constexpr int64_t kSortedMinSamples = int64_t{1} << 20;
+constexpr double kVoxelMaxDensity = 6.0;
+// The gather/scatter backward stays the default until the sorted pipeline
+// outruns it on the benchmark shapes (MSDA_BWD_PATH=sorted selects it).
+constexpr bool kSortedByDefault = false;
+
+FastDiv make_fdiv(uint32_t d) {
+  if (d == 0) d = 1;
+  uint32_t l = 0;
+  while ((uint64_t{1} << l) < d) ++l;
+  const uint64_t m = ((uint64_t{1} << (31 + l)) + d - 1) / d;
+  return FastDiv{static_cast<uint32_t>(m), 31 + l};
+}
+
+bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan& pl) {
+  if (a.scatter_only || a.fused || p.shapes_dev != nullptr) return false;
+  // rows wider than two chunks per lane keep the scatter plan (the sorted
+  // walk holds 2^d corner rows and their gradients in registers)
+  Problem pw = p;
+  LaunchShape lw = ls;
+  bwd_gather_shape(a, pw, lw);
+  if (lw.vpl > 2) return false;
+  const char* env = std::getenv("MSDA_BWD_PATH");
+  const bool forced = env && std::strcmp(env, "sorted") == 0;
+  if (env && !forced) return false;
+  const int64_t samples = a.B * a.Q * a.H * a.L * a.P;
+  if (samples == 0 || a.C == 0 || a.L == 0) return false;
+  if (!forced && (!kSortedByDefault || samples < kSortedMinSamples)) return false;
+  const char* dens_env = std::getenv("MSDA_VOXEL_DENSITY");
+  double max_dens = dens_env ? std::atof(dens_env) : kVoxelMaxDensity;
+  // The voxel kernel takes the forward's lane shape (16-byte chunks where the
+  // row allows); shapes it is not instantiated for keep every level dense.
+  if (!((ls.vb == 16 && ls.vpl <= 4) || ((ls.vb == 4 || ls.vb == 2) && ls.vpl == 1)))
+    max_dens = -1.0;
+  const int tile_max = kThreads;                     // voxels per voxel-kernel CTA (one per thread)
+  const int64_t row_bytes = a.C * dtype_bytes(a.vdt);
+  // samples the voxel kernel stages per round: as many as fit 40 KB of shared
+  // memory next to the range bounds, at most 512
+  const int64_t bounds_max = int64_t{4} * (tile_max + 2) * 4 + 4 * 64;
+  // per staged sample: weights (16 B), grad_out row index (4 B), grad_out row + 16 B pad
+  int64_t cap = (40 * 1024 - bounds_max) / (36 + row_bytes);
+  cap = std::min<int64_t>(cap, 512) & ~int64_t{1};
+  if (cap < 16) max_dens = -1.0;
+  SortPlan sp{};
+  int64_t seg = 0, vox = 0, acc_keys = 0, units = 0, max_bounds = 0;
+  int nvl = 0;
+  const bool f32 = a.vdt == MSDA_FLOAT32;
+  for (int64_t l = 0; l < a.L; ++l) {
+    int64_t ncell = 1, nvox = 1;
+    for (int ax = 0; ax < 3; ++ax) {
+      const int64_t sz = ax < a.ndim ? p.lv.size[l][ax] : 1;
+      sp.cells[l][ax] = static_cast<int32_t>(ax < a.ndim ? sz + 1 : 1);
+      ncell *= sp.cells[l][ax];
+      nvox *= sz;
+    }
+    sp.lvl_base[l] = static_cast<int32_t>(seg);
+    seg += ncell + 1;
+    if (seg >= INT32_MAX) return false;
+    const double dens = static_cast<double>(a.Q * a.P) / static_cast<double>(ncell);
+    if (dens <= max_dens && nvox > 0) {
+      // tile: up to tile_max voxels, NY rows of TX; fewer rows when the
+      // expected samples of its cell rows pass two staging rounds
+      const int64_t W = p.lv.size[l][0], Hl = p.lv.size[l][1];
+      const int64_t tx = std::min<int64_t>(W, tile_max);
+      int64_t ny = std::max<int64_t>(1, std::min<int64_t>(tile_max / tx, Hl));
+      const int zr = a.ndim == 3 ? 2 : 1;
+      while (ny > 1 && static_cast<double>(zr * (ny + 1) * (tx + 1)) * dens > 2.0 * cap) --ny;
+      VoxTile vt;
+      vt.tx = static_cast<int32_t>(tx);
+      vt.ny = static_cast<int32_t>(ny);
+      vt.ntx = static_cast<int32_t>((W + tx - 1) / tx);
+      vt.nty = static_cast<int32_t>((Hl + ny - 1) / ny);
+      max_bounds = std::max<int64_t>(max_bounds, zr * (ny + 1) * (tx + 2) + zr * (ny + 1) + 1);
+      sp.voxel_mask |= 1 << l;
+      sp.vl_level[nvl] = static_cast<int32_t>(l);
+      sp.vl_tile[nvl] = vt;
+      sp.vl_ubase[nvl] = static_cast<int32_t>(units);
+      units += int64_t{vt.ntx} * vt.nty * (a.ndim == 3 ? p.lv.size[l][2] : 1);
+      vox += nvox;
+      ++nvl;
+      if (vox >= INT32_MAX || units >= INT32_MAX) return false;
+    } else {
+      pl.acc_start[l] = static_cast<int32_t>(f32 ? p.lv.start[l] : acc_keys);
+      acc_keys += nvox;
+      sp.dl_level[sp.ndl++] = static_cast<int32_t>(l);
+    }
+  }
+  sp.vl_ubase[nvl] = static_cast<int32_t>(units);
+  sp.dchunks = static_cast<int32_t>((a.Q * a.P + kWalkChunk - 1) / kWalkChunk);
+  sp.dlog2g = pw.log2g;
+  sp.dnv = static_cast<int32_t>(a.C * dtype_bytes(a.vdt) / lw.vb);
+  const int64_t per_b_smp = a.Q * a.H * a.L * a.P;
+  const int64_t per_b_keys = a.H * seg;
+  const int64_t per_b_vox = a.H * vox;
+  const int64_t lim = INT32_MAX - 1;
+  int64_t nb = a.B;
+  nb = std::min(nb, lim / per_b_smp);
+  nb = std::min(nb, lim / per_b_keys);
+  if (per_b_vox > 0) nb = std::min(nb, lim / per_b_vox);
+  if (units > 0) nb = std::min(nb, lim / (a.H * units));
+  // MSDA_SORTED_CHUNK_B (tests, tuning): at most this many batch entries per chunk
+  const char* cb_env = std::getenv("MSDA_SORTED_CHUNK_B");
+  if (cb_env && std::atoll(cb_env) > 0) nb = std::min<int64_t>(nb, std::atoll(cb_env));
+  if (nb < 1) return false;
+  sp.n = static_cast<int32_t>(nb * per_b_smp);
+  sp.nkeys = static_cast<int32_t>(nb * per_b_keys);
+  sp.seg_keys = static_cast<int32_t>(seg);
+  sp.nvl = nvl;
+  sp.units_per_bh = static_cast<int32_t>(units);
+  sp.vcap = static_cast<int32_t>(cap);
+  sp.vnv = p.nv;
+  sp.div_nv = make_fdiv(static_cast<uint32_t>(std::max<int32_t>(p.nv, 1)));
+  sp.vsmem = static_cast<int32_t>(cap * (36 + row_bytes) + max_bounds * 4);
+  if (nvl > 0 && sp.vsmem > 48 * 1024) return false;  // within the default dynamic limit
+  sp.div_lp = make_fdiv(static_cast<uint32_t>(a.L * a.P));
+  sp.div_p = make_fdiv(static_cast<uint32_t>(a.P));
+  sp.div_h = make_fdiv(static_cast<uint32_t>(a.H));
+  sp.div_l = make_fdiv(static_cast<uint32_t>(a.L));
+  sp.div_q = make_fdiv(static_cast<uint32_t>(a.Q));
+  pl.sp = sp;
+  pl.sorted = true;
+  pl.chunk_b = nb;
+  pl.smp_per_b = per_b_smp;
+  pl.keys_per_b = per_b_keys;
+  pl.compact = !f32;
+  pl.acc_keys = f32 ? a.K : acc_keys;
+  pl.direct16 = 0;
+  const int64_t nblk = (int64_t{sp.nkeys} + kScanTile - 1) / kScanTile;
+  const int64_t n = sp.n;
+  const size_t sizes[4] = {
+      static_cast<size_t>(sp.nkeys + 2) * 4, static_cast<size_t>(nblk + 1) * 4,
+      static_cast<size_t>(n) * sizeof(SRec),
+      f32 ? 0 : static_cast<size_t>(nb * acc_keys * a.H * a.C) * sizeof(float)};
+  size_t off = 0;
+  for (int i = 0; i < 4; ++i) {
+    pl.soff[i] = off;
+    off += align256(sizes[i]);
+  }
+  pl.ws_bytes = off;
+  return true;
+}
 
 // Gather-path value-gradient targets (see kDirect16Contrib).
 void plan_gather_targets(const Args& a, const Problem& p, BwdPlan& pl) {
   pl.acc_keys = a.K;
   if (dtype_bytes(a.vdt) != 2 || p.shapes_dev != nullptr || a.K == 0) return;
   const char* env = std::getenv("MSDA_BWD_DIRECT16");
-  if (env && std::strcmp(env, "0") == 0) return;
+  if (env == nullptr || std::strcmp(env, "1") != 0) return;
   // MSDA_BWD_DIRECT16_MAX (tuning): the contribution bound.
   const char* mx = std::getenv("MSDA_BWD_DIRECT16_MAX");
   const double bound = mx ? std::atof(mx) : kDirect16Contrib;
@@ -438,143 +595,105 @@ void plan_gather_targets(const Args& a, const Problem& p, BwdPlan& pl) {
   pl.acc_keys = keys;
 }
 
-size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
-
-// Shared memory of the tile kernel for a tile shape: value tile + halo + one
-// zero row, and the tile's fp32 value gradient.
-int64_t tile_smem_bytes(int ndim, const int32_t* t, int64_t row_bytes, int64_t C, int G) {
-  const int64_t halo = int64_t{t[0] + 1} * (t[1] + 1) * (ndim == 3 ? t[2] + 1 : 1);
-  const int64_t vox = int64_t{t[0]} * t[1] * t[2];
-  (void)G;
-  return (halo + 1) * row_bytes + vox * C * 4;
-}
-
-bool choose_tile(int ndim, int64_t row_bytes, int64_t C, int G, int budget, int32_t* tile,
-                 int* smem) {
-  static const int32_t c3[][3] = {{8, 8, 8}, {8, 8, 4}, {8, 4, 4}, {4, 4, 4}, {4, 4, 2}, {4, 2, 2}, {2, 2, 2}};
-  static const int32_t c2[][3] = {{32, 16, 1}, {16, 16, 1}, {16, 8, 1}, {8, 8, 1}, {8, 4, 1}, {4, 4, 1}, {2, 2, 1}};
-  const char* env = std::getenv("MSDA_BIN_TILE");
-  int32_t forced[3] = {0, 0, 1};
-  if (env && std::sscanf(env, "%d,%d,%d", &forced[0], &forced[1], &forced[2]) >= 2) {
-    if (ndim == 2) forced[2] = 1;
-  } else {
-    forced[0] = 0;
-  }
-  for (int i = -1; i < 7; ++i) {
-    const int32_t* t = i < 0 ? forced : (ndim == 3 ? c3[i] : c2[i]);
-    if (t[0] <= 0 || t[1] <= 0 || t[2] <= 0) continue;
-    const int64_t bytes = tile_smem_bytes(ndim, t, row_bytes, C, G);
-    if (bytes <= budget || (i < 0 && bytes <= 200 * 1024)) {
-      tile[0] = t[0]; tile[1] = t[1]; tile[2] = t[2];
-      *smem = static_cast<int>(bytes);
-      return true;
-    }
-  }
-  return false;
-}
-
 void plan_bwd(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan& pl) {
-  const int64_t e = dtype_bytes(a.vdt);
-  const int64_t samples = a.B * a.Q * a.H * a.L * a.P;
   pl = BwdPlan{};
-  const char* env = std::getenv("MSDA_BWD_PATH");
-  // The binned path is opt-in (MSDA_BWD_PATH=binned) until it outruns the
-  // gather/scatter kernel on the benchmark shapes.
-  const bool force_binned = env && std::strcmp(env, "binned") == 0 && !a.fused;
-  const bool force_gather = !force_binned;
-  bool ok_binned = !force_gather && p.shapes_dev == nullptr && ls.vb == 16 && ls.vpl == 1 &&
-                   samples > 0 && a.C > 0 && (force_binned || samples >= kBinnedMinSamples) &&
-                   a.P <= 16 && a.Q < (int64_t{1} << 26) && a.L * a.P <= 512 &&
-                   samples * (int64_t{1} << a.ndim) < INT32_MAX;
-  for (int64_t l = 0; ok_binned && l < a.L; ++l)
-    for (int ax = 0; ax < 3; ++ax) ok_binned = ok_binned && p.lv.size[l][ax] > 0;
-  int smem = 0;
-  BinPlan& bp = pl.bp;
-  if (ok_binned) {
-    const char* sb = std::getenv("MSDA_BIN_SMEM_KB");
-    const int budget = sb ? std::atoi(sb) * 1024 : kBinSmemBudget;
-    ok_binned = choose_tile(a.ndim, a.C * e, a.C, 1 << p.log2g, budget, bp.tile, &smem);
-  }
-  if (ok_binned) {
-    int64_t ntl = 0;
-    const double straddle = (1.0 + 1.0 / bp.tile[0]) * (1.0 + 1.0 / bp.tile[1]) *
-                            (a.ndim == 3 ? 1.0 + 1.0 / bp.tile[2] : 1.0);
-    int64_t acc_keys = 0;
-    // Tuning / test knobs: records per tile above which a level reduces
-    // through the fp32 accumulator, and records per work item there.
-    const char* ar = std::getenv("MSDA_BIN_ATOMIC_RECORDS");
-    const int64_t atomic_records = ar ? std::atoll(ar) : kAtomicLevelRecords;
-    const char* sm = std::getenv("MSDA_BIN_SMAX");
-    bp.s_max = sm && std::atoi(sm) > 0 ? std::atoi(sm) : 2048;
-    for (int64_t l = 0; l < a.L; ++l) {
-      int64_t nt = 1;
-      for (int ax = 0; ax < 3; ++ax) {
-        bp.ntile[l][ax] = (p.lv.size[l][ax] + bp.tile[ax] - 1) / bp.tile[ax];
-        nt *= bp.ntile[l][ax];
-      }
-      bp.tile_base[l] = static_cast<int32_t>(ntl);
-      ntl += nt;
-      const double expect = static_cast<double>(a.Q * a.P) * straddle / static_cast<double>(nt);
-      if (expect > static_cast<double>(atomic_records)) {
-        bp.atomic_mask |= 1 << l;
-        const int64_t nkey = int64_t{p.lv.size[l][0]} * p.lv.size[l][1] * p.lv.size[l][2];
-        bp.acc_start[l] = static_cast<int32_t>(a.vdt == MSDA_FLOAT32 ? p.lv.start[l] : acc_keys);
-        acc_keys += nkey;
-      }
-    }
-    if (a.vdt == MSDA_FLOAT32) acc_keys = a.K;
-    ok_binned = ntl <= kMaxTilesPerBh;
-    bp.ntl = static_cast<int32_t>(ntl);
-    bp.acc_keys = acc_keys;
-    const int64_t rpc = std::max<int64_t>(1, 32768 / std::max<int64_t>(1, a.L * a.P));
-    bp.rows_per_chunk = static_cast<int32_t>(rpc);
-    bp.nchunk = static_cast<int32_t>((a.Q + rpc - 1) / rpc);
-    bp.nlevels = static_cast<int32_t>(a.L);
-  }
-  if (!ok_binned) {
-    pl.binned = false;
-    plan_gather_targets(a, p, pl);
-    pl.ws_bytes = (a.vdt == MSDA_FLOAT32)
-                      ? 0 : static_cast<size_t>(a.B * pl.acc_keys * a.H * a.C) * sizeof(float);
-    return;
-  }
-  pl.binned = true;
-  const int64_t nb = a.B * a.H * bp.ntl;
-  pl.bl.ndim = a.ndim;
-  pl.bl.nb = nb;
-  pl.bl.smem_main = smem;
-  pl.bl.fp32_value = a.vdt == MSDA_FLOAT32;
-  const int64_t scan_blocks = (nb + 1 + kScanThreads * kScanItems - 1) / (kScanThreads * kScanItems);
-  const int64_t max_records = samples * (int64_t{1} << a.ndim);
-  const size_t sizes[8] = {
-      static_cast<size_t>(nb) * 4, static_cast<size_t>(nb + 1) * 4, static_cast<size_t>(nb) * 4,
-      static_cast<size_t>(nb + 1) * 4, 4, static_cast<size_t>(scan_blocks + 1) * 4,
-      static_cast<size_t>(max_records) * 4,
-      (bp.atomic_mask && a.vdt != MSDA_FLOAT32)
-          ? static_cast<size_t>(a.B * bp.acc_keys * a.H * a.C) * sizeof(float) : 0};
-  size_t off = 0;
-  for (int i = 0; i < 8; ++i) {
-    pl.off[i] = off;
-    off += align256(sizes[i]);
-  }
-  pl.ws_bytes = off;
+  if (plan_sorted(a, p, ls, pl)) return;
+  plan_gather_targets(a, p, pl);
+  pl.ws_bytes = (a.vdt == MSDA_FLOAT32)
+                    ? 0 : static_cast<size_t>(a.B * pl.acc_keys * a.H * a.C) * sizeof(float);
 }
 
-cudaError_t dispatch_bwd_binned(int vdt, int sdt, const BinLaunch& bl, const Problem& p,
-                                const BinPlan& bp, const BinBuffers& bb, const void* go, void* gv,
-                                void* gl, void* ga, cudaStream_t st) {
+cudaError_t dispatch_sorted(int vdt, int sdt, const LaunchShape& ls, const LaunchShape& lsd,
+                            const Problem& p, const SortPlan& sp, const void* go, float* gacc,
+                            void* gv, void* gl, void* ga, cudaStream_t st) {
   switch (vdt) {
-    case MSDA_FLOAT32: return launch_bwd_binned<float, float>(bl, p, bp, bb, go, gv, gl, ga, st);
+    case MSDA_FLOAT32:
+      return launch_sorted_bwd<float, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st);
     case MSDA_FLOAT16:
       return sdt == MSDA_FLOAT32
-                 ? launch_bwd_binned<__half, float>(bl, p, bp, bb, go, gv, gl, ga, st)
-                 : launch_bwd_binned<__half, __half>(bl, p, bp, bb, go, gv, gl, ga, st);
+                 ? launch_sorted_bwd<__half, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st)
+                 : launch_sorted_bwd<__half, __half>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st);
     default:
       return sdt == MSDA_FLOAT32
-                 ? launch_bwd_binned<__nv_bfloat16, float>(bl, p, bp, bb, go, gv, gl, ga, st)
-                 : launch_bwd_binned<__nv_bfloat16, __nv_bfloat16>(bl, p, bp, bb, go, gv, gl,
-                                                                   ga, st);
+                 ? launch_sorted_bwd<__nv_bfloat16, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga,
+                                                           st)
+                 : launch_sorted_bwd<__nv_bfloat16, __nv_bfloat16>(ls, lsd, p, sp, go, gacc, gv,
+                                                                   gl, ga, st);
   }
+}
+
+// The cell-sorted backward, chunk by chunk of batch entries (pointers
+// offset to the chunk; the workspace is reused by every chunk).
+int run_bwd_sorted(const Args& a, Problem p, LaunchShape ls, const BwdPlan& pl, const void* go,
+                   void* gv, void* gl, void* ga, void* ws, cudaStream_t st) {
+  LaunchShape lsd = ls;  // the dense kernel's lane shape
+  {
+    Problem pd = p;
+    bwd_gather_shape(a, pd, lsd);
+  }
+  const int64_t e = dtype_bytes(a.vdt), se = dtype_bytes(a.sdt);
+  const int64_t row_bytes = a.H * a.C * e;  // one key of value / grad_value
+  const bool f32 = a.vdt == MSDA_FLOAT32;
+  char* w = static_cast<char*>(ws);
+  SortPlan sp = pl.sp;
+  sp.start = reinterpret_cast<int32_t*>(w + pl.soff[0]);  // [0] stays 0
+  sp.cnt = reinterpret_cast<int32_t*>(w + pl.soff[0]) + 1;
+  sp.bsum = reinterpret_cast<int32_t*>(w + pl.soff[1]);
+  sp.srec = reinterpret_cast<SRec*>(w + pl.soff[2]);
+  float* acc = f32 ? nullptr : reinterpret_cast<float*>(w + pl.soff[3]);
+  p.acc_compact = pl.compact ? 1 : 0;
+  p.acc_keys = pl.acc_keys;
+  for (int l = 0; l < kMaxLevels; ++l) p.acc_start[l] = pl.acc_start[l];
+  p.direct16 = 0;
+  p.grad_value16 = nullptr;
+  const int64_t smp_bytes = pl.smp_per_b;  // samples per batch entry
+  cudaError_t err = cudaSuccess;
+  for (int64_t b0 = 0; b0 < a.B; b0 += pl.chunk_b) {
+    const int64_t nb = std::min(pl.chunk_b, a.B - b0);
+    Problem pc = p;
+    pc.B = nb;
+    pc.value = static_cast<const char*>(a.value) + b0 * a.K * row_bytes;
+    pc.loc = static_cast<const char*>(a.loc) + b0 * smp_bytes * a.ndim * se;
+    pc.attn = static_cast<const char*>(a.attn) + b0 * smp_bytes * se;
+    SortPlan sc = sp;
+    sc.n = static_cast<int32_t>(nb * pl.smp_per_b);
+    sc.nkeys = static_cast<int32_t>(nb * pl.keys_per_b);
+    LaunchShape lc = ls;  // dots kernel: one lane group per (b, q, h) row of the chunk
+    lc.grid = ((nb * a.Q * a.H << p.log2g) + kThreads - 1) / kThreads;
+    const void* go_c = static_cast<const char*>(go) + b0 * a.Q * a.H * a.C * e;
+    char* gv_c = static_cast<char*>(gv) + b0 * a.K * row_bytes;
+    void* gl_c = static_cast<char*>(gl) + b0 * smp_bytes * a.ndim * se;
+    void* ga_c = static_cast<char*>(ga) + b0 * smp_bytes * se;
+    // dense levels: zero their reduction targets
+    int64_t dense_keys = 0;
+    for (int64_t l = 0; l < a.L; ++l) {
+      if ((sp.voxel_mask >> l) & 1) continue;
+      const int64_t nvox = int64_t{p.lv.size[l][0]} * p.lv.size[l][1] * p.lv.size[l][2];
+      dense_keys += nvox;
+      if (f32 && nvox > 0) {
+        err = cudaMemset2DAsync(gv_c + p.lv.start[l] * row_bytes,
+                                static_cast<size_t>(a.K * row_bytes), 0,
+                                static_cast<size_t>(nvox * row_bytes), static_cast<size_t>(nb), st);
+        if (err != cudaSuccess) return cuda_fail(err, "zeroing grad_value rows");
+      }
+    }
+    if (!f32 && dense_keys > 0) {
+      err = cudaMemsetAsync(acc, 0, static_cast<size_t>(nb * dense_keys * a.H * a.C) * sizeof(float),
+                            st);
+      if (err != cudaSuccess) return cuda_fail(err, "zeroing the grad_value accumulator");
+    }
+    float* gacc = f32 ? reinterpret_cast<float*>(gv_c) : acc;
+    err = dispatch_sorted(a.vdt, a.sdt, lc, lsd, pc, sc, go_c, gacc, gv_c, gl_c, ga_c, st);
+    if (err != cudaSuccess) return cuda_fail(err, "sorted backward launch");
+    if (!f32 && dense_keys > 0) {
+      Problem pcast = pc;
+      pcast.direct16 = sp.voxel_mask;  // the levels the accumulator does not hold
+      err = a.vdt == MSDA_FLOAT16 ? launch_compact_cast<__half>(pcast, acc, gv_c, st)
+                                  : launch_compact_cast<__nv_bfloat16>(pcast, acc, gv_c, st);
+      if (err != cudaSuccess) return cuda_fail(err, "grad_value cast launch");
+    }
+  }
+  return ok();
 }
 
 int run_bwd(const Args& a, const void* go, void* gv, void* gl, void* ga, void* ws,
@@ -602,22 +721,9 @@ int run_bwd(const Args& a, const void* go, void* gv, void* gl, void* ga, void* w
                   pl.ws_bytes, ws == nullptr ? size_t{0} : ws_bytes);
     if (!aligned(ws, 256)) return fail(MSDA_ERROR_WORKSPACE, "workspace must be 256-byte aligned");
   }
+  if (pl.sorted)
+    return run_bwd_sorted(a, p, ls, pl, go, gv, gl, ga, ws, static_cast<cudaStream_t>(stream));
   cudaError_t err;
-  if (pl.binned) {
-    char* w = static_cast<char*>(ws);
-    BinBuffers bb;
-    bb.counts = reinterpret_cast<int32_t*>(w + pl.off[0]);
-    bb.starts = reinterpret_cast<int32_t*>(w + pl.off[1]);
-    bb.cursor = reinterpret_cast<int32_t*>(w + pl.off[2]);
-    bb.item_start = reinterpret_cast<int32_t*>(w + pl.off[3]);
-    bb.item_counter = reinterpret_cast<int32_t*>(w + pl.off[4]);
-    bb.scan_tmp = reinterpret_cast<int32_t*>(w + pl.off[5]);
-    bb.records = reinterpret_cast<int32_t*>(w + pl.off[6]);
-    bb.acc = a.vdt == MSDA_FLOAT32 ? static_cast<float*>(gv) : reinterpret_cast<float*>(w + pl.off[7]);
-    err = dispatch_bwd_binned(a.vdt, a.sdt, pl.bl, p, pl.bp, bb, go, gv, gl, ga, st);
-    if (err != cudaSuccess) return cuda_fail(err, "binned backward launch");
-    return ok();
-  }
   float* gacc = nullptr;
   if (a.vdt == MSDA_FLOAT32) {
     gacc = static_cast<float*>(gv);
@@ -834,12 +940,13 @@ int msda_cast_from_f32(const float* src, void* dst, int dst_dtype, int64_t count
 static size_t workspace_bytes(int ndim, int value_dtype, int64_t batch, int64_t num_keys,
                               int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
                               int spatial_shapes_on_device, int64_t num_levels,
-                              int64_t num_queries, int64_t num_points, int fused) {
+                              int64_t num_queries, int64_t num_points, int fused,
+                              bool scatter_only = false) {
   // Plan with 256-byte aligned stand-in pointers (never dereferenced).
   void* fake = reinterpret_cast<void*>(uintptr_t{256});
   Args a{ndim, fake, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,
          spatial_shapes_on_device, num_levels, fake, fake, value_dtype, num_queries, num_points,
-         1, 1e-4, static_cast<const float*>(fake), fused};
+         1, 1e-4, static_cast<const float*>(fake), fused, scatter_only};
   msda::Problem p;
   msda::LaunchShape ls;
   const void* bufs[2] = {fake, fake};
@@ -865,6 +972,35 @@ size_t msda_fused_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batch, 
   return workspace_bytes(ndim, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,
                          spatial_shapes_on_device, num_levels, num_queries, num_points, 1);
 }
+
+}  // extern "C"
+
+namespace msda {
+// The static-scratch backward (msda_noalloc.cu) keeps the gather/scatter
+// plan, whose workspace its fixed array was sized for.
+size_t scatter_workspace_bytes(int ndim, int value_dtype, int64_t batch, int64_t num_keys,
+                               int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+                               int spatial_shapes_on_device, int64_t num_levels,
+                               int64_t num_queries, int64_t num_points) {
+  return workspace_bytes(ndim, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,
+                         spatial_shapes_on_device, num_levels, num_queries, num_points, 0, true);
+}
+
+int bwd_scatter(int ndim, const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+                int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+                int spatial_shapes_on_device, int64_t num_levels, const void* sampling_locations,
+                const void* attention_weights, int sampling_dtype, int64_t num_queries,
+                int64_t num_points, int clamp_grid, double clamp_eps, const void* grad_output,
+                void* grad_value, void* grad_sampling_locations, void* grad_attention_weights,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  MSDA_ARGS(ndim);
+  a.scatter_only = true;
+  return run_bwd(a, grad_output, grad_value, grad_sampling_locations, grad_attention_weights,
+                 workspace, workspace_bytes, stream);
+}
+}  // namespace msda
+
+extern "C" {
 
 const char* msda_status_string(int status) {
   switch (status) {

@@ -1,8 +1,6 @@
 // Kernel instantiations for value dtype __nv_bfloat16, sampling dtype __nv_bfloat16.
-#include "msda_binned_launch.cuh"
 #include "msda_launch.cuh"
 
 namespace msda {
 MSDA_INSTANTIATE_MODE(__nv_bfloat16, __nv_bfloat16, false)
-MSDA_INSTANTIATE_BINNED(__nv_bfloat16, __nv_bfloat16)
 }  // namespace msda

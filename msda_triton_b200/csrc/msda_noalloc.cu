@@ -21,7 +21,20 @@
 #include "../../include/msda_b200.h"
 
 namespace msda {
-int set_last_error(int code, const char* msg);  // msda_capi.cu: feeds msda_last_error()
+// msda_capi.cu: feeds msda_last_error(); the gather/scatter-plan backward
+// and its workspace size.
+int set_last_error(int code, const char* msg);
+size_t scatter_workspace_bytes(int ndim, int value_dtype, int64_t batch, int64_t num_keys,
+                               int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+                               int spatial_shapes_on_device, int64_t num_levels,
+                               int64_t num_queries, int64_t num_points);
+int bwd_scatter(int ndim, const void* value, int value_dtype, int64_t batch, int64_t num_keys,
+                int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
+                int spatial_shapes_on_device, int64_t num_levels, const void* sampling_locations,
+                const void* attention_weights, int sampling_dtype, int64_t num_queries,
+                int64_t num_points, int clamp_grid, double clamp_eps, const void* grad_output,
+                void* grad_value, void* grad_sampling_locations, void* grad_attention_weights,
+                void* workspace, size_t workspace_bytes, void* stream);
 }  // namespace msda
 
 namespace {
@@ -68,10 +81,10 @@ extern "C" MSDA_API int msda_bwd_static_scratch(
     int clamp_grid, double clamp_eps, const void* grad_output, void* grad_value,
     void* grad_sampling_locations, void* grad_attention_weights, void* stream) {
   if (ndim != 2 && ndim != 3) return noalloc_fail(MSDA_ERROR_INVALID_ARGUMENT, "ndim must be 2 or 3");
-  const size_t need = msda_bwd_workspace_bytes(ndim, value_dtype, batch, num_keys, num_heads,
-                                               channels, spatial_shapes,
-                                               spatial_shapes_on_device, num_levels, num_queries,
-                                               num_points);
+  const size_t need = msda::scatter_workspace_bytes(ndim, value_dtype, batch, num_keys,
+                                                    num_heads, channels, spatial_shapes,
+                                                    spatial_shapes_on_device, num_levels,
+                                                    num_queries, num_points);
   if (need > kStaticScratchBytes) {
     char msg[256];
     snprintf(msg, sizeof(msg),
@@ -84,8 +97,8 @@ extern "C" MSDA_API int msda_bwd_static_scratch(
   int rc = scratch_address(&scratch);
   if (rc != MSDA_SUCCESS) return rc;
   // The regular backward zero-fills the part of the workspace it uses.
-  rc = (ndim == 2 ? msda2d_bwd : msda3d_bwd)(
-      value, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,
+  rc = msda::bwd_scatter(
+      ndim, value, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,
       spatial_shapes_on_device, num_levels, sampling_locations, attention_weights,
       sampling_dtype, num_queries, num_points, clamp_grid, clamp_eps, grad_output, grad_value,
       grad_sampling_locations, grad_attention_weights, scratch, kStaticScratchBytes, stream);

@@ -1,0 +1,800 @@
+// msda_sorted.cuh -- the cell-sorted MSDA backward.
+//
+// The value gradient of MSDA is a scatter: every sample adds a*w_c*grad_out
+// into the 2^d corner rows around it.  Done per sample with vector
+// reductions (red.global.add), its cost is set by the L2's reduction rate --
+// measured on B200 at 47 G rows/s for 128-byte fp32 rows and 79 G rows/s for
+// 64-byte bf16 rows, against 250 G rows/s for plain 64-byte row gathers.  This
+// path groups the samples by the cell they fall in (a counting sort keyed by
+// (b, h, level, cell)) and forms the value gradient without per-sample
+// reductions:
+//
+//   sparse levels ("voxel" levels, few samples per cell): each value row's
+//     gradient is GATHERED from the samples of the 2^d cells around it --
+//     msda_voxel_kernel sums them in fp32 registers and stores the row once.
+//     No reductions, no zero-fill, one rounding per element.
+//   dense levels (many samples per cell): msda_dense_kernel walks the sorted
+//     samples of each cell in segments and keeps the cell's 2^d corner
+//     gradients in registers, flushing them with one fp32 vector reduction
+//     per corner and segment instead of one per sample.
+//
+// grad_attn and grad_loc need no sort: msda_dots_kernel computes them in
+// query order (the forward's gather plus the corner dot products), and
+// counts the samples per cell on the way.
+//
+// Pipeline for one chunk of batch entries (all on one stream):
+//   msda_dots_kernel       grad_attn, grad_loc; count[key] += 1 per sample
+//   msda_scan_*            counts -> exclusive bucket starts
+//   msda_place_kernel      record (a, fractions, grad_out row, key) at atomicAdd(cursor[key], 1)
+//   msda_dense_kernel      dense-level value gradient, per cell segment
+//   msda_voxel_kernel      sparse-level value gradient, gathered per value row
+//
+// Cells.  A sample at level l falls in the cell of its lower corner
+// (i0x, i0y[, i0z]) with each i0 in [-1, size-1] (grid_sample's corner
+// range for in-range and clamped locations); cell indices are i0 + 1, so the
+// level has (W+1)(H+1)[(D+1)] cells plus one "dead" bucket for samples with
+// no corner inside the level (locations far outside [0, 1] without the
+// clamp, NaN).  Every (b, h, level) owns exactly Q*P consecutive sorted
+// positions.  The value row at voxel (vx, vy, vz) is a corner of the cells
+// with i0 in {v-1, v} on every axis.
+//
+// Reference kernel this replaces: _bwd_kernel (src/msda_triton/triton/
+// msda_3d.py:291-653) and _bwd_kernel_2d (triton/msda_2d.py:263-510).
+#pragma once
+
+#include "msda_kernels.cuh"
+
+namespace msda {
+
+// n / d for 0 <= n < 2^31 as one 64-bit multiply and shift: with
+// l = ceil(log2 d) and m = ceil(2^(31+l) / d), floor(n*m / 2^(31+l)) equals
+// floor(n / d) because the rounding error n*(m*d - 2^(31+l)) / (d*2^(31+l))
+// stays below 1/d.
+struct FastDiv {
+  uint32_t m;
+  uint32_t shift;
+};
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+  return static_cast<uint32_t>((static_cast<uint64_t>(n) * f.m) >> f.shift);
+}
+
+// Tile of msda_voxel_kernel on one level: NY voxel rows x TX voxels.
+struct VoxTile {
+  int32_t tx, ny;     // voxels per row segment, rows per CTA
+  int32_t ntx, nty;   // tiles along x and y
+};
+
+// One sample at its sorted position (32 bytes: one sector).
+struct __align__(16) SRec {
+  float a;        // attention weight
+  float f[3];     // fractional offsets inside the cell
+  uint32_t row;   // (b, q, h) row of grad_out
+  int32_t key;    // bucket key
+  uint32_t pad[2];
+};
+
+// Everything the sorted pipeline adds to Problem (one chunk of batch
+// entries; the Problem's pointers are already offset to the chunk and its B
+// is the chunk's batch count).
+struct SortPlan {
+  int32_t n;                       // samples in the chunk: B*Q*H*L*P
+  int32_t nkeys;                   // bucket keys: B*H*seg_keys
+  int32_t seg_keys;                // keys per (b, h): sum over levels of cells_l + 1
+  int32_t lvl_base[kMaxLevels];    // first key of level l inside a (b, h) block
+  int32_t cells[kMaxLevels][3];    // cell-grid extent per axis (size + 1; 1 for z in 2D)
+  int32_t voxel_mask;              // levels whose value gradient msda_voxel_kernel gathers
+  int32_t ndl;                     // dense levels (msda_dense_kernel)
+  int32_t dl_level[kMaxLevels];    // k-th dense level
+  int32_t dchunks;                 // msda_dense_kernel CTAs per (b, h, dense level)
+  int32_t dlog2g, dnv;             // msda_dense_kernel lane group: 2^dlog2g lanes, dnv chunks per row
+  int32_t nvl;                     // voxel levels
+  int32_t vl_level[kMaxLevels];    // k-th voxel level
+  VoxTile vl_tile[kMaxLevels];     // msda_voxel_kernel tile of the k-th voxel level
+  int32_t vl_ubase[kMaxLevels + 1];// first voxel-kernel CTA of the k-th voxel level inside a (b, h) block
+  int32_t units_per_bh;            // vl_ubase[nvl]
+  int32_t vcap;                    // samples staged per round by msda_voxel_kernel
+  int32_t vnv;                     // msda_voxel_kernel: VB-byte chunks per channel row
+  FastDiv div_nv;                  // / vnv
+  int32_t vsmem;                   // its dynamic shared memory
+  FastDiv div_lp, div_p, div_h, div_l, div_q;
+  int32_t* cnt;                    // nkeys + 1: counts, then exclusive starts, then (after
+                                   // msda_place_kernel's cursor increments) the next bucket's start
+  const int32_t* start;            // cnt - 1, after msda_place_kernel: start[k] (start[0] = 0)
+  int32_t* bsum;                   // scan block sums
+  SRec* srec;                      // n: the samples in sorted order
+};
+
+// Bucket key of a resolved sample: the (b, h) block, the level's key range,
+// then the cell (z-major, x fastest), or the level's dead bucket.
+template <int NDIM>
+__device__ __forceinline__ int32_t bucket_key(const Point<NDIM>& pt, const int32_t* sz,
+                                              const int32_t* cells, int32_t base) {
+  bool dead = false;
+  int32_t c = 0;
+  int32_t ncell = 1;
+#pragma unroll
+  for (int a = NDIM - 1; a >= 0; --a) {
+    const int32_t i = pt.i0[a] + 1;
+    dead |= static_cast<uint32_t>(i) > static_cast<uint32_t>(sz[a]);
+    c = c * cells[a] + i;
+    ncell *= cells[a];
+  }
+  return base + (dead ? ncell : c);
+}
+
+// Level geometry from the host-resolved table (the sorted path requires
+// host shapes).
+__device__ __forceinline__ LevelGeom level_geom_tab(const Problem& p, int l, int64_t key_bytes) {
+  LevelGeom g;
+  g.sz[0] = p.lv.size[l][0];
+  g.sz[1] = p.lv.size[l][1];
+  g.sz[2] = p.lv.size[l][2];
+  g.start = p.lv.start[l];
+  g.dx = key_bytes;
+  g.dy = key_bytes * g.sz[0];
+  g.dz = g.dy * g.sz[1];
+  return g;
+}
+
+// Plain (shared-memory) loads of one chunk.
+template <int VB> __device__ __forceinline__ Raw<VB> ld_shared_chunk(const void* p);
+template <> __device__ __forceinline__ Raw<16> ld_shared_chunk<16>(const void* p) {
+  const uint4 v = *reinterpret_cast<const uint4*>(p);
+  Raw<16> r; r.w[0] = v.x; r.w[1] = v.y; r.w[2] = v.z; r.w[3] = v.w; return r;
+}
+template <> __device__ __forceinline__ Raw<8> ld_shared_chunk<8>(const void* p) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  Raw<8> r; r.w[0] = v.x; r.w[1] = v.y; return r;
+}
+template <> __device__ __forceinline__ Raw<4> ld_shared_chunk<4>(const void* p) {
+  Raw<4> r; r.w[0] = *reinterpret_cast<const unsigned int*>(p); return r;
+}
+template <> __device__ __forceinline__ Raw<2> ld_shared_chunk<2>(const void* p) {
+  Raw<2> r; r.h = *reinterpret_cast<const unsigned short*>(p); return r;
+}
+
+// ------------------------------------------------------------------ dots
+// grad_attn and grad_loc in query order, as the gather/scatter backward
+// computes them (one lane group per (b, q, h) row, the row's grad_out chunk
+// loaded once), without the value-gradient scatter.  Each sample's four
+// results (d out/d attn, d out/d index per axis) are lane partials over the
+// row's channel chunks; kDotBatch samples are reduced together by a
+// transposed butterfly -- each step halves the values a lane keeps -- so a
+// sample costs a few shuffles instead of a full butterfly of four values.
+// The lane that ends with a sample's grad_attn also counts the sample into
+// its bucket (the counting sort's histogram).
+constexpr int kDotBatch = 2;
+
+template <typename T, typename TS, int NDIM, int VB, int VPL>
+__global__ void __launch_bounds__(kThreads, 4)
+    msda_dots_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
+                     TS* __restrict__ grad_loc, TS* __restrict__ grad_attn) {
+  using CK = Chunk<T, VB>;
+  constexpr int EPV = CK::EPV;
+  constexpr int NC = 1 << NDIM;
+  constexpr int NV = kDotBatch * 4;
+  const uint64_t tid = static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  uint64_t r = tid >> p.log2g;
+  const int G = 1 << p.log2g;
+  const int j = static_cast<int>(tid & static_cast<uint64_t>(G - 1));
+  const int lane = static_cast<int>(threadIdx.x & 31u);
+  const unsigned gmask = G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane & ~(G - 1)));
+  // rows past the end stay (on row 0, storing nothing) for the group shuffles
+  const bool active = r < static_cast<uint64_t>(p.B * p.Q * p.H);
+  if (!active) r = 0;
+  const RowCoord rc = decode_row(static_cast<uint32_t>(r), p);
+  const int64_t row = (rc.b * p.Q + rc.q) * p.H + rc.h;
+  const int64_t key_bytes = p.H * p.C * static_cast<int64_t>(sizeof(T));
+  const char* vbase = static_cast<const char*>(p.value) +
+                      (rc.b * p.K * p.H + rc.h) * p.C * static_cast<int64_t>(sizeof(T));
+  const int LP = static_cast<int>(p.L * p.P);
+  const TS* lrow = static_cast<const TS*>(p.loc) + row * LP * NDIM;
+  const TS* arow = static_cast<const TS*>(p.attn) + row * LP;
+  const int32_t kbh = (static_cast<int32_t>(rc.b) * static_cast<int32_t>(p.H) +
+                       static_cast<int32_t>(rc.h)) * sp.seg_keys;
+
+  bool has[VPL];
+#pragma unroll
+  for (int v = 0; v < VPL; ++v) has[v] = j + v * G < p.nv;
+  float go[VPL][EPV];
+  {
+    const char* gorow = reinterpret_cast<const char*>(grad_out) +
+                        row * p.C * static_cast<int64_t>(sizeof(T));
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      const Raw<VB> rg = has[v] ? ld_chunk<VB>(gorow + (j + v * G) * VB) : raw_zero<VB>();
+      CK::unpack(rg, go[v]);
+    }
+  }
+  // values this lane keeps after the transposed steps, and the first one
+  int vbase_i = 0, steps = 0;
+#pragma unroll
+  for (int s = 1, half = NV / 2; s < NV; s <<= 1, half >>= 1)
+    if (s < G) {
+      ++steps;
+      if (j & s) vbase_i += half;
+    }
+  const int nkeep = NV >> steps;
+  const bool writer = G <= NV || j < NV;  // lanes above NV hold duplicates
+
+  const int P = static_cast<int>(p.P);
+  int l = 0, pp = 0;
+  for (int s0 = 0; s0 < LP; s0 += kDotBatch) {
+    float v[NV];
+    float sa[kDotBatch];
+    int32_t sinfo[kDotBatch], skey[kDotBatch];
+#pragma unroll
+    for (int i = 0; i < kDotBatch; ++i) {
+      v[4 * i] = v[4 * i + 1] = v[4 * i + 2] = v[4 * i + 3] = 0.0f;
+      sa[i] = 0.0f;
+      sinfo[i] = 0;
+      skey[i] = 0;
+      const int s = s0 + i;
+      if (s < LP) {
+        const LevelGeom g = level_geom_tab(p, l, key_bytes);
+        const Point<NDIM> pt = load_point<TS, NDIM>(lrow + s * NDIM, g.sz, p);
+        const float a = Elem<TS>::to_f(arow[s]);
+        const Corners<NDIM> cs = make_corners<NDIM>(pt, g, vbase, key_bytes, j * VB);
+        Raw<VB> raw[NC][VPL];
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+          for (int vv = 0; vv < VPL; ++vv)
+            raw[c][vv] = has[vv] ? MSDA_LD_VALUE(VB, cs.valid[c] ? cs.ptr[c] + vv * G * VB : cs.ptr[c])
+                                 : raw_zero<VB>();
+        // lane partial dot products with the corner rows (corners outside
+        // the level read the zero row: their dot is exactly 0)
+        float D[NC];
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          float dot = 0.0f;
+#pragma unroll
+          for (int vv = 0; vv < VPL; ++vv) {
+            float x[EPV];
+            CK::unpack(raw[c][vv], x);
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) dot = fmaf(go[vv][e], x[e], dot);
+          }
+          D[c] = dot;
+        }
+        // sum over corners of w_c * D_c and of d(w_c)/d(index) * D_c, factored
+        // axis by axis: ex = the x-interpolated dots, dx = their x-differences
+        const float fx = pt.f[0], fy = pt.f[1];
+        const float gx0 = __fsub_rn(1.0f, fx), gy0 = __fsub_rn(1.0f, fy);
+        float ex[NC / 2], dx[NC / 2];
+#pragma unroll
+        for (int t = 0; t < NC / 2; ++t) {
+          ex[t] = fmaf(fx, D[2 * t + 1], gx0 * D[2 * t]);
+          dx[t] = D[2 * t + 1] - D[2 * t];
+        }
+        float g_attn, g_x, g_y, g_z = 0.0f;
+        if constexpr (NDIM == 2) {
+          g_attn = fmaf(fy, ex[1], gy0 * ex[0]);
+          g_x = fmaf(fy, dx[1], gy0 * dx[0]);
+          g_y = ex[1] - ex[0];
+        } else {
+          const float fz = pt.f[2], gz0 = __fsub_rn(1.0f, fz);
+          // t = by + 2 * bz
+          const float ey0 = fmaf(fy, ex[1], gy0 * ex[0]);  // z = 0, y-interpolated
+          const float ey1 = fmaf(fy, ex[3], gy0 * ex[2]);  // z = 1
+          g_attn = fmaf(fz, ey1, gz0 * ey0);
+          g_x = fmaf(fz, fmaf(fy, dx[3], gy0 * dx[2]), gz0 * fmaf(fy, dx[1], gy0 * dx[0]));
+          g_y = fmaf(fz, ex[3] - ex[2], gz0 * (ex[1] - ex[0]));
+          g_z = ey1 - ey0;
+        }
+        v[4 * i] = g_attn;
+        v[4 * i + 1] = g_x;
+        v[4 * i + 2] = g_y;
+        v[4 * i + 3] = g_z;
+        sa[i] = a;
+        int32_t pass = 0;
+#pragma unroll
+        for (int ax = 0; ax < NDIM; ++ax) pass |= pt.pass[ax] ? (1 << ax) : 0;
+        sinfo[i] = l | (pass << 8);
+        skey[i] = bucket_key<NDIM>(pt, g.sz, sp.cells[l], kbh + sp.lvl_base[l]);
+        if (++pp == P) { pp = 0; ++l; }
+      }
+    }
+    // transposed reduction over the group
+#pragma unroll
+    for (int s = 1, half = NV / 2; s < NV; s <<= 1, half >>= 1) {
+      if (s < G) {
+        const bool up = (j & s) != 0;
+#pragma unroll
+        for (int t = 0; t < NV / 2; ++t) {
+          if (t < half) {
+            const float send = up ? v[t] : v[t + half];
+            const float keep = up ? v[t + half] : v[t];
+            v[t] = keep + __shfl_xor_sync(gmask, send, s);
+          }
+        }
+      }
+    }
+    for (int s = NV; s < G; s <<= 1) v[0] += __shfl_xor_sync(gmask, v[0], s);
+    if (active && writer) {
+#pragma unroll
+      for (int t = 0; t < NV; ++t) {
+        if (t < nkeep) {
+          const int idx = vbase_i + t;
+          const int slot = idx >> 2, comp = idx & 3;
+          const int s = s0 + slot;
+          if (s < LP) {
+            float a = 0.0f;
+            int32_t info = 0, key = 0;
+#pragma unroll
+            for (int i = 0; i < kDotBatch; ++i)
+              if (i == slot) { a = sa[i]; info = sinfo[i]; key = skey[i]; }
+            const int64_t si = row * LP + s;
+            if (comp == 0) {
+              grad_attn[si] = Elem<TS>::from_f(v[t]);
+              atomicAdd(sp.cnt + key, 1);  // the bucket histogram (result unused: a reduction)
+            } else if (comp - 1 < NDIM) {
+              const int ax = comp - 1, ls = info & 0xff;
+              const float val = ((info >> (8 + ax)) & 1)
+                                    ? a * v[t] * static_cast<float>(p.lv.size[ls][ax]) : 0.0f;
+              grad_loc[si * NDIM + ax] = Elem<TS>::from_f(val);
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ place
+// One thread per sample: its record at the next free slot of its bucket.
+template <typename TS, int NDIM>
+__global__ void __launch_bounds__(kThreads) msda_place_kernel(const Problem p, const SortPlan sp) {
+  const uint32_t s = blockIdx.x * kThreads + threadIdx.x;
+  if (s >= static_cast<uint32_t>(sp.n)) return;
+  const uint32_t rl = fdiv(s, sp.div_p);       // row * L + l
+  const uint32_t row = fdiv(rl, sp.div_l);     // (b * Q + q) * H + h
+  const int32_t l = static_cast<int32_t>(rl - row * static_cast<uint32_t>(p.L));
+  const uint32_t bq = fdiv(row, sp.div_h);
+  const int32_t h = static_cast<int32_t>(row - bq * static_cast<uint32_t>(p.H));
+  const uint32_t b = fdiv(bq, sp.div_q);
+  const Point<NDIM> pt = load_point<TS, NDIM>(
+      static_cast<const TS*>(p.loc) + static_cast<int64_t>(s) * NDIM, p.lv.size[l], p);
+  SRec rec;
+  rec.a = Elem<TS>::to_f(static_cast<const TS*>(p.attn)[s]);
+  rec.f[0] = pt.f[0];
+  rec.f[1] = pt.f[1];
+  rec.f[2] = NDIM == 3 ? pt.f[2] : 0.0f;
+  rec.row = row;
+  rec.key = bucket_key<NDIM>(pt, p.lv.size[l], sp.cells[l],
+                             (static_cast<int32_t>(b) * static_cast<int32_t>(p.H) + h) *
+                                 sp.seg_keys + sp.lvl_base[l]);
+  rec.pad[0] = rec.pad[1] = 0u;
+  // the bucket's cursor: starts at the bucket's start, ends at the next one's
+  const int32_t at = atomicAdd(sp.cnt + rec.key, 1);
+  uint4* dst = reinterpret_cast<uint4*>(sp.srec + at);
+  const uint4* src = reinterpret_cast<const uint4*>(&rec);
+  dst[0] = src[0];
+  dst[1] = src[1];
+}
+
+// ------------------------------------------------------------------ scan
+// Exclusive scan of n int32 counts in place, with data[n] = total, in three
+// launches: per-tile sums, a single-CTA scan of the tile sums, and the tiles'
+// own scans offset by their tile's prefix.
+constexpr int kScanThreads = 256;
+constexpr int kScanPer = 16;
+constexpr int kScanTile = kScanThreads * kScanPer;
+
+__device__ __forceinline__ int32_t block_exclusive_scan(int32_t v, int32_t* warp_tot,
+                                                        int32_t& total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int32_t t = lane < (kScanThreads / 32) ? warp_tot[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    if (lane < (kScanThreads / 32)) warp_tot[lane] = t;  // inclusive warp prefixes
+  }
+  __syncthreads();
+  total = warp_tot[kScanThreads / 32 - 1];
+  const int32_t before = w > 0 ? warp_tot[w - 1] : 0;
+  const int32_t r = before + x - v;
+  __syncthreads();
+  return r;
+}
+
+static __global__ void __launch_bounds__(kScanThreads)
+    msda_scan_reduce_kernel(const int32_t* __restrict__ data, int64_t n, int32_t* __restrict__ bsum) {
+  __shared__ int32_t wt[kScanThreads / 32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile;
+  int32_t sum = 0;
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int64_t k = base + i * kScanThreads + threadIdx.x;
+    if (k < n) sum += data[k];
+  }
+  int32_t total;
+  block_exclusive_scan(sum, wt, total);
+  if (threadIdx.x == 0) bsum[blockIdx.x] = total;
+}
+
+static __global__ void __launch_bounds__(kScanThreads)
+    msda_scan_top_kernel(int32_t* __restrict__ bsum, int32_t nblk) {
+  __shared__ int32_t wt[kScanThreads / 32];
+  int32_t carry = 0;
+  for (int32_t base = 0; base < nblk; base += kScanThreads) {
+    const int32_t k = base + static_cast<int32_t>(threadIdx.x);
+    const int32_t v = k < nblk ? bsum[k] : 0;
+    int32_t total;
+    const int32_t ex = block_exclusive_scan(v, wt, total);
+    if (k < nblk) bsum[k] = carry + ex;
+    carry += total;
+  }
+  if (threadIdx.x == 0) bsum[nblk] = carry;
+}
+
+static __global__ void __launch_bounds__(kScanThreads)
+    msda_scan_down_kernel(int32_t* __restrict__ data, int64_t n, const int32_t* __restrict__ bsum,
+                          int32_t nblk) {
+  __shared__ int32_t tile[kScanTile];
+  __shared__ int32_t wt[kScanThreads / 32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile;
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int idx = i * kScanThreads + threadIdx.x;
+    const int64_t k = base + idx;
+    tile[idx] = k < n ? data[k] : 0;
+  }
+  __syncthreads();
+  int32_t loc[kScanPer];
+  int32_t sum = 0;
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    loc[i] = tile[threadIdx.x * kScanPer + i];
+    sum += loc[i];
+  }
+  int32_t total;
+  int32_t run = block_exclusive_scan(sum, wt, total) + bsum[blockIdx.x];
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    tile[threadIdx.x * kScanPer + i] = run;
+    run += loc[i];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int idx = i * kScanThreads + threadIdx.x;
+    const int64_t k = base + idx;
+    if (k < n) data[k] = tile[idx];
+  }
+  if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) data[n] = bsum[nblk];
+}
+
+
+// ------------------------------------------------------------------ dense levels
+// Value gradient of the dense levels.  One CTA per kWalkChunk sorted
+// positions of one (b, h, dense level) -- each owns exactly Q*P consecutive
+// positions -- cut into segments of one cell, at most kSegMax long.  One lane
+// group per segment: per sample its grad_out row (prefetched one sample
+// ahead) times a * w_corner is added to the cell's 2^d corner gradients in
+// fp32 registers, which are flushed with one vector reduction per corner.
+constexpr int kWalkChunk = 512;
+constexpr int kSegMax = 16;
+
+template <typename T, int NDIM, int VB, int VPL>
+__global__ void __launch_bounds__(kThreads)
+    msda_dense_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
+                      float* __restrict__ gacc) {
+  using CK = Chunk<T, VB>;
+  constexpr int EPV = CK::EPV;
+  constexpr int NC = 1 << NDIM;
+  __shared__ int32_t mkey[kWalkChunk];
+  __shared__ uint32_t mrow[kWalkChunk];
+  __shared__ float4 mf[kWalkChunk];  // (a, fx, fy, fz)
+  __shared__ int32_t seg[kWalkChunk + 1];
+  __shared__ int32_t warp_tot[kThreads / 32];
+
+  const uint32_t u = blockIdx.x;
+  const uint32_t chunk = u % static_cast<uint32_t>(sp.dchunks);
+  const uint32_t r1 = u / static_cast<uint32_t>(sp.dchunks);
+  const int kd = static_cast<int>(r1 % static_cast<uint32_t>(sp.ndl));
+  const uint32_t bh = r1 / static_cast<uint32_t>(sp.ndl);
+  const int l = sp.dl_level[kd];
+  const int64_t qp = p.Q * p.P;
+  const int64_t base = (static_cast<int64_t>(bh) * p.L + l) * qp + int64_t{chunk} * kWalkChunk;
+  const int cnt = static_cast<int>(min(static_cast<int64_t>(kWalkChunk),
+                                       qp - int64_t{chunk} * kWalkChunk));
+  for (int t = threadIdx.x; t < cnt; t += kThreads) {
+    const SRec rec = sp.srec[base + t];
+    mkey[t] = rec.key;
+    mrow[t] = rec.row;
+    mf[t] = make_float4(rec.a, rec.f[0], rec.f[1], rec.f[2]);
+  }
+  __syncthreads();
+  {
+    const int t0 = 2 * threadIdx.x;
+    bool h0 = false, h1 = false;
+    if (t0 < cnt) h0 = (t0 % kSegMax == 0) || mkey[t0] != mkey[t0 - 1];
+    if (t0 + 1 < cnt) h1 = ((t0 + 1) % kSegMax == 0) || mkey[t0 + 1] != mkey[t0];
+    int32_t total;
+    const int32_t off = block_exclusive_scan(static_cast<int32_t>(h0) + static_cast<int32_t>(h1),
+                                             warp_tot, total);
+    if (h0) seg[off] = t0;
+    if (h1) seg[off + (h0 ? 1 : 0)] = t0 + 1;
+    if (threadIdx.x == 0) seg[total] = cnt;
+    __syncthreads();
+    if (threadIdx.x == 0) warp_tot[0] = total;
+    __syncthreads();
+  }
+  const int nseg = warp_tot[0];
+
+  const int G = 1 << sp.dlog2g;
+  const int ng = kThreads >> sp.dlog2g;
+  const int grp = static_cast<int>(threadIdx.x) >> sp.dlog2g;
+  const int j = static_cast<int>(threadIdx.x) & (G - 1);
+  const int64_t row_bytes = p.C * static_cast<int64_t>(sizeof(T));
+  const int32_t cx = sp.cells[l][0], cy = sp.cells[l][1];
+  const int32_t ncell = cx * cy * sp.cells[l][2];
+  const int32_t kl = static_cast<int32_t>(bh) * sp.seg_keys + sp.lvl_base[l];
+  const int32_t sz0 = p.lv.size[l][0], sz1 = p.lv.size[l][1], sz2 = p.lv.size[l][2];
+  const int32_t b = static_cast<int32_t>(bh / static_cast<uint32_t>(p.H));
+  const int32_t h = static_cast<int32_t>(bh - static_cast<uint32_t>(b) * static_cast<uint32_t>(p.H));
+  const int64_t kshift = p.acc_compact ? p.acc_start[l] : p.lv.start[l];
+  float* gbase = gacc + ((static_cast<int64_t>(b) * p.acc_keys + kshift) * p.H + h) * p.C + j * EPV;
+  bool has[VPL];
+#pragma unroll
+  for (int v = 0; v < VPL; ++v) has[v] = (j + v * G < sp.dnv);
+
+  for (int sg = grp; sg < nseg; sg += ng) {
+    const int ta = seg[sg], tb = seg[sg + 1];
+    const int32_t c = mkey[ta] - kl;
+    if (c >= ncell) continue;  // the dead bucket: no corner inside the level
+    // the cell's lower corner and which of its corners lie inside the level
+    const int32_t ix = c % cx - 1;
+    const int32_t iy = (c / cx) % cy - 1;
+    const int32_t iz = NDIM == 3 ? c / (cx * cy) - 1 : 0;
+    uint32_t vbits = 0;
+#pragma unroll
+    for (int cc = 0; cc < NC; ++cc) {
+      const int32_t x = ix + (cc & 1), y = iy + ((cc >> 1) & 1), z = iz + ((cc >> 2) & 1);
+      const bool ok = static_cast<uint32_t>(x) < static_cast<uint32_t>(sz0) &&
+                      static_cast<uint32_t>(y) < static_cast<uint32_t>(sz1) &&
+                      (NDIM == 2 || static_cast<uint32_t>(z) < static_cast<uint32_t>(sz2));
+      vbits |= ok ? (1u << cc) : 0u;
+    }
+    float acc[NC][VPL][EPV];
+#pragma unroll
+    for (int cc = 0; cc < NC; ++cc)
+#pragma unroll
+      for (int v = 0; v < VPL; ++v)
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) acc[cc][v][e] = 0.0f;
+    Raw<VB> gnext[VPL];
+    {
+      const char* gr = reinterpret_cast<const char*>(grad_out) +
+                       static_cast<int64_t>(mrow[ta]) * row_bytes + j * VB;
+#pragma unroll
+      for (int v = 0; v < VPL; ++v) gnext[v] = has[v] ? ld_chunk<VB>(gr + v * G * VB) : raw_zero<VB>();
+    }
+    for (int t = ta; t < tb; ++t) {
+      float go[VPL][EPV];
+#pragma unroll
+      for (int v = 0; v < VPL; ++v) CK::unpack(gnext[v], go[v]);
+      if (t + 1 < tb) {
+        const char* gr = reinterpret_cast<const char*>(grad_out) +
+                         static_cast<int64_t>(mrow[t + 1]) * row_bytes + j * VB;
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) gnext[v] = has[v] ? ld_chunk<VB>(gr + v * G * VB) : raw_zero<VB>();
+      }
+      const float4 af = mf[t];
+      const float fr[3] = {af.y, af.z, af.w};
+      float wt[3][2];
+#pragma unroll
+      for (int ax = 0; ax < 3; ++ax) {
+        if (ax < NDIM) { wt[ax][0] = __fsub_rn(1.0f, fr[ax]); wt[ax][1] = fr[ax]; }
+        else { wt[ax][0] = 1.0f; wt[ax][1] = 0.0f; }
+      }
+#pragma unroll
+      for (int cc = 0; cc < NC; ++cc) {
+        float w = __fmul_rn(wt[0][cc & 1], wt[1][(cc >> 1) & 1]);
+        if (NDIM == 3) w = __fmul_rn(w, wt[2][(cc >> 2) & 1]);
+        const float aw = af.x * w;
+#pragma unroll
+        for (int v = 0; v < VPL; ++v)
+#pragma unroll
+          for (int e = 0; e < EPV; ++e) acc[cc][v][e] = fmaf(aw, go[v][e], acc[cc][v][e]);
+      }
+    }
+    const int32_t k0 = (iz * sz1 + iy) * sz0 + ix;
+#pragma unroll
+    for (int cc = 0; cc < NC; ++cc) {
+      if (!((vbits >> cc) & 1u)) continue;
+      const int32_t k = k0 + (cc & 1) + ((cc >> 1) & 1) * sz0 + ((cc >> 2) & 1) * sz0 * sz1;
+      float* dst = gbase + static_cast<int64_t>(k) * p.H * p.C;
+#pragma unroll
+      for (int v = 0; v < VPL; ++v)
+        if (has[v]) red_add_f32<EPV>(dst + v * G * EPV, acc[cc][v]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ voxel gather
+// Value gradient of the sparse levels.  One CTA per tile of NY voxel rows x TX
+// voxels at one (b, h, level, z), one thread per voxel (up to kThreads).
+// Voxel (x, y, z) is a corner of the cells with lower corner (x-1 or x, y-1
+// or y, z-1 or z), so the tile's samples lie in the cell rows (y', z') =
+// (y0-1 .. y0+NY-1, z-1 .. z), each row's cells x0-1 .. x0+TX-1 being one
+// contiguous range of the sorted records.  The CTA stages, in rounds of
+// sp.vcap samples: the range bounds, then per sample its four (bx, by)
+// corner weights a * w (the reference's product order) and its grad_out row
+// (rows padded by 16 bytes so the lanes' row reads spread over the banks).
+// Each thread then walks, for each of the 2^(d-1) cell rows its voxel
+// touches, the samples of cells x-1 (its upper-x corner) and x (lower-x
+// corner), summing a * w_corner * grad_out over all C channels in fp32
+// registers, kVoxChunks row chunks per pass; the row is stored once.
+constexpr int kVoxChunks = 2;
+
+template <typename T, int NDIM, int VB, int VPL>
+__global__ void __launch_bounds__(kThreads, 6)
+    msda_voxel_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
+                      T* __restrict__ grad_value) {
+  using CK = Chunk<T, VB>;
+  constexpr int EPV = CK::EPV;
+  extern __shared__ __align__(16) unsigned char vsm[];
+  const int64_t row_bytes = p.C * static_cast<int64_t>(sizeof(T));
+  const int rowb = static_cast<int>(row_bytes);
+  const int rowp = rowb + 16;  // staged row stride
+  const int nv = sp.vnv;       // VB-byte chunks per row
+
+  // unit -> (b, h, voxel level, z, y tile, x tile)
+  const uint32_t u = blockIdx.x;
+  const uint32_t bh = u / static_cast<uint32_t>(sp.units_per_bh);
+  uint32_t rem = u - bh * static_cast<uint32_t>(sp.units_per_bh);
+  int k = 0;
+  while (k + 1 < sp.nvl && rem >= static_cast<uint32_t>(sp.vl_ubase[k + 1])) ++k;
+  rem -= static_cast<uint32_t>(sp.vl_ubase[k]);
+  const int l = sp.vl_level[k];
+  const VoxTile vt = sp.vl_tile[k];
+  const int32_t W = p.lv.size[l][0], Hs = p.lv.size[l][1];
+  const uint32_t xt = rem % static_cast<uint32_t>(vt.ntx);
+  const uint32_t r2 = rem / static_cast<uint32_t>(vt.ntx);
+  const uint32_t yt = r2 % static_cast<uint32_t>(vt.nty);
+  const int32_t vz = static_cast<int32_t>(r2 / static_cast<uint32_t>(vt.nty));
+  const int32_t x0 = static_cast<int32_t>(xt) * vt.tx;
+  const int32_t y0 = static_cast<int32_t>(yt) * vt.ny;
+  const int32_t b = static_cast<int32_t>(bh / static_cast<uint32_t>(p.H));
+  const int32_t h = static_cast<int32_t>(bh - static_cast<uint32_t>(b) * static_cast<uint32_t>(p.H));
+  const int32_t cxn = sp.cells[l][0], cyn = sp.cells[l][1];
+  const int32_t kb = static_cast<int32_t>(bh) * sp.seg_keys + sp.lvl_base[l];
+  const int nyr = vt.ny + 1;                       // cell rows per z
+  const int ncr = (NDIM == 3 ? 2 : 1) * nyr;       // cell rows
+  const int cw = vt.tx + 2;                        // bounds per cell row
+
+  float4* ws = reinterpret_cast<float4*>(vsm);                          // vcap
+  unsigned char* go_s = vsm + static_cast<size_t>(sp.vcap) * 16;       // vcap * rowp
+  uint32_t* rows_s = reinterpret_cast<uint32_t*>(go_s + static_cast<size_t>(sp.vcap) * rowp);
+  int32_t* cnt_s = reinterpret_cast<int32_t*>(rows_s + sp.vcap);       // ncr * cw
+  int32_t* off_s = cnt_s + ncr * cw;                                    // ncr + 1
+
+  // range bounds: cnt_s[cr][c] = start of cell x0-1+c of cell row cr
+  for (int cr = 0; cr < ncr; ++cr) {
+    const int dz = (NDIM == 3 && cr >= nyr) ? 1 : 0;
+    const int32_t yc = y0 - 1 + (cr - dz * nyr);  // the cell row's i0y
+    const int32_t zc = NDIM == 3 ? vz - dz : -1;
+    const int32_t krow = kb + ((zc + 1) * cyn + (yc + 1)) * cxn;
+    for (int c = threadIdx.x; c < cw; c += kThreads)  // rows outside the level are empty;
+      cnt_s[cr * cw + c] =                            // past the row end: its end bound
+          yc <= Hs - 1 ? __ldg(sp.start + krow + min(x0 + c, cxn)) : 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t o = 0;
+    for (int cr = 0; cr < ncr; ++cr) {
+      off_s[cr] = o;
+      o += cnt_s[cr * cw + cw - 1] - cnt_s[cr * cw];
+    }
+    off_s[ncr] = o;
+  }
+  __syncthreads();
+  const int32_t total = off_s[ncr];
+
+  // this thread's voxel
+  const int ry = static_cast<int>(threadIdx.x) / vt.tx;
+  const int xl = static_cast<int>(threadIdx.x) - ry * vt.tx;
+  const bool active = ry < vt.ny && y0 + ry < Hs && x0 + xl < W;
+  char* dst = nullptr;
+  if (active) {
+    const int64_t key = static_cast<int64_t>(p.lv.start[l]) +
+                        (static_cast<int64_t>(vz) * Hs + y0 + ry) * W + x0 + xl;
+    dst = reinterpret_cast<char*>(grad_value) + ((static_cast<int64_t>(b) * p.K + key) * p.H + h) * row_bytes;
+  }
+
+  for (int c0 = 0; c0 < nv; c0 += kVoxChunks) {
+    float acc[kVoxChunks][EPV];
+#pragma unroll
+    for (int m = 0; m < kVoxChunks; ++m)
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) acc[m][e] = 0.0f;
+    for (int32_t q0 = 0; q0 < total; q0 += sp.vcap) {
+      const int nr = min(sp.vcap, total - q0);
+      if (c0 == 0 || total > sp.vcap) {
+        // stage the round's weights and grad_out rows
+        if (q0 > 0 || c0 > 0) __syncthreads();
+        for (int q = threadIdx.x; q < nr; q += kThreads) {
+          const int32_t qq = q0 + q;
+          int lo = 0, hi = ncr;  // cell row: off_s[lo] <= qq < off_s[lo + 1]
+          while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (off_s[mid] <= qq) lo = mid; else hi = mid;
+          }
+          const int32_t pos = cnt_s[lo * cw] + (qq - off_s[lo]);
+          const SRec rec = sp.srec[pos];
+          const int dz = (NDIM == 3 && lo >= nyr) ? 1 : 0;
+          const float wx0 = __fsub_rn(1.0f, rec.f[0]), wx1 = rec.f[0];
+          const float wy0 = __fsub_rn(1.0f, rec.f[1]), wy1 = rec.f[1];
+          float w00 = __fmul_rn(wx0, wy0), w01 = __fmul_rn(wx0, wy1);
+          float w10 = __fmul_rn(wx1, wy0), w11 = __fmul_rn(wx1, wy1);
+          if (NDIM == 3) {
+            const float wz = dz ? rec.f[2] : __fsub_rn(1.0f, rec.f[2]);
+            w00 = __fmul_rn(w00, wz); w01 = __fmul_rn(w01, wz);
+            w10 = __fmul_rn(w10, wz); w11 = __fmul_rn(w11, wz);
+          }
+          ws[q] = make_float4(rec.a * w00, rec.a * w01, rec.a * w10, rec.a * w11);
+          rows_s[q] = rec.row;
+        }
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < nr * nv; idx += kThreads) {
+          const int q = static_cast<int>(fdiv(static_cast<uint32_t>(idx), sp.div_nv));
+          const int c = idx - q * nv;
+          const char* src = reinterpret_cast<const char*>(grad_out) +
+                            static_cast<int64_t>(rows_s[q]) * row_bytes + c * VB;
+          st_chunk<VB>(go_s + static_cast<size_t>(q) * rowp + c * VB, ld_chunk<VB>(src));
+        }
+        __syncthreads();
+      }
+      if (active) {
+#pragma unroll
+        for (int dz = 0; dz < (NDIM == 3 ? 2 : 1); ++dz) {
+#pragma unroll
+          for (int dy = 0; dy < 2; ++dy) {
+            const int cr = dz * nyr + (ry - dy + 1);
+            const int32_t* crp = cnt_s + cr * cw + xl;
+            const int32_t slot0 = off_s[cr] - cnt_s[cr * cw] - q0;  // position -> round slot
+            const int32_t qa = max(crp[0] + slot0, 0);
+            const int32_t qs = crp[1] + slot0;  // cell x-1 | cell x
+            const int32_t qb = min(crp[2] + slot0, nr);
+            for (int32_t q = qa; q < qb; ++q) {
+              const float4 w4 = ws[q];
+              // cell x-1: this voxel is its upper-x corner (bx = 1); cell x: lower (bx = 0)
+              const float w = q < qs ? (dy ? w4.w : w4.z) : (dy ? w4.y : w4.x);
+              const unsigned char* gq = go_s + static_cast<size_t>(q) * rowp + c0 * VB;
+#pragma unroll
+              for (int m = 0; m < kVoxChunks; ++m) {
+                if (c0 + m < nv) {
+                  float go[EPV];
+                  CK::unpack(ld_shared_chunk<VB>(gq + m * VB), go);
+#pragma unroll
+                  for (int e = 0; e < EPV; ++e) acc[m][e] = fmaf(w, go[e], acc[m][e]);
+                }
+              }
+            }
+          }
+        }
+      }
+    }
+    if (active) {
+#pragma unroll
+      for (int m = 0; m < kVoxChunks; ++m)
+        if (c0 + m < nv) st_chunk<VB>(dst + (c0 + m) * VB, CK::pack(acc[m]));
+    }
+  }
+}
+
+}  // namespace msda

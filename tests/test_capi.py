@@ -50,10 +50,15 @@ def _ws(dtype, B, shapes, H, C, Q, P, on_dev=0):
 
 def test_workspace_bytes_gather_path(monkeypatch):
     # The gather/scatter backward: nothing for fp32; for 16-bit values an fp32
-    # accumulator over the keys of the levels with more than 8 expected
-    # contributions per element (2^d * Q * P / voxels) -- sparser levels
-    # reduce straight into grad_value.
+    # accumulator over every key by default.
+    monkeypatch.delenv("MSDA_BWD_DIRECT16", raising=False)
     assert _ws(_lib.FLOAT32, 2, [(10, 10)], 8, 32, 50, 4) == 0
+    assert _ws(_lib.BFLOAT16, 2, [(10, 10)], 8, 32, 50, 4) == 2 * 100 * 8 * 32 * 4
+    assert _ws(_lib.FLOAT16, 2, [(10, 10), (5, 5)], 8, 32, 50, 4) == 2 * 125 * 8 * 32 * 4
+    # Opt-in (MSDA_BWD_DIRECT16=1): levels with at most 8 expected
+    # contributions per element (2^d * Q * P / voxels) reduce straight into
+    # grad_value; only the busier levels keep accumulator rows.
+    monkeypatch.setenv("MSDA_BWD_DIRECT16", "1")
     # 4 * 50 * 4 / 100 = 8 contributions: direct, no workspace
     assert _ws(_lib.BFLOAT16, 2, [(10, 10)], 8, 32, 50, 4) == 0
     # 4 * 51 * 4 / 100 > 8: the whole level in fp32
@@ -63,23 +68,41 @@ def test_workspace_bytes_gather_path(monkeypatch):
     # 3D: 8 corners per sample
     assert _ws(_lib.BFLOAT16, 1, [(8, 8, 8), (4, 4, 4)], 2, 16, 128, 4) == 64 * 2 * 16 * 4
     assert _ws(_lib.FLOAT16, 0, [(10, 10)], 8, 32, 50, 4) == 0
-    # the switch that keeps every level in fp32
-    monkeypatch.setenv("MSDA_BWD_DIRECT16", "0")
-    assert _ws(_lib.BFLOAT16, 2, [(10, 10), (5, 5)], 8, 32, 50, 4) == 2 * 125 * 8 * 32 * 4
 
 
-def test_workspace_bytes_binned_path(monkeypatch):
-    # Host shapes, binned backward selected: records (at most 2^d per sample)
-    # plus bucket tables; far below the fp32 accumulator.
-    monkeypatch.setenv("MSDA_BWD_PATH", "binned")
+def _align(x):
+    return (x + 255) // 256 * 256
+
+
+def test_workspace_bytes_sorted_path(monkeypatch):
+    # Host shapes and >= 2^20 samples: the cell-sorted backward.  Its
+    # workspace: bucket counts (one per cell of the (W+1)(H+1)(D+1) grid plus
+    # a dead bucket, per level and (b, h), plus two), scan block sums, a
+    # 32-byte record per sample, and the fp32 accumulator of the levels with
+    # more than 6 samples per cell.
+    monkeypatch.setenv("MSDA_BWD_PATH", "sorted")
+    monkeypatch.delenv("MSDA_VOXEL_DENSITY", raising=False)
+    monkeypatch.delenv("MSDA_SORTED_CHUNK_B", raising=False)
     B, H, C, Q, P = 2, 8, 32, 20000, 4
     shapes = [(32, 64, 64), (16, 32, 32), (8, 16, 16)]
-    ws = _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P)
-    samples = B * Q * H * len(shapes) * P
-    assert samples * 8 * 4 <= ws < samples * 8 * 4 + 64 * 2**20
+    cells = [int(np.prod([s + 1 for s in sh])) for sh in shapes]
+    dense = [c for c, sh in zip(cells, shapes) if Q * P / c > 6.0]
+    assert len(dense) == 1  # only the coarsest level is aggregated per cell
+    acc_keys = int(np.prod(shapes[-1]))
+    nkeys = B * H * sum(c + 1 for c in cells)
+    n = B * Q * H * len(shapes) * P
+    nblk = (nkeys + 4095) // 4096
+    expect = (_align((nkeys + 2) * 4) + _align((nblk + 1) * 4) + _align(n * 32)
+              + _align(B * acc_keys * H * C * 4))
+    assert _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P) == expect
+    # fp32 values reduce the dense levels straight into grad_value: no accumulator
+    assert _ws(_lib.FLOAT32, B, shapes, H, C, Q, P) == expect - _align(B * acc_keys * H * C * 4)
     # device-resident shapes cannot be planned on the host: gather path
     K = sum(int(np.prod(s)) for s in shapes)
     assert _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P, on_dev=1) == B * K * H * C * 4
+    # MSDA_BWD_PATH=scatter keeps the gather/scatter plan (fp32 accumulator)
+    monkeypatch.setenv("MSDA_BWD_PATH", "scatter")
+    assert _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P) == B * K * H * C * 4
 
 
 # A fake device address: every case below fails validation on the host before
@@ -189,8 +212,9 @@ def test_fused_workspace_is_the_gather_plan(monkeypatch):
         return lib.msda_fused_bwd_workspace_bytes(3, _lib.BFLOAT16, B, K, H, C, shp.ctypes.data,
                                                   0, len(shapes), Q, P)
 
+    monkeypatch.setenv("MSDA_BWD_PATH", "scatter")
     gather = _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P)
     assert fused() == gather
-    monkeypatch.setenv("MSDA_BWD_PATH", "binned")
-    assert _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P) != gather  # the plain entry switches
+    monkeypatch.setenv("MSDA_BWD_PATH", "sorted")
+    assert _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P) != gather  # the plain entry sorts
     assert fused() == gather

@@ -1,11 +1,14 @@
-"""Backward of 16-bit values with per-level value-gradient targets.
+"""Backward of 16-bit values with per-level value-gradient targets, the
+opt-in mode of the gather/scatter backward (MSDA_BWD_DIRECT16=1).
 
 Levels with at most 8 expected contributions per grad_value element reduce
 with 16-bit vector reductions straight into grad_value (as the reference's
 atomic_add into a grad_value of the input dtype does); busier levels keep
 fp32 accumulation in a workspace that holds only their keys, rounded into
-grad_value by a cast kernel.  Every case below mixes the two and is checked
-against the oracle at the half-precision bar.
+grad_value by a cast kernel.  Every case below mixes the two, on uniformly
+spread locations (the assumption of the contribution bound), and is checked
+against the oracle at the half-precision bar.  The default keeps every level
+in fp32 (clustered locations: tests/test_sorted_gpu.py).
 """
 
 from __future__ import annotations
@@ -21,6 +24,12 @@ from tests.test_msda_gpu import check_all, cuda_fwd_bwd, oracle_all
 pytestmark = pytest.mark.gpu
 
 HALF = [torch.bfloat16, torch.float16]
+
+
+@pytest.fixture(autouse=True)
+def direct16_scatter(monkeypatch):
+    monkeypatch.setenv("MSDA_BWD_PATH", "scatter")
+    monkeypatch.setenv("MSDA_BWD_DIRECT16", "1")
 
 
 def _workspace(ndim, dtype, B, shapes, H, C, Q, P):

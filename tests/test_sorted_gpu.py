@@ -1,0 +1,168 @@
+"""The cell-sorted backward (msda_sorted.cuh) against the oracle and the
+reference's golden vectors.
+
+The sorted pipeline is the default backward for large problems with host
+shapes; these tests force it (MSDA_BWD_PATH=sorted) on small problems so the
+oracle finishes in seconds, and steer every level through both ways of
+forming the value gradient: gathered per value row (MSDA_VOXEL_DENSITY high)
+and aggregated per cell with fp32 reductions (MSDA_VOXEL_DENSITY=0).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from msda_triton_b200 import _lib
+from tests._util import TOL_FWD_F32, TOL_GRAD_F32, TOL_HALF, make_inputs
+from tests.conftest import golden_names, load_golden
+from tests.test_msda_gpu import check_all, cuda_fwd_bwd, oracle_all
+
+pytestmark = pytest.mark.gpu
+
+# voxel-density thresholds: every level gathered / default split / every level aggregated
+SPLITS = {"voxel": "1e9", "auto": None, "cell": "0"}
+
+
+def _env(monkeypatch, split="auto", chunk=None, path="sorted"):
+    monkeypatch.setenv("MSDA_BWD_PATH", path)
+    if SPLITS[split] is None:
+        monkeypatch.delenv("MSDA_VOXEL_DENSITY", raising=False)
+    else:
+        monkeypatch.setenv("MSDA_VOXEL_DENSITY", SPLITS[split])
+    if chunk is None:
+        monkeypatch.delenv("MSDA_SORTED_CHUNK_B", raising=False)
+    else:
+        monkeypatch.setenv("MSDA_SORTED_CHUNK_B", str(chunk))
+
+
+def _tols(dtype):
+    return (TOL_FWD_F32, TOL_GRAD_F32) if dtype == torch.float32 else (TOL_HALF, TOL_HALF)
+
+
+def _cast(inp, vdt, sdt):
+    value, shp, loc, attn, go = inp
+    return value.to(vdt), shp, loc.to(sdt), attn.to(sdt), go.to(vdt)
+
+
+def _upcast(inp):
+    return [x.float() if x.is_floating_point() else x for x in inp]
+
+
+@pytest.mark.parametrize("split", ["voxel", "cell"])
+@pytest.mark.parametrize("name", golden_names())
+def test_golden_parity_sorted(monkeypatch, name, split):
+    """Every golden fixture through the sorted backward, each level formed
+    both ways, against the reference's own outputs."""
+    _env(monkeypatch, split)
+    z = load_golden(name)
+    t = {k: torch.from_numpy(z[k]) for k in ("value", "loc", "attn", "grad_out", "shapes")}
+    ndim = t["shapes"].shape[1]
+    got = cuda_fwd_bwd(ndim, t["value"], t["shapes"], t["loc"], t["attn"], t["grad_out"],
+                       bool(z["clamp"]), float(z["eps"]))
+    ref = [torch.from_numpy(z[k]) for k in ("out", "grad_value", "grad_loc", "grad_attn")]
+    check_all(got, ref, TOL_FWD_F32, TOL_GRAD_F32, f"{name} sorted/{split}")
+
+
+CASES = [
+    # ndim, B, Q, H, C, P, shapes
+    (2, 2, 700, 4, 32, 4, [(40, 60), (20, 30), (10, 15), (5, 8)]),
+    (3, 2, 900, 4, 32, 4, [(16, 24, 24), (8, 12, 12), (4, 6, 6)]),
+    (3, 3, 400, 8, 16, 2, [(3, 4, 4), (12, 16, 20), (2, 3, 3)]),
+    (2, 1, 300, 3, 64, 3, [(7, 9), (1, 1), (30, 2)]),
+]
+DTYPES = [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16),
+          (torch.float16, torch.float16), (torch.bfloat16, torch.float32),
+          (torch.float16, torch.float32)]
+
+
+@pytest.mark.parametrize("split", ["voxel", "auto", "cell"])
+@pytest.mark.parametrize("dt", DTYPES, ids=lambda d: f"{str(d[0])[6:]}-{str(d[1])[6:]}")
+@pytest.mark.parametrize("case", CASES, ids=[f"{c[0]}d-{len(c[6])}lvl-q{c[2]}" for c in CASES])
+def test_sorted_matches_oracle(monkeypatch, case, dt, split):
+    ndim, B, Q, H, C, P, shapes = case
+    _env(monkeypatch, split)
+    tf, tg = _tols(dt[0])
+    for clamp, rng in ((True, (0.0, 1.0)), (False, (-0.15, 1.15))):
+        inp = _cast(make_inputs(B, Q, H, C, P, shapes, seed=Q + C + ndim, loc_range=rng), *dt)
+        got = cuda_fwd_bwd(ndim, *inp, clamp=clamp)
+        ref = oracle_all(*_upcast(inp), clamp=clamp)
+        check_all(got, ref, tf, tg, f"{case} {dt} {split} clamp={clamp}")
+
+
+@pytest.mark.parametrize("ndim", [2, 3])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_chunks_match_one_pass(monkeypatch, ndim, dtype):
+    """Batch entries split over chunks (one, two, then all at once) give the
+    oracle's result, each chunk reusing the same workspace."""
+    shapes = [(30, 40), (15, 20), (8, 10)] if ndim == 2 else [(12, 16, 16), (6, 8, 8), (3, 4, 4)]
+    inp = _cast(make_inputs(5, 300, 4, 32, 4, shapes, seed=7 + ndim), dtype, dtype)
+    ref = oracle_all(*_upcast(inp))
+    tf, tg = _tols(dtype)
+    for chunk in (1, 2, None):
+        _env(monkeypatch, "auto", chunk)
+        got = cuda_fwd_bwd(ndim, *inp)
+        check_all(got, ref, tf, tg, f"chunk={chunk}")
+
+
+@pytest.mark.parametrize("ndim", [2, 3])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_sorted_and_scatter_paths_agree(monkeypatch, ndim, dtype):
+    """The two backward plans on one problem: the forward is the same kernel
+    (bitwise equal), every gradient agrees at the parity bar (the per-sample
+    sums run in another order)."""
+    shapes = [(40, 50), (20, 25), (10, 12)] if ndim == 2 else [(16, 20, 20), (8, 10, 10), (4, 5, 5)]
+    inp = _cast(make_inputs(2, 800, 8, 32, 4, shapes, seed=31 + ndim), dtype, dtype)
+    _env(monkeypatch, "auto")
+    srt = cuda_fwd_bwd(ndim, *inp)
+    _env(monkeypatch, path="scatter")
+    sct = cuda_fwd_bwd(ndim, *inp)
+    assert torch.equal(srt[0], sct[0])
+    tol = TOL_GRAD_F32 if dtype == torch.float32 else TOL_HALF
+    check_all(srt, sct, tol, tol, "sorted vs scatter")
+
+
+def _clustered(ndim, B, Q, H, C, P, shapes, box, seed, dtype):
+    """Every sample of level 0 inside a box of `box` cells per axis at the
+    centre of the level (hundreds of samples per cell), the other levels
+    uniform."""
+    value, shp, loc, attn, go = make_inputs(B, Q, H, C, P, shapes, seed=seed)
+    g = torch.Generator().manual_seed(seed + 1)
+    for ax in range(ndim):
+        n = shapes[0][ndim - 1 - ax]  # (x, y, z) -> W, H, D
+        lo = (n // 2 - box / 2) / n
+        loc[:, :, :, 0, :, ax] = lo + torch.rand(B, Q, H, P, generator=g) * (box / n)
+    return _cast((value, shp, loc, attn, go), dtype, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("ndim", [2, 3])
+@pytest.mark.parametrize("path", ["sorted", "scatter"])
+def test_clustered_samples_half_precision(monkeypatch, ndim, dtype, path):
+    """Hundreds of contributions per grad_value element on a level the
+    density plan rates sparse: every fp16/bf16 backward stays within the
+    half-precision bar of the fp32 oracle."""
+    shapes = [(64, 96), (32, 48), (16, 24)] if ndim == 2 else [(24, 32, 32), (12, 16, 16), (6, 8, 8)]
+    inp = _clustered(ndim, 2, 2000, 4, 32, 4, shapes, 4, 11 + ndim, dtype)
+    _env(monkeypatch, "auto", path=path)
+    got = cuda_fwd_bwd(ndim, *inp)
+    ref = oracle_all(*_upcast(inp))
+    check_all(got, ref, TOL_HALF, TOL_HALF, f"clustered {dtype} {path}")
+
+
+def test_workspace_reports_sorted_plan(monkeypatch):
+    """The workspace query follows the plan: the sorted plan needs per-sample
+    and per-cell arrays, the scatter plan only the fp32 accumulator."""
+    shapes = np.array([(16, 24, 24), (8, 12, 12)], dtype=np.int32)
+    K = int(np.prod(shapes, axis=1).sum())
+    B, Q, H, C, P = 2, 900, 4, 32, 4
+    q = lambda: _lib.lib().msda_bwd_workspace_bytes(3, _lib.BFLOAT16, B, K, H, C,
+                                                     shapes.ctypes.data, 0, 2, Q, P)
+    _env(monkeypatch, "auto")
+    sorted_ws = q()
+    _env(monkeypatch, path="scatter")
+    scatter_ws = q()
+    samples = B * Q * H * 2 * P
+    assert sorted_ws >= samples * 32
+    assert scatter_ws == B * K * H * C * 4
