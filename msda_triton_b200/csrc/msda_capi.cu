@@ -413,25 +413,22 @@ struct BwdPlan {
   int64_t chunk_b = 0;    // batch entries per chunk
   int64_t smp_per_b = 0;  // samples per batch entry
   int64_t keys_per_b = 0; // bucket keys per batch entry
-  size_t soff[4] = {};    // bucket counts (one leading zero), bsum, srec, acc
+  size_t soff[5] = {};    // bucket counts, bsum, ranks, srec, acc
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
 
 // ------------------------------------------------------------ sorted plan
 // The cell-sorted backward runs when the level shapes are on the host and the
-// problem is large enough to amortise its nine launches.  Per level it
-// picks how the value gradient is formed: gathered per value row (levels
-// with at most kVoxelMaxDensity samples per cell and (b, h): each sample is
-// read by its 2^d corner rows) or aggregated per cell in registers and
-// flushed with fp32 reductions (denser levels: one flush per cell).  The
-// break-even follows from the measured B200 rates of 64-byte row gathers
-// (250 G rows/s) and 128-byte fp32 reductions (47 G rows/s).
+// problem is large enough to amortise its launches.  Per level it picks how
+// the value gradient is formed: gathered per value row (levels with at most
+// kVoxelMaxDensity samples per cell and (b, h)) or aggregated per cell in
+// registers and flushed with fp32 reductions (denser levels).  Measured on
+// the 3D xl workload (B=8, bf16): level 0 (0.38 samples per cell) 6.9 ms
+// gathered; level 1 (3.0 per cell) 7.5 ms gathered against ~2 ms aggregated.
 constexpr int64_t kSortedMinSamples = int64_t{1} << 20;
-constexpr double kVoxelMaxDensity = 6.0;
-// The gather/scatter backward stays the default until the sorted pipeline
-// outruns it on the benchmark shapes (MSDA_BWD_PATH=sorted selects it).
-constexpr bool kSortedByDefault = false;
+constexpr double kVoxelMaxDensity = 2.0;
+constexpr bool kSortedByDefault = true;
 
 FastDiv make_fdiv(uint32_t d) {
   if (d == 0) d = 1;
@@ -461,13 +458,14 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   // row allows); shapes it is not instantiated for keep every level dense.
   if (!((ls.vb == 16 && ls.vpl <= 4) || ((ls.vb == 4 || ls.vb == 2) && ls.vpl == 1)))
     max_dens = -1.0;
-  const int tile_max = kThreads;                     // voxels per voxel-kernel CTA (one per thread)
+  const int tile_max = (kThreads / 32) * 32;         // voxels per voxel-kernel CTA (a warp per 32)
   const int64_t row_bytes = a.C * dtype_bytes(a.vdt);
-  // samples the voxel kernel stages per round: as many as fit 40 KB of shared
-  // memory next to the range bounds, at most 512
+  // samples the voxel kernel stages per round: as many as fit next to the
+  // warps' accumulators (32 KB) and the range bounds in 72 KB, at most 512
   const int64_t bounds_max = int64_t{4} * (tile_max + 2) * 4 + 4 * 64;
-  // per staged sample: weights (16 B), grad_out row index (4 B), grad_out row + 16 B pad
-  int64_t cap = (40 * 1024 - bounds_max) / (36 + row_bytes);
+  const int64_t acc_bytes = int64_t{kThreads / 32} * 32 * 32 * 4;
+  // per staged sample: its record (32 B), cell row / x offset (4 B), grad_out row
+  int64_t cap = (72 * 1024 - acc_bytes - bounds_max) / (36 + row_bytes);
   cap = std::min<int64_t>(cap, 512) & ~int64_t{1};
   if (cap < 16) max_dens = -1.0;
   SortPlan sp{};
@@ -490,8 +488,10 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
       // tile: up to tile_max voxels, NY rows of TX; fewer rows when the
       // expected samples of its cell rows pass two staging rounds
       const int64_t W = p.lv.size[l][0], Hl = p.lv.size[l][1];
+      // rows of up to 8 segments of 32 voxels (a warp each)
       const int64_t tx = std::min<int64_t>(W, tile_max);
-      int64_t ny = std::max<int64_t>(1, std::min<int64_t>(tile_max / tx, Hl));
+      const int64_t segs = (tx + 31) / 32;
+      int64_t ny = std::max<int64_t>(1, std::min<int64_t>((kThreads / 32) / segs, Hl));
       const int zr = a.ndim == 3 ? 2 : 1;
       while (ny > 1 && static_cast<double>(zr * (ny + 1) * (tx + 1)) * dens > 2.0 * cap) --ny;
       VoxTile vt;
@@ -515,9 +515,19 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
     }
   }
   sp.vl_ubase[nvl] = static_cast<int32_t>(units);
-  sp.dchunks = static_cast<int32_t>((a.Q * a.P + kWalkChunk - 1) / kWalkChunk);
+  // dense kernel: up to 512 positions per CTA, records + grad_out rows in
+  // at most 64 KB of shared memory
+  {
+    const int64_t per = static_cast<int64_t>(sizeof(SRec)) + row_bytes + 4;
+    int64_t dchunk = std::min<int64_t>(512, (64 * 1024 - 4) / per);
+    dchunk = std::max<int64_t>(dchunk, 2 * kSegMax) & ~int64_t{1};
+    sp.dchunk = static_cast<int32_t>(dchunk);
+    sp.dchunks = static_cast<int32_t>((a.Q * a.P + dchunk - 1) / dchunk);
+    sp.dsmem = static_cast<int32_t>(dchunk * per + 4);
+  }
   sp.dlog2g = pw.log2g;
   sp.dnv = static_cast<int32_t>(a.C * dtype_bytes(a.vdt) / lw.vb);
+  sp.div_dnv = make_fdiv(static_cast<uint32_t>(std::max<int32_t>(sp.dnv, 1)));
   const int64_t per_b_smp = a.Q * a.H * a.L * a.P;
   const int64_t per_b_keys = a.H * seg;
   const int64_t per_b_vox = a.H * vox;
@@ -539,8 +549,8 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   sp.vcap = static_cast<int32_t>(cap);
   sp.vnv = p.nv;
   sp.div_nv = make_fdiv(static_cast<uint32_t>(std::max<int32_t>(p.nv, 1)));
-  sp.vsmem = static_cast<int32_t>(cap * (36 + row_bytes) + max_bounds * 4);
-  if (nvl > 0 && sp.vsmem > 48 * 1024) return false;  // within the default dynamic limit
+  sp.vsmem = static_cast<int32_t>(acc_bytes + cap * (36 + row_bytes) + max_bounds * 4);
+  if (nvl > 0 && sp.vsmem > 100 * 1024) return false;
   sp.div_lp = make_fdiv(static_cast<uint32_t>(a.L * a.P));
   sp.div_p = make_fdiv(static_cast<uint32_t>(a.P));
   sp.div_h = make_fdiv(static_cast<uint32_t>(a.H));
@@ -556,12 +566,12 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   pl.direct16 = 0;
   const int64_t nblk = (int64_t{sp.nkeys} + kScanTile - 1) / kScanTile;
   const int64_t n = sp.n;
-  const size_t sizes[4] = {
-      static_cast<size_t>(sp.nkeys + 2) * 4, static_cast<size_t>(nblk + 1) * 4,
-      static_cast<size_t>(n) * sizeof(SRec),
+  const size_t sizes[5] = {
+      static_cast<size_t>(sp.nkeys + 1) * 4, static_cast<size_t>(nblk + 1) * 4,
+      static_cast<size_t>(n) * 4, static_cast<size_t>(n) * sizeof(SRec),
       f32 ? 0 : static_cast<size_t>(nb * acc_keys * a.H * a.C) * sizeof(float)};
   size_t off = 0;
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < 5; ++i) {
     pl.soff[i] = off;
     off += align256(sizes[i]);
   }
@@ -603,22 +613,43 @@ void plan_bwd(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan& p
                     ? 0 : static_cast<size_t>(a.B * pl.acc_keys * a.H * a.C) * sizeof(float);
 }
 
+// The calling thread's side stream and fork/join events on the current
+// device, created on first use (outside stream capture on that first call).
+SideStream side_stream() {
+  constexpr int kMaxDev = 64;
+  thread_local SideStream cache[kMaxDev];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return SideStream{};
+  SideStream& s = cache[dev];
+  if (s.stream == nullptr) {
+    SideStream n;
+    if (cudaStreamCreateWithFlags(&n.stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&n.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&n.join, cudaEventDisableTiming) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return SideStream{};  // run everything on the caller's stream
+    }
+    s = n;
+  }
+  return s;
+}
+
 cudaError_t dispatch_sorted(int vdt, int sdt, const LaunchShape& ls, const LaunchShape& lsd,
                             const Problem& p, const SortPlan& sp, const void* go, float* gacc,
                             void* gv, void* gl, void* ga, cudaStream_t st) {
+  const SideStream side = side_stream();
   switch (vdt) {
     case MSDA_FLOAT32:
-      return launch_sorted_bwd<float, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st);
+      return launch_sorted_bwd<float, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st, side);
     case MSDA_FLOAT16:
       return sdt == MSDA_FLOAT32
-                 ? launch_sorted_bwd<__half, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st)
-                 : launch_sorted_bwd<__half, __half>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st);
+                 ? launch_sorted_bwd<__half, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st, side)
+                 : launch_sorted_bwd<__half, __half>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st, side);
     default:
       return sdt == MSDA_FLOAT32
-                 ? launch_sorted_bwd<__nv_bfloat16, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga,
-                                                           st)
+                 ? launch_sorted_bwd<__nv_bfloat16, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st, side)
                  : launch_sorted_bwd<__nv_bfloat16, __nv_bfloat16>(ls, lsd, p, sp, go, gacc, gv,
-                                                                   gl, ga, st);
+                                                                   gl, ga, st, side);
   }
 }
 
@@ -636,11 +667,11 @@ int run_bwd_sorted(const Args& a, Problem p, LaunchShape ls, const BwdPlan& pl, 
   const bool f32 = a.vdt == MSDA_FLOAT32;
   char* w = static_cast<char*>(ws);
   SortPlan sp = pl.sp;
-  sp.start = reinterpret_cast<int32_t*>(w + pl.soff[0]);  // [0] stays 0
-  sp.cnt = reinterpret_cast<int32_t*>(w + pl.soff[0]) + 1;
+  sp.cnt = reinterpret_cast<int32_t*>(w + pl.soff[0]);
   sp.bsum = reinterpret_cast<int32_t*>(w + pl.soff[1]);
-  sp.srec = reinterpret_cast<SRec*>(w + pl.soff[2]);
-  float* acc = f32 ? nullptr : reinterpret_cast<float*>(w + pl.soff[3]);
+  sp.pos = reinterpret_cast<int32_t*>(w + pl.soff[2]);
+  sp.srec = reinterpret_cast<SRec*>(w + pl.soff[3]);
+  float* acc = f32 ? nullptr : reinterpret_cast<float*>(w + pl.soff[4]);
   p.acc_compact = pl.compact ? 1 : 0;
   p.acc_keys = pl.acc_keys;
   for (int l = 0; l < kMaxLevels; ++l) p.acc_start[l] = pl.acc_start[l];

@@ -23,9 +23,9 @@
 // counts the samples per cell on the way.
 //
 // Pipeline for one chunk of batch entries (all on one stream):
-//   msda_dots_kernel       grad_attn, grad_loc; count[key] += 1 per sample
+//   msda_dots_kernel       grad_attn, grad_loc; rank = atomicAdd(count[key], 1)
 //   msda_scan_*            counts -> exclusive bucket starts
-//   msda_place_kernel      record (a, fractions, grad_out row, key) at atomicAdd(cursor[key], 1)
+//   msda_place_kernel      record (a, fractions, grad_out row, key) at start[key] + rank
 //   msda_dense_kernel      dense-level value gradient, per cell segment
 //   msda_voxel_kernel      sparse-level value gradient, gathered per value row
 //
@@ -86,8 +86,11 @@ struct SortPlan {
   int32_t voxel_mask;              // levels whose value gradient msda_voxel_kernel gathers
   int32_t ndl;                     // dense levels (msda_dense_kernel)
   int32_t dl_level[kMaxLevels];    // k-th dense level
+  int32_t dchunk;                  // sorted positions per msda_dense_kernel CTA
   int32_t dchunks;                 // msda_dense_kernel CTAs per (b, h, dense level)
   int32_t dlog2g, dnv;             // msda_dense_kernel lane group: 2^dlog2g lanes, dnv chunks per row
+  FastDiv div_dnv;                 // / dnv
+  int32_t dsmem;                   // msda_dense_kernel dynamic shared memory
   int32_t nvl;                     // voxel levels
   int32_t vl_level[kMaxLevels];    // k-th voxel level
   VoxTile vl_tile[kMaxLevels];     // msda_voxel_kernel tile of the k-th voxel level
@@ -98,10 +101,9 @@ struct SortPlan {
   FastDiv div_nv;                  // / vnv
   int32_t vsmem;                   // its dynamic shared memory
   FastDiv div_lp, div_p, div_h, div_l, div_q;
-  int32_t* cnt;                    // nkeys + 1: counts, then exclusive starts, then (after
-                                   // msda_place_kernel's cursor increments) the next bucket's start
-  const int32_t* start;            // cnt - 1, after msda_place_kernel: start[k] (start[0] = 0)
+  int32_t* cnt;                    // nkeys + 1: counts, then exclusive starts
   int32_t* bsum;                   // scan block sums
+  int32_t* pos;                    // n: each sample's rank inside its bucket
   SRec* srec;                      // n: the samples in sorted order
 };
 
@@ -154,6 +156,33 @@ template <> __device__ __forceinline__ Raw<2> ld_shared_chunk<2>(const void* p) 
   Raw<2> r; r.h = *reinterpret_cast<const unsigned short*>(p); return r;
 }
 
+// Asynchronous global -> shared copies (cp.async, sm_80+): a staging loop
+// issues all of its copies before any completes, so a phase costs one memory
+// round trip instead of one per loop iteration.
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+template <int N>
+__device__ __forceinline__ void cp_async(void* dst, const void* src) {
+  static_assert(N == 4 || N == 8 || N == 16, "cp.async copies 4, 8 or 16 bytes");
+  if constexpr (N == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+                 : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(smem_addr(dst)), "l"(src),
+                 "n"(N)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+// One VB-byte chunk, asynchronously where cp.async has the width.
+template <int VB>
+__device__ __forceinline__ void stage_chunk(void* dst, const void* src) {
+  if constexpr (VB >= 4) cp_async<VB>(dst, src);
+  else st_chunk<VB>(dst, ld_chunk<VB>(src));
+}
+
 // ------------------------------------------------------------------ dots
 // grad_attn and grad_loc in query order, as the gather/scatter backward
 // computes them (one lane group per (b, q, h) row, the row's grad_out chunk
@@ -163,7 +192,7 @@ template <> __device__ __forceinline__ Raw<2> ld_shared_chunk<2>(const void* p) 
 // transposed butterfly -- each step halves the values a lane keeps -- so a
 // sample costs a few shuffles instead of a full butterfly of four values.
 // The lane that ends with a sample's grad_attn also counts the sample into
-// its bucket (the counting sort's histogram).
+// its bucket (the counting sort's histogram) and keeps its rank there.
 constexpr int kDotBatch = 2;
 
 template <typename T, typename TS, int NDIM, int VB, int VPL>
@@ -292,7 +321,13 @@ __global__ void __launch_bounds__(kThreads, 4)
 #pragma unroll
         for (int ax = 0; ax < NDIM; ++ax) pass |= pt.pass[ax] ? (1 << ax) : 0;
         sinfo[i] = l | (pass << 8);
-        skey[i] = bucket_key<NDIM>(pt, g.sz, sp.cells[l], kbh + sp.lvl_base[l]);
+        // the sample's rank in its bucket, taken now by the lane that will
+        // store the sample's results, so the atomic's latency hides behind
+        // the corner loads
+        const int vi = 4 * i;
+        if (active && writer && vi >= vbase_i && vi < vbase_i + nkeep)
+          skey[i] = atomicAdd(sp.cnt + bucket_key<NDIM>(pt, g.sz, sp.cells[l],
+                                                        kbh + sp.lvl_base[l]), 1);
         if (++pp == P) { pp = 0; ++l; }
       }
     }
@@ -328,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 4)
             const int64_t si = row * LP + s;
             if (comp == 0) {
               grad_attn[si] = Elem<TS>::from_f(v[t]);
-              atomicAdd(sp.cnt + key, 1);  // the bucket histogram (result unused: a reduction)
+              sp.pos[si] = key;  // the rank taken above
             } else if (comp - 1 < NDIM) {
               const int ax = comp - 1, ls = info & 0xff;
               const float val = ((info >> (8 + ax)) & 1)
@@ -343,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 4)
 }
 
 // ------------------------------------------------------------------ place
-// One thread per sample: its record at the next free slot of its bucket.
+// One thread per sample: its record at start[key] + rank.
 template <typename TS, int NDIM>
 __global__ void __launch_bounds__(kThreads) msda_place_kernel(const Problem p, const SortPlan sp) {
   const uint32_t s = blockIdx.x * kThreads + threadIdx.x;
@@ -366,8 +401,7 @@ __global__ void __launch_bounds__(kThreads) msda_place_kernel(const Problem p, c
                              (static_cast<int32_t>(b) * static_cast<int32_t>(p.H) + h) *
                                  sp.seg_keys + sp.lvl_base[l]);
   rec.pad[0] = rec.pad[1] = 0u;
-  // the bucket's cursor: starts at the bucket's start, ends at the next one's
-  const int32_t at = atomicAdd(sp.cnt + rec.key, 1);
+  const int32_t at = __ldg(sp.cnt + rec.key) + sp.pos[s];
   uint4* dst = reinterpret_cast<uint4*>(sp.srec + at);
   const uint4* src = reinterpret_cast<const uint4*>(&rec);
   dst[0] = src[0];
@@ -479,13 +513,14 @@ static __global__ void __launch_bounds__(kScanThreads)
 
 
 // ------------------------------------------------------------------ dense levels
-// Value gradient of the dense levels.  One CTA per kWalkChunk sorted
-// positions of one (b, h, dense level) -- each owns exactly Q*P consecutive
-// positions -- cut into segments of one cell, at most kSegMax long.  One lane
-// group per segment: per sample its grad_out row (prefetched one sample
-// ahead) times a * w_corner is added to the cell's 2^d corner gradients in
-// fp32 registers, which are flushed with one vector reduction per corner.
-constexpr int kWalkChunk = 512;
+// Value gradient of the dense levels.  One CTA per sp.dchunk sorted positions
+// of one (b, h, dense level) -- each owns exactly Q*P consecutive positions.
+// The CTA stages the positions' records and their grad_out rows in shared
+// memory (cp.async: two memory round trips), cuts the positions into
+// segments of one cell, at most kSegMax long, and gives each segment to a
+// lane group: per sample a * w_corner * grad_out is added to the cell's 2^d
+// corner gradients in fp32 registers, flushed with one vector reduction per
+// corner.
 constexpr int kSegMax = 16;
 
 template <typename T, int NDIM, int VB, int VPL>
@@ -495,10 +530,13 @@ __global__ void __launch_bounds__(kThreads)
   using CK = Chunk<T, VB>;
   constexpr int EPV = CK::EPV;
   constexpr int NC = 1 << NDIM;
-  __shared__ int32_t mkey[kWalkChunk];
-  __shared__ uint32_t mrow[kWalkChunk];
-  __shared__ float4 mf[kWalkChunk];  // (a, fx, fy, fz)
-  __shared__ int32_t seg[kWalkChunk + 1];
+  extern __shared__ __align__(16) unsigned char dsm[];
+  const int chunkn = sp.dchunk;
+  SRec* rec_s = reinterpret_cast<SRec*>(dsm);                              // chunkn
+  const int64_t row_bytes = p.C * static_cast<int64_t>(sizeof(T));
+  const int rowb = static_cast<int>(row_bytes);
+  unsigned char* go_s = dsm + static_cast<size_t>(chunkn) * sizeof(SRec);  // chunkn * rowb
+  int32_t* seg = reinterpret_cast<int32_t*>(go_s + static_cast<size_t>(chunkn) * rowb);
   __shared__ int32_t warp_tot[kThreads / 32];
 
   const uint32_t u = blockIdx.x;
@@ -508,27 +546,34 @@ __global__ void __launch_bounds__(kThreads)
   const uint32_t bh = r1 / static_cast<uint32_t>(sp.ndl);
   const int l = sp.dl_level[kd];
   const int64_t qp = p.Q * p.P;
-  const int64_t base = (static_cast<int64_t>(bh) * p.L + l) * qp + int64_t{chunk} * kWalkChunk;
-  const int cnt = static_cast<int>(min(static_cast<int64_t>(kWalkChunk),
-                                       qp - int64_t{chunk} * kWalkChunk));
-  for (int t = threadIdx.x; t < cnt; t += kThreads) {
-    const SRec rec = sp.srec[base + t];
-    mkey[t] = rec.key;
-    mrow[t] = rec.row;
-    mf[t] = make_float4(rec.a, rec.f[0], rec.f[1], rec.f[2]);
-  }
+  const int64_t base = (static_cast<int64_t>(bh) * p.L + l) * qp + int64_t{chunk} * chunkn;
+  const int cnt = static_cast<int>(min(static_cast<int64_t>(chunkn), qp - int64_t{chunk} * chunkn));
+  // records, then the grad_out rows they name
+  for (int idx = threadIdx.x; idx < cnt * 2; idx += kThreads)
+    cp_async<16>(reinterpret_cast<char*>(rec_s) + idx * 16,
+                 reinterpret_cast<const char*>(sp.srec + base) + idx * 16);
+  cp_async_wait_all();
   __syncthreads();
+  const int nv = sp.dnv;
+  for (int idx = threadIdx.x; idx < cnt * nv; idx += kThreads) {
+    const int t = static_cast<int>(fdiv(static_cast<uint32_t>(idx), sp.div_dnv));
+    const int c = idx - t * nv;
+    stage_chunk<VB>(go_s + static_cast<size_t>(t) * rowb + c * VB,
+                    reinterpret_cast<const char*>(grad_out) +
+                        static_cast<int64_t>(rec_s[t].row) * row_bytes + c * VB);
+  }
   {
     const int t0 = 2 * threadIdx.x;
     bool h0 = false, h1 = false;
-    if (t0 < cnt) h0 = (t0 % kSegMax == 0) || mkey[t0] != mkey[t0 - 1];
-    if (t0 + 1 < cnt) h1 = ((t0 + 1) % kSegMax == 0) || mkey[t0 + 1] != mkey[t0];
+    if (t0 < cnt) h0 = (t0 % kSegMax == 0) || rec_s[t0].key != rec_s[t0 - 1].key;
+    if (t0 + 1 < cnt) h1 = ((t0 + 1) % kSegMax == 0) || rec_s[t0 + 1].key != rec_s[t0].key;
     int32_t total;
     const int32_t off = block_exclusive_scan(static_cast<int32_t>(h0) + static_cast<int32_t>(h1),
                                              warp_tot, total);
     if (h0) seg[off] = t0;
     if (h1) seg[off + (h0 ? 1 : 0)] = t0 + 1;
     if (threadIdx.x == 0) seg[total] = cnt;
+    cp_async_wait_all();
     __syncthreads();
     if (threadIdx.x == 0) warp_tot[0] = total;
     __syncthreads();
@@ -539,7 +584,6 @@ __global__ void __launch_bounds__(kThreads)
   const int ng = kThreads >> sp.dlog2g;
   const int grp = static_cast<int>(threadIdx.x) >> sp.dlog2g;
   const int j = static_cast<int>(threadIdx.x) & (G - 1);
-  const int64_t row_bytes = p.C * static_cast<int64_t>(sizeof(T));
   const int32_t cx = sp.cells[l][0], cy = sp.cells[l][1];
   const int32_t ncell = cx * cy * sp.cells[l][2];
   const int32_t kl = static_cast<int32_t>(bh) * sp.seg_keys + sp.lvl_base[l];
@@ -550,11 +594,11 @@ __global__ void __launch_bounds__(kThreads)
   float* gbase = gacc + ((static_cast<int64_t>(b) * p.acc_keys + kshift) * p.H + h) * p.C + j * EPV;
   bool has[VPL];
 #pragma unroll
-  for (int v = 0; v < VPL; ++v) has[v] = (j + v * G < sp.dnv);
+  for (int v = 0; v < VPL; ++v) has[v] = (j + v * G < nv);
 
   for (int sg = grp; sg < nseg; sg += ng) {
     const int ta = seg[sg], tb = seg[sg + 1];
-    const int32_t c = mkey[ta] - kl;
+    const int32_t c = rec_s[ta].key - kl;
     if (c >= ncell) continue;  // the dead bucket: no corner inside the level
     // the cell's lower corner and which of its corners lie inside the level
     const int32_t ix = c % cx - 1;
@@ -576,36 +620,25 @@ __global__ void __launch_bounds__(kThreads)
       for (int v = 0; v < VPL; ++v)
 #pragma unroll
         for (int e = 0; e < EPV; ++e) acc[cc][v][e] = 0.0f;
-    Raw<VB> gnext[VPL];
-    {
-      const char* gr = reinterpret_cast<const char*>(grad_out) +
-                       static_cast<int64_t>(mrow[ta]) * row_bytes + j * VB;
-#pragma unroll
-      for (int v = 0; v < VPL; ++v) gnext[v] = has[v] ? ld_chunk<VB>(gr + v * G * VB) : raw_zero<VB>();
-    }
     for (int t = ta; t < tb; ++t) {
       float go[VPL][EPV];
+      const unsigned char* gq = go_s + static_cast<size_t>(t) * rowb + j * VB;
 #pragma unroll
-      for (int v = 0; v < VPL; ++v) CK::unpack(gnext[v], go[v]);
-      if (t + 1 < tb) {
-        const char* gr = reinterpret_cast<const char*>(grad_out) +
-                         static_cast<int64_t>(mrow[t + 1]) * row_bytes + j * VB;
-#pragma unroll
-        for (int v = 0; v < VPL; ++v) gnext[v] = has[v] ? ld_chunk<VB>(gr + v * G * VB) : raw_zero<VB>();
-      }
-      const float4 af = mf[t];
-      const float fr[3] = {af.y, af.z, af.w};
+      for (int v = 0; v < VPL; ++v)
+        CK::unpack(has[v] ? ld_shared_chunk<VB>(gq + v * G * VB) : raw_zero<VB>(), go[v]);
+      const float a = rec_s[t].a;
       float wt[3][2];
 #pragma unroll
       for (int ax = 0; ax < 3; ++ax) {
-        if (ax < NDIM) { wt[ax][0] = __fsub_rn(1.0f, fr[ax]); wt[ax][1] = fr[ax]; }
+        const float f = rec_s[t].f[ax];
+        if (ax < NDIM) { wt[ax][0] = __fsub_rn(1.0f, f); wt[ax][1] = f; }
         else { wt[ax][0] = 1.0f; wt[ax][1] = 0.0f; }
       }
 #pragma unroll
       for (int cc = 0; cc < NC; ++cc) {
         float w = __fmul_rn(wt[0][cc & 1], wt[1][(cc >> 1) & 1]);
         if (NDIM == 3) w = __fmul_rn(w, wt[2][(cc >> 2) & 1]);
-        const float aw = af.x * w;
+        const float aw = a * w;
 #pragma unroll
         for (int v = 0; v < VPL; ++v)
 #pragma unroll
@@ -627,31 +660,31 @@ __global__ void __launch_bounds__(kThreads)
 
 // ------------------------------------------------------------------ voxel gather
 // Value gradient of the sparse levels.  One CTA per tile of NY voxel rows x TX
-// voxels at one (b, h, level, z), one thread per voxel (up to kThreads).
-// Voxel (x, y, z) is a corner of the cells with lower corner (x-1 or x, y-1
-// or y, z-1 or z), so the tile's samples lie in the cell rows (y', z') =
-// (y0-1 .. y0+NY-1, z-1 .. z), each row's cells x0-1 .. x0+TX-1 being one
-// contiguous range of the sorted records.  The CTA stages, in rounds of
-// sp.vcap samples: the range bounds, then per sample its four (bx, by)
-// corner weights a * w (the reference's product order) and its grad_out row
-// (rows padded by 16 bytes so the lanes' row reads spread over the banks).
-// Each thread then walks, for each of the 2^(d-1) cell rows its voxel
-// touches, the samples of cells x-1 (its upper-x corner) and x (lower-x
-// corner), summing a * w_corner * grad_out over all C channels in fp32
-// registers, kVoxChunks row chunks per pass; the row is stored once.
-constexpr int kVoxChunks = 2;
+// voxels at one (b, h, level, z); one warp per 32-voxel segment of a row,
+// lanes over channels.  Voxel (x, y, z) is a corner of the cells with lower
+// corner (x-1 or x, y-1 or y, z-1 or z), so the tile's samples lie in the
+// cell rows (y', z') = (y0-1 .. y0+NY-1, z-1 .. z), each row's cells
+// x0-1 .. x0+TX-1 being one contiguous range of the sorted records.  The CTA
+// stages, in rounds of sp.vcap samples (cp.async: three memory round trips):
+// the range bounds, the records -- turned into their four (bx, by) corner
+// weights a * w (the reference's product order) and their cell's x offset --
+// and their grad_out rows.  A warp then walks, for each of the 2^(d-1) cell
+// rows its voxel row touches, the samples of the 33 cells around its
+// segment, every lane adding its channel's a * w * grad_out to the sample's
+// two x-corners in a warp-private fp32 accumulator in shared memory (the
+// lanes of a row hit 32 distinct banks).  Each voxel row is stored once.
+// The work follows the number of samples, not the busiest voxel.
 
 template <typename T, int NDIM, int VB, int VPL>
-__global__ void __launch_bounds__(kThreads, 6)
+__global__ void __launch_bounds__(kThreads)
     msda_voxel_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
                       T* __restrict__ grad_value) {
-  using CK = Chunk<T, VB>;
-  constexpr int EPV = CK::EPV;
   extern __shared__ __align__(16) unsigned char vsm[];
+  const int lane = static_cast<int>(threadIdx.x & 31u);
+  const int warp = static_cast<int>(threadIdx.x >> 5);
   const int64_t row_bytes = p.C * static_cast<int64_t>(sizeof(T));
   const int rowb = static_cast<int>(row_bytes);
-  const int rowp = rowb + 16;  // staged row stride
-  const int nv = sp.vnv;       // VB-byte chunks per row
+  const int nv = sp.vnv;  // VB-byte chunks per row (staging)
 
   // unit -> (b, h, voxel level, z, y tile, x tile)
   const uint32_t u = blockIdx.x;
@@ -677,11 +710,12 @@ __global__ void __launch_bounds__(kThreads, 6)
   const int ncr = (NDIM == 3 ? 2 : 1) * nyr;       // cell rows
   const int cw = vt.tx + 2;                        // bounds per cell row
 
-  float4* ws = reinterpret_cast<float4*>(vsm);                          // vcap
-  unsigned char* go_s = vsm + static_cast<size_t>(sp.vcap) * 16;       // vcap * rowp
-  uint32_t* rows_s = reinterpret_cast<uint32_t*>(go_s + static_cast<size_t>(sp.vcap) * rowp);
-  int32_t* cnt_s = reinterpret_cast<int32_t*>(rows_s + sp.vcap);       // ncr * cw
-  int32_t* off_s = cnt_s + ncr * cw;                                    // ncr + 1
+  float* acc_s = reinterpret_cast<float*>(vsm);                       // warps x 32 voxels x 32 lanes
+  SRec* rec_s = reinterpret_cast<SRec*>(vsm + (kThreads / 32) * 32 * 32 * sizeof(float));  // vcap
+  unsigned char* go_s = reinterpret_cast<unsigned char*>(rec_s + sp.vcap);               // vcap * rowb
+  int32_t* lo_s = reinterpret_cast<int32_t*>(go_s + static_cast<size_t>(sp.vcap) * rowb);
+  int32_t* cnt_s = lo_s + sp.vcap;                                    // ncr * cw
+  int32_t* off_s = cnt_s + ncr * cw;                                  // ncr + 1
 
   // range bounds: cnt_s[cr][c] = start of cell x0-1+c of cell row cr
   for (int cr = 0; cr < ncr; ++cr) {
@@ -689,10 +723,14 @@ __global__ void __launch_bounds__(kThreads, 6)
     const int32_t yc = y0 - 1 + (cr - dz * nyr);  // the cell row's i0y
     const int32_t zc = NDIM == 3 ? vz - dz : -1;
     const int32_t krow = kb + ((zc + 1) * cyn + (yc + 1)) * cxn;
-    for (int c = threadIdx.x; c < cw; c += kThreads)  // rows outside the level are empty;
-      cnt_s[cr * cw + c] =                            // past the row end: its end bound
-          yc <= Hs - 1 ? __ldg(sp.start + krow + min(x0 + c, cxn)) : 0;
+    for (int c = threadIdx.x; c < cw; c += kThreads) {
+      if (yc <= Hs - 1)  // past the row end: its end bound
+        cp_async<4>(cnt_s + cr * cw + c, sp.cnt + krow + min(x0 + c, cxn));
+      else
+        cnt_s[cr * cw + c] = 0;  // rows outside the level are empty
+    }
   }
+  cp_async_wait_all();
   __syncthreads();
   if (threadIdx.x == 0) {
     int32_t o = 0;
@@ -705,28 +743,25 @@ __global__ void __launch_bounds__(kThreads, 6)
   __syncthreads();
   const int32_t total = off_s[ncr];
 
-  // this thread's voxel
-  const int ry = static_cast<int>(threadIdx.x) / vt.tx;
-  const int xl = static_cast<int>(threadIdx.x) - ry * vt.tx;
-  const bool active = ry < vt.ny && y0 + ry < Hs && x0 + xl < W;
-  char* dst = nullptr;
-  if (active) {
-    const int64_t key = static_cast<int64_t>(p.lv.start[l]) +
-                        (static_cast<int64_t>(vz) * Hs + y0 + ry) * W + x0 + xl;
-    dst = reinterpret_cast<char*>(grad_value) + ((static_cast<int64_t>(b) * p.K + key) * p.H + h) * row_bytes;
-  }
+  // this warp's 32-voxel segment
+  const int segs = (vt.tx + 31) / 32;
+  const int ry = warp / segs, sgi = warp - ry * segs;
+  const int32_t xw = x0 + sgi * 32;  // first voxel of the segment
+  const bool wactive = ry < vt.ny && y0 + ry < Hs && xw < W;
+  float* acc = acc_s + warp * 32 * 32;
 
-  for (int c0 = 0; c0 < nv; c0 += kVoxChunks) {
-    float acc[kVoxChunks][EPV];
-#pragma unroll
-    for (int m = 0; m < kVoxChunks; ++m)
-#pragma unroll
-      for (int e = 0; e < EPV; ++e) acc[m][e] = 0.0f;
+  const int ncb = (static_cast<int>(p.C) + 31) / 32;  // 32-channel blocks
+  for (int cb = 0; cb < ncb; ++cb) {
+    const int ch = cb * 32 + lane;
+    const bool lact = ch < p.C;
+#pragma unroll 4
+    for (int v = 0; v < 32; ++v) acc[v * 32 + lane] = 0.0f;
     for (int32_t q0 = 0; q0 < total; q0 += sp.vcap) {
       const int nr = min(sp.vcap, total - q0);
-      if (c0 == 0 || total > sp.vcap) {
-        // stage the round's weights and grad_out rows
-        if (q0 > 0 || c0 > 0) __syncthreads();
+      if (cb == 0 || total > sp.vcap) {
+        // stage the round: records, then per record its four (bx, by) corner
+        // weights in place of (a, f), its cell's x offset and its grad_out row
+        if (q0 > 0 || cb > 0) __syncthreads();
         for (int q = threadIdx.x; q < nr; q += kThreads) {
           const int32_t qq = q0 + q;
           int lo = 0, hi = ncr;  // cell row: off_s[lo] <= qq < off_s[lo + 1]
@@ -734,9 +769,21 @@ __global__ void __launch_bounds__(kThreads, 6)
             const int mid = (lo + hi) >> 1;
             if (off_s[mid] <= qq) lo = mid; else hi = mid;
           }
-          const int32_t pos = cnt_s[lo * cw] + (qq - off_s[lo]);
-          const SRec rec = sp.srec[pos];
+          lo_s[q] = lo;
+          const SRec* src = sp.srec + cnt_s[lo * cw] + (qq - off_s[lo]);
+          cp_async<16>(reinterpret_cast<char*>(rec_s + q), src);
+          cp_async<16>(reinterpret_cast<char*>(rec_s + q) + 16, reinterpret_cast<const char*>(src) + 16);
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        for (int q = threadIdx.x; q < nr; q += kThreads) {
+          const SRec rec = rec_s[q];
+          const int lo = lo_s[q];
           const int dz = (NDIM == 3 && lo >= nyr) ? 1 : 0;
+          const int32_t yc = y0 - 1 + (lo - dz * nyr);
+          const int32_t zc = NDIM == 3 ? vz - dz : -1;
+          // the cell's x offset in the tile: shifted cell index - x0 (cell i0x = x0 + c - 1)
+          lo_s[q] = rec.key - (kb + ((zc + 1) * cyn + (yc + 1)) * cxn) - x0;
           const float wx0 = __fsub_rn(1.0f, rec.f[0]), wx1 = rec.f[0];
           const float wy0 = __fsub_rn(1.0f, rec.f[1]), wy1 = rec.f[1];
           float w00 = __fmul_rn(wx0, wy0), w01 = __fmul_rn(wx0, wy1);
@@ -746,54 +793,51 @@ __global__ void __launch_bounds__(kThreads, 6)
             w00 = __fmul_rn(w00, wz); w01 = __fmul_rn(w01, wz);
             w10 = __fmul_rn(w10, wz); w11 = __fmul_rn(w11, wz);
           }
-          ws[q] = make_float4(rec.a * w00, rec.a * w01, rec.a * w10, rec.a * w11);
-          rows_s[q] = rec.row;
+          *reinterpret_cast<float4*>(rec_s + q) =
+              make_float4(rec.a * w00, rec.a * w01, rec.a * w10, rec.a * w11);
+          for (int c = 0; c < nv; ++c)
+            stage_chunk<VB>(go_s + static_cast<size_t>(q) * rowb + c * VB,
+                            reinterpret_cast<const char*>(grad_out) +
+                                static_cast<int64_t>(rec.row) * row_bytes + c * VB);
         }
-        __syncthreads();
-        for (int idx = threadIdx.x; idx < nr * nv; idx += kThreads) {
-          const int q = static_cast<int>(fdiv(static_cast<uint32_t>(idx), sp.div_nv));
-          const int c = idx - q * nv;
-          const char* src = reinterpret_cast<const char*>(grad_out) +
-                            static_cast<int64_t>(rows_s[q]) * row_bytes + c * VB;
-          st_chunk<VB>(go_s + static_cast<size_t>(q) * rowp + c * VB, ld_chunk<VB>(src));
-        }
+        cp_async_wait_all();
         __syncthreads();
       }
-      if (active) {
+      if (wactive) {
 #pragma unroll
         for (int dz = 0; dz < (NDIM == 3 ? 2 : 1); ++dz) {
 #pragma unroll
           for (int dy = 0; dy < 2; ++dy) {
             const int cr = dz * nyr + (ry - dy + 1);
-            const int32_t* crp = cnt_s + cr * cw + xl;
-            const int32_t slot0 = off_s[cr] - cnt_s[cr * cw] - q0;  // position -> round slot
-            const int32_t qa = max(crp[0] + slot0, 0);
-            const int32_t qs = crp[1] + slot0;  // cell x-1 | cell x
-            const int32_t qb = min(crp[2] + slot0, nr);
+            const int32_t* crp = cnt_s + cr * cw;
+            const int32_t slot0 = off_s[cr] - crp[0] - q0;  // position -> round slot
+            const int c0 = sgi * 32;                        // cells c0 .. c0+32 touch the segment
+            const int32_t qa = max(crp[c0] + slot0, 0);
+            const int32_t qb = min(crp[min(c0 + 33, cw - 1)] + slot0, nr);
             for (int32_t q = qa; q < qb; ++q) {
-              const float4 w4 = ws[q];
-              // cell x-1: this voxel is its upper-x corner (bx = 1); cell x: lower (bx = 0)
-              const float w = q < qs ? (dy ? w4.w : w4.z) : (dy ? w4.y : w4.x);
-              const unsigned char* gq = go_s + static_cast<size_t>(q) * rowp + c0 * VB;
-#pragma unroll
-              for (int m = 0; m < kVoxChunks; ++m) {
-                if (c0 + m < nv) {
-                  float go[EPV];
-                  CK::unpack(ld_shared_chunk<VB>(gq + m * VB), go);
-#pragma unroll
-                  for (int e = 0; e < EPV; ++e) acc[m][e] = fmaf(w, go[e], acc[m][e]);
-                }
-              }
+              const float4 w4 = *reinterpret_cast<const float4*>(rec_s + q);
+              const int vlo = lo_s[q] - 1 - sgi * 32;  // the cell's lower-x voxel in the segment
+              const float g = lact ? Elem<T>::to_f(reinterpret_cast<const T*>(
+                                         go_s + static_cast<size_t>(q) * rowb)[ch])
+                                   : 0.0f;
+              if (static_cast<unsigned>(vlo) < 32u)
+                acc[vlo * 32 + lane] = fmaf(dy ? w4.y : w4.x, g, acc[vlo * 32 + lane]);
+              if (static_cast<unsigned>(vlo + 1) < 32u)
+                acc[(vlo + 1) * 32 + lane] = fmaf(dy ? w4.w : w4.z, g, acc[(vlo + 1) * 32 + lane]);
             }
           }
         }
       }
     }
-    if (active) {
-#pragma unroll
-      for (int m = 0; m < kVoxChunks; ++m)
-        if (c0 + m < nv) st_chunk<VB>(dst + (c0 + m) * VB, CK::pack(acc[m]));
+    if (wactive && lact) {
+      const int32_t y = y0 + ry;
+      const int64_t key0 = static_cast<int64_t>(p.lv.start[l]) + (static_cast<int64_t>(vz) * Hs + y) * W;
+      T* gvb = grad_value + (static_cast<int64_t>(b) * p.K) * p.H * p.C + h * p.C + ch;
+      const int nvox = min(32, W - xw);
+      for (int v = 0; v < nvox; ++v)
+        gvb[(key0 + xw + v) * p.H * p.C] = Elem<T>::from_f(acc[v * 32 + lane]);
     }
+    if (cb + 1 < ncb) __syncwarp();
   }
 }
 

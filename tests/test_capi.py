@@ -77,23 +77,23 @@ def _align(x):
 def test_workspace_bytes_sorted_path(monkeypatch):
     # Host shapes and >= 2^20 samples: the cell-sorted backward.  Its
     # workspace: bucket counts (one per cell of the (W+1)(H+1)(D+1) grid plus
-    # a dead bucket, per level and (b, h), plus two), scan block sums, a
-    # 32-byte record per sample, and the fp32 accumulator of the levels with
-    # more than 6 samples per cell.
+    # a dead bucket, per level and (b, h), plus one), scan block sums, a rank
+    # and a 32-byte record per sample, and the fp32 accumulator of the levels
+    # with more than 2 samples per cell.
     monkeypatch.setenv("MSDA_BWD_PATH", "sorted")
     monkeypatch.delenv("MSDA_VOXEL_DENSITY", raising=False)
     monkeypatch.delenv("MSDA_SORTED_CHUNK_B", raising=False)
     B, H, C, Q, P = 2, 8, 32, 20000, 4
     shapes = [(32, 64, 64), (16, 32, 32), (8, 16, 16)]
     cells = [int(np.prod([s + 1 for s in sh])) for sh in shapes]
-    dense = [c for c, sh in zip(cells, shapes) if Q * P / c > 6.0]
-    assert len(dense) == 1  # only the coarsest level is aggregated per cell
-    acc_keys = int(np.prod(shapes[-1]))
+    dense = [sh for c, sh in zip(cells, shapes) if Q * P / c > 2.0]
+    assert len(dense) == 2  # the finest level is gathered per value row
+    acc_keys = sum(int(np.prod(sh)) for sh in dense)
     nkeys = B * H * sum(c + 1 for c in cells)
     n = B * Q * H * len(shapes) * P
     nblk = (nkeys + 4095) // 4096
-    expect = (_align((nkeys + 2) * 4) + _align((nblk + 1) * 4) + _align(n * 32)
-              + _align(B * acc_keys * H * C * 4))
+    expect = (_align((nkeys + 1) * 4) + _align((nblk + 1) * 4) + _align(n * 4)
+              + _align(n * 32) + _align(B * acc_keys * H * C * 4))
     assert _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P) == expect
     # fp32 values reduce the dense levels straight into grad_value: no accumulator
     assert _ws(_lib.FLOAT32, B, shapes, H, C, Q, P) == expect - _align(B * acc_keys * H * C * 4)
