@@ -5,17 +5,20 @@
 
 A step is one forward + backward pass (msda3d / msda2d through the public
 autograd API) over one batch of synthetic inputs already resident in HBM.
-Default workload: the BASELINE "3D xl" config -- bf16, B=8 per GPU, Q=100000,
+Default workload: the BASELINE "3D xl" config -- bf16, global B=8, Q=100000,
 H=8, C=32, L=4, P=4, levels (64,128,128),(32,64,64),(16,32,32),(8,16,16).
 
 Multi-GPU (torchrun, one process per GPU): batch sharding with no data-path
-collective -- every rank runs its own B=8 instance (weak scaling); the step
-time is the max over ranks (NCCL all_reduce of the CUDA-event time).
+collective.  By default the global batch is split over the ranks (strong
+scaling: B/N entries per rank, BASELINE config 4 as written);
+--scaling weak gives every rank its own full batch.  The step time is the
+max over ranks (NCCL all_reduce of the CUDA-event time).
 
---impl reference: the CPU oracle (oracle/, a C restatement of the reference's
-msda*_pytorch path; the reference itself is Python + Triton and cannot run on
-this box's host) times a bounded sample of the same workload on all host
-threads; rank 0 only.
+--impl reference: the reference's own CPU implementation of the path --
+msda{2,3}d_pytorch (grid_sample) from the unmodified package installed
+under baseline/_ref, fp32, all host threads -- times a bounded sample of the
+same workload; rank 0 only.  Without baseline/_ref the C restatement in
+oracle/ stands in (kind "port").
 """
 
 from __future__ import annotations
@@ -218,6 +221,13 @@ def run_ours(args, wl, rank, world, local_rank):
                                 device_id=dev)
 
     fn = M.msda3d if wl["ndim"] == 3 else M.msda2d
+    global_b = wl["B"]
+    if args.scaling == "strong" and world > 1:
+        if wl["B"] % world:
+            raise SystemExit(f"--scaling strong: batch {wl['B']} does not split over {world} GPUs")
+        wl = dict(wl, B=wl["B"] // world)
+    else:
+        global_b = wl["B"] * world
     value, shapes, loc, attn, go = make_inputs(wl, dev, seed=1234 + rank)
     v = value.requires_grad_(True)
     lo = loc.requires_grad_(True)
@@ -272,6 +282,7 @@ def run_ours(args, wl, rank, world, local_rank):
     fwd_times = time_events(k_fwd, kiters + 2, stream)[2:]
     kern = {"fwd": statistics.mean(fwd_times)}
     bwd_launches = 0
+    ws_bytes = 0
     if not fwd_only:
         # The backward entry exactly as the autograd path calls it: zero-fill
         # of the value-gradient targets, the scatter kernel and (16-bit
@@ -288,7 +299,7 @@ def run_ours(args, wl, rank, world, local_rank):
                                      gl.data_ptr(), ga.data_ptr(), ws.data_ptr(), ws_bytes, sp))
 
         kern["bwd"] = statistics.mean(time_events(k_bwd, kiters + 2, stream)[2:])
-        bwd_launches = 1 + (1 if wl["dtype"] != torch.float32 and ws_bytes > 0 else 0)
+        bwd_launches = _bwd_launches(wl, ws_bytes)
         del ws, gv, gl, ga
     if dist is not None:
         for k in list(kern):
@@ -324,13 +335,13 @@ def run_ours(args, wl, rank, world, local_rank):
         "warmup": args.warmup,
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.scaling == "strong" and world > 1 else "weak",
         "vs_baseline": None,
         "dtype": DTYPE_NAME[wl["dtype"]],
         "data": "synthetic (seeded N(0,1) value/grad_out, U[0,1) locations, softmax weights)",
         "config": {
             "workload": args.workload, "ndim": wl["ndim"], "batch_per_gpu": B,
-            "global_batch": B * world, "num_queries": Q, "num_heads": H, "channels": C,
+            "global_batch": global_b, "num_queries": Q, "num_heads": H, "channels": C,
             "num_levels": L, "num_points": P, "spatial_shapes": wl["shapes"],
             "parallelism": f"batch-sharded dp{world} (no collective)",
             "l2": f"inputs larger than L2 (value {value.numel() * value.element_size() / 1e9:.2f} GB"
@@ -341,8 +352,7 @@ def run_ours(args, wl, rank, world, local_rank):
         "pass_bytes": per_pass,
         "pass_roofline_frac": pass_gbs / peak,
         "roofline": {
-            "kernel": "msda_fwd_kernel" if dom == "fwd" else
-                      "backward entry (zero-fill + msda_bwd_kernel + cast)",
+            "kernel": "msda_fwd_kernel" if dom == "fwd" else _bwd_entry_name(wl, ws_bytes),
             "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak, "peak_source": peak_kind,
             "algorithmic_bytes": dom_bytes, "traffic": traffic,
@@ -352,8 +362,31 @@ def run_ours(args, wl, rank, world, local_rank):
         "e2e": e2e,
     }
     # the CPU baseline is a single-GPU figure: rank 0 at N=1 only
-    res["cpu_baseline"] = cpu_baseline(args, wl) if world == 1 else None
+    res["cpu_baseline"] = cpu_baseline(args, WORKLOADS[args.workload]) if world == 1 else None
     return res
+
+
+def _bwd_plan_is_sorted(wl, ws_bytes):
+    """Whether the library picked the cell-sorted backward for this workload
+    (its workspace holds a 32-byte record per sample)."""
+    return ws_bytes >= algorithmic_bytes(wl)["samples"] * 32
+
+
+def _bwd_launches(wl, ws_bytes):
+    """Our kernel launches in one backward entry: the cell-sorted plan runs the
+    dot-product kernel, three scan kernels, the placement kernel, the dense-
+    and voxel-level value-gradient kernels and the accumulator cast; the
+    gather/scatter plan the scatter kernel and (16-bit values) the cast."""
+    if _bwd_plan_is_sorted(wl, ws_bytes):
+        return 8
+    return 1 + (1 if wl["dtype"] != torch.float32 and ws_bytes > 0 else 0)
+
+
+def _bwd_entry_name(wl, ws_bytes):
+    if _bwd_plan_is_sorted(wl, ws_bytes):
+        return ("backward entry, cell-sorted (msda_dots_kernel + scan + msda_place_kernel + "
+                "msda_dense_kernel + msda_voxel_kernel + cast)")
+    return "backward entry, gather/scatter (zero-fill + msda_bwd_kernel + cast)"
 
 
 class _Null:
@@ -481,6 +514,10 @@ def run_reference_triton(args, wl, rank, world, local_rank):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     fn = ref.msda3d if wl["ndim"] == 3 else ref.msda2d
+    global_b = wl["B"] * world
+    if args.scaling == "strong" and world > 1 and wl["B"] % world == 0:
+        global_b = wl["B"]
+        wl = dict(wl, B=wl["B"] // world)
     value, shapes, loc, attn, go = make_inputs(wl, dev, seed=1234 + rank)
     v, lo, a = (t.requires_grad_(True) for t in (value, loc, attn))
     fwd_only = wl.get("fwd_only", False)
@@ -526,9 +563,10 @@ def run_reference_triton(args, wl, rank, world, local_rank):
         "metric": "MSDA fwd+bwd Gsamples/s" if not fwd_only else "MSDA fwd Gsamples/s",
         "value": samples / (ms * 1e-3) / 1e9, "unit": "Gsamples/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "fwd_ms": fwd_ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if global_b == B else "weak",
+        "vs_baseline": None,
         "dtype": DTYPE_NAME[wl["dtype"]], "data": "synthetic (same seeded inputs as our arm)",
-        "config": {"workload": args.workload, "batch_per_gpu": B, "global_batch": B * world,
+        "config": {"workload": args.workload, "batch_per_gpu": B, "global_batch": global_b,
                    "num_queries": Q, "source": "unmodified reference from baseline/_ref "
                    "(msda_triton " + getattr(ref, "__version__", "0.1.0") + ")"},
         "e2e": e2e,
@@ -674,19 +712,56 @@ def run_module(args, wl, rank, world, local_rank):
             "clocks": clk.summary()}
 
 
-# ---------------------------------------------------------------- CPU (oracle) arm
-def _cpu_sample(wl, target_s):
+# ---------------------------------------------------------------- CPU arms
+def _cpu_sample(wl, target_s, per_sample_us):
     """A bounded sample of the workload for the CPU: batch 1, and a query count
-    that keeps one fwd+bwd near `target_s` seconds (about 2 us of CPU per
-    sample per thread-group, measured on the oracle)."""
+    that keeps one fwd+bwd near `target_s` seconds at `per_sample_us`
+    microseconds per sample (measured for each implementation)."""
     B, K, H, C, Q, L, P = dims(wl)
-    return dict(wl, B=1, Q=max(64, min(Q, int(Q * target_s / 8.0))))
+    q = int(target_s * 1e6 / per_sample_us / (H * L * P))
+    return dict(wl, B=1, Q=max(64, min(Q, q)))
 
 
-def cpu_oracle_step(wl, inputs, nthreads):
+def cpu_inputs(wl, seed=7):
+    B, K, H, C, Q, L, P = dims(wl)
+    d = wl["ndim"]
+    g = torch.Generator().manual_seed(seed)
+    value = torch.randn(B, K, H, C, generator=g)
+    loc = torch.rand(B, Q, H, L, P, d, generator=g)
+    attn = torch.randn(B, Q, H, L * P, generator=g).softmax(-1).view(B, Q, H, L, P)
+    go = torch.randn(B, Q, H * C, generator=g)
+    shapes = torch.tensor(wl["shapes"], dtype=torch.int64)
+    return value, shapes, loc, attn, go
+
+
+def _reference_pytorch():
+    """msda{2,3}d_pytorch of the unmodified reference under baseline/_ref."""
+    ref = load_reference_triton()
+    if ref is None:
+        return None
+    from msda_triton.pytorch import msda2d_pytorch, msda3d_pytorch
+
+    return {2: msda2d_pytorch, 3: msda3d_pytorch}
+
+
+def cpu_step_reference(fns, wl, inputs):
+    """One fp32 fwd(+bwd) of the reference's grid_sample path on the host."""
+    value, shapes, loc, attn, go = inputs
+    fwd_only = wl.get("fwd_only", False)
+    v, lo, a = (t.detach().requires_grad_(not fwd_only) for t in (value, loc, attn))
+    t = time.perf_counter()
+    out = fns[wl["ndim"]](v, shapes, lo, a, True, 1e-4)
+    if not fwd_only:
+        torch.autograd.grad(out, (v, lo, a), go)
+    return time.perf_counter() - t
+
+
+def cpu_step_port(wl, inputs, nthreads):
+    """One fwd(+bwd) of the C restatement (oracle/), the stand-in when the
+    reference package is not installed."""
     from oracle import msda_bwd_oracle, msda_fwd_oracle
 
-    value, shapes, loc, attn, go = inputs
+    value, shapes, loc, attn, go = (t.numpy() for t in inputs)
     t = time.perf_counter()
     msda_fwd_oracle(value, shapes, loc, attn, True, 1e-4, nthreads)
     if not wl.get("fwd_only", False):
@@ -694,44 +769,48 @@ def cpu_oracle_step(wl, inputs, nthreads):
     return time.perf_counter() - t
 
 
-def cpu_inputs(wl, seed=7):
-    B, K, H, C, Q, L, P = dims(wl)
-    d = wl["ndim"]
-    g = torch.Generator().manual_seed(seed)
-    value = torch.randn(B, K, H, C, generator=g).numpy()
-    loc = torch.rand(B, Q, H, L, P, d, generator=g).numpy()
-    attn = torch.randn(B, Q, H, L * P, generator=g).softmax(-1).view(B, Q, H, L, P).numpy()
-    go = torch.randn(B, Q, H * C, generator=g).numpy()
-    shapes = torch.tensor(wl["shapes"], dtype=torch.int64).numpy()
-    return value, shapes, loc, attn, go
-
-
-def cpu_baseline(args, wl, steps=1, target_s=4.0):
+def cpu_measure(wl, steps, warmup, target_s):
+    """Time the CPU implementation on a bounded sample: the reference's own
+    msda*_pytorch when installed, else the C port.  Returns (seconds per
+    pass list, sample workload, kind, threads)."""
     nthreads = os.cpu_count() or 1
-    swl = _cpu_sample(wl, target_s)
+    fns = _reference_pytorch()
+    if fns is not None:
+        torch.set_num_threads(nthreads)
+        swl = _cpu_sample(wl, target_s, 0.8)
+        inputs = cpu_inputs(swl)
+        for _ in range(warmup):
+            cpu_step_reference(fns, swl, inputs)
+        ts = [cpu_step_reference(fns, swl, inputs) for _ in range(steps)]
+        return ts, swl, "reference", torch.get_num_threads()
+    swl = _cpu_sample(wl, target_s, 0.16)
     inputs = cpu_inputs(swl)
-    cpu_oracle_step(swl, inputs, nthreads)  # warm-up (page-in, thread pool)
-    ts = [cpu_oracle_step(swl, inputs, nthreads) for _ in range(steps)]
+    for _ in range(warmup):
+        cpu_step_port(swl, inputs, nthreads)
+    ts = [cpu_step_port(swl, inputs, nthreads) for _ in range(steps)]
+    return ts, swl, "port", nthreads
+
+
+def _cpu_desc(kind, wl, swl, samples, steps, t):
+    what = ("the reference's msda_triton.pytorch grid_sample path (baseline/_ref), fp32"
+            if kind == "reference" else "fp32 C port of the reference path (oracle/, OpenMP)")
+    return (f"{what}, fwd{'' if wl.get('fwd_only') else '+bwd'} on batch 1, Q={swl['Q']} "
+            f"({samples} samples), median of {steps} after 1 warm-up; {t:.2f} s per pass")
+
+
+def cpu_baseline(args, wl, steps=3, target_s=3.0):
+    ts, swl, kind, cores = cpu_measure(wl, steps, 1, target_s)
     t = statistics.median(ts)
     samples = algorithmic_bytes(swl)["samples"]
-    return {
-        "value": samples / t / 1e9, "unit": "Gsamples/s", "cores": nthreads, "kind": "port",
-        "sample": f"fp32 oracle (C, OpenMP) fwd{'' if wl.get('fwd_only') else '+bwd'} on batch 1, "
-                  f"Q={swl['Q']} of the {args.workload} workload ({samples} samples), "
-                  f"median of {steps} after 1 warm-up; {t:.2f} s per pass",
-    }
+    return {"value": samples / t / 1e9, "unit": "Gsamples/s", "cores": cores, "kind": kind,
+            "sample": _cpu_desc(kind, wl, swl, samples, steps, t)}
 
 
 def run_reference(args, wl, rank):
     if rank != 0:
         return None
-    nthreads = os.cpu_count() or 1
-    swl = _cpu_sample(wl, 3.0)
-    inputs = cpu_inputs(swl)
-    for _ in range(args.warmup):
-        cpu_oracle_step(swl, inputs, nthreads)
-    ts = [cpu_oracle_step(swl, inputs, nthreads) for _ in range(args.steps)]
-    t = sum(ts) / len(ts)
+    ts, swl, kind, cores = cpu_measure(wl, args.steps, args.warmup, 2.0)
+    t = statistics.median(ts)
     samples = algorithmic_bytes(swl)["samples"]
     val = samples / t / 1e9
     fwd_only = wl.get("fwd_only", False)
@@ -740,12 +819,12 @@ def run_reference(args, wl, rank):
         "metric": "MSDA fwd+bwd Gsamples/s" if not fwd_only else "MSDA fwd Gsamples/s",
         "value": val, "unit": "Gsamples/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-        "data": "synthetic (seeded)",
+        "scaling": "strong" if args.gpus > 1 and args.scaling == "strong" else "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
         "config": {"workload": args.workload, "ndim": wl["ndim"], "batch_per_gpu": 1,
                    "num_queries": swl["Q"], "note": "bounded CPU sample of the workload"},
-        "cpu_baseline": {"value": val, "unit": "Gsamples/s", "cores": nthreads, "kind": "port",
-                         "sample": f"oracle fwd{'' if fwd_only else '+bwd'}, batch 1, Q={swl['Q']}"},
+        "cpu_baseline": {"value": val, "unit": "Gsamples/s", "cores": cores, "kind": kind,
+                         "sample": _cpu_desc(kind, wl, swl, samples, args.steps, t)},
         "e2e": {"value": val, "unit": "Gsamples/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -765,6 +844,9 @@ def main():
     ap.add_argument("--reduce-dtype", default="float32", choices=["float32", "value"],
                     help="--shard query: sum the partial value gradients in fp32 (reduce-scatter "
                          "+ all-gather, one rounding) or in the value dtype (one all_reduce)")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="--gpus N: split the workload's batch over the GPUs (strong) or give "
+                         "every GPU the whole batch (weak)")
     ap.add_argument("--batch", type=int, default=0,
                     help="per-GPU batch override (a smaller case of the workload, for profiling)")
     args = ap.parse_args()

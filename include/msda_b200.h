@@ -180,10 +180,13 @@ MSDA_API size_t msda_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batc
  * from a 32 MiB array inside the library's device image, reserved on every
  * GPU that loads the library until the process exits.  Problems needing more
  * than 32 MiB of scratch (msda_bwd_workspace_bytes) are rejected with
- * MSDA_ERROR_WORKSPACE.  The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress); make that first call outside any
- * stream capture.  All calls share the array: calls whose GPU work overlaps
- * on one device race; serialise them.  Each call clears what it uses. */
+ * MSDA_ERROR_WORKSPACE.  The first call on a device, and the first call
+ * after the current driver context changed (another context made current,
+ * or a cudaDeviceReset that destroyed the old one), looks up the array's
+ * device address (cudaGetSymbolAddress) and caches it for that context;
+ * make such a call outside any stream capture.  All calls share the array:
+ * calls whose GPU work overlaps on one device race; serialise them.  Each
+ * call clears what it uses. */
 MSDA_API int msda_bwd_static_scratch(int ndim, const void* value, int value_dtype, int64_t batch,
                int64_t num_keys, int64_t num_heads, int64_t channels,
                const int32_t* spatial_shapes, int spatial_shapes_on_device, int64_t num_levels,

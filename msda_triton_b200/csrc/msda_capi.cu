@@ -429,6 +429,10 @@ size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
 constexpr int64_t kSortedMinSamples = int64_t{1} << 20;
 constexpr double kVoxelMaxDensity = 2.0;
 constexpr bool kSortedByDefault = true;
+// Sorted positions per dense-kernel CTA and at most this many samples staged
+// per voxel-kernel round.
+constexpr int64_t kDenseChunk = 512;
+constexpr int64_t kVoxelCap = 512;
 
 FastDiv make_fdiv(uint32_t d) {
   if (d == 0) d = 1;
@@ -466,7 +470,7 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   const int64_t acc_bytes = int64_t{kThreads / 32} * 32 * 32 * 4;
   // per staged sample: its record (32 B), cell row / x offset (4 B), grad_out row
   int64_t cap = (72 * 1024 - acc_bytes - bounds_max) / (36 + row_bytes);
-  cap = std::min<int64_t>(cap, 512) & ~int64_t{1};
+  cap = std::min<int64_t>(cap, kVoxelCap) & ~int64_t{1};
   if (cap < 16) max_dens = -1.0;
   SortPlan sp{};
   int64_t seg = 0, vox = 0, acc_keys = 0, units = 0, max_bounds = 0;
@@ -519,7 +523,7 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   // at most 64 KB of shared memory
   {
     const int64_t per = static_cast<int64_t>(sizeof(SRec)) + row_bytes + 4;
-    int64_t dchunk = std::min<int64_t>(512, (64 * 1024 - 4) / per);
+    int64_t dchunk = std::min<int64_t>(kDenseChunk, (64 * 1024 - 4) / per);
     dchunk = std::max<int64_t>(dchunk, 2 * kSegMax) & ~int64_t{1};
     sp.dchunk = static_cast<int32_t>(dchunk);
     sp.dchunks = static_cast<int32_t>((a.Q * a.P + dchunk - 1) / dchunk);
@@ -613,43 +617,21 @@ void plan_bwd(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan& p
                     ? 0 : static_cast<size_t>(a.B * pl.acc_keys * a.H * a.C) * sizeof(float);
 }
 
-// The calling thread's side stream and fork/join events on the current
-// device, created on first use (outside stream capture on that first call).
-SideStream side_stream() {
-  constexpr int kMaxDev = 64;
-  thread_local SideStream cache[kMaxDev];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return SideStream{};
-  SideStream& s = cache[dev];
-  if (s.stream == nullptr) {
-    SideStream n;
-    if (cudaStreamCreateWithFlags(&n.stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaEventCreateWithFlags(&n.fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&n.join, cudaEventDisableTiming) != cudaSuccess) {
-      (void)cudaGetLastError();
-      return SideStream{};  // run everything on the caller's stream
-    }
-    s = n;
-  }
-  return s;
-}
-
 cudaError_t dispatch_sorted(int vdt, int sdt, const LaunchShape& ls, const LaunchShape& lsd,
                             const Problem& p, const SortPlan& sp, const void* go, float* gacc,
                             void* gv, void* gl, void* ga, cudaStream_t st) {
-  const SideStream side = side_stream();
   switch (vdt) {
     case MSDA_FLOAT32:
-      return launch_sorted_bwd<float, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st, side);
+      return launch_sorted_bwd<float, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st);
     case MSDA_FLOAT16:
       return sdt == MSDA_FLOAT32
-                 ? launch_sorted_bwd<__half, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st, side)
-                 : launch_sorted_bwd<__half, __half>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st, side);
+                 ? launch_sorted_bwd<__half, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st)
+                 : launch_sorted_bwd<__half, __half>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st);
     default:
       return sdt == MSDA_FLOAT32
-                 ? launch_sorted_bwd<__nv_bfloat16, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st, side)
+                 ? launch_sorted_bwd<__nv_bfloat16, float>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st)
                  : launch_sorted_bwd<__nv_bfloat16, __nv_bfloat16>(ls, lsd, p, sp, go, gacc, gv,
-                                                                   gl, ga, st, side);
+                                                                   gl, ga, st);
   }
 }
 

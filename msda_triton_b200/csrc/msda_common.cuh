@@ -212,8 +212,9 @@ struct LevelSmem {
 
 // Fill the CTA's level table.  Host-resolved tables are copied.  Device
 // shapes are read here (no host sync, like the reference's GPU-shape path,
-// triton/msda_2d.py:76-82); a level that would reach past K is disabled so a
-// malformed device table can never cause an out-of-range read.
+// triton/msda_2d.py:76-82); a level that would reach past K -- and every
+// level after it -- is disabled, with the size product checked before it can
+// overflow, so a malformed device table can never cause an out-of-range read.
 __device__ __forceinline__ void load_levels(const Problem& p, LevelSmem& s, int ndim) {
   if (threadIdx.x == 0) {
     if (p.shapes_dev == nullptr) {
@@ -228,13 +229,18 @@ __device__ __forceinline__ void load_levels(const Problem& p, LevelSmem& s, int 
       for (int l = 0; l < p.L; ++l) {
         int32_t sz[3] = {1, 1, 1};
         int64_t n = 1;
+        bool fits = true;
         for (int a = 0; a < ndim; ++a) {
           int32_t v = p.shapes_dev[l * ndim + (ndim - 1 - a)];
           v = v < 0 ? 0 : v;
           sz[a] = v;
-          n *= v;
+          // stop before the product can overflow: a level larger than K
+          // cannot fit anyway
+          if (v > p.K || (v > 0 && n > p.K / v)) fits = false;
+          else n *= v;
         }
-        const bool fits = start + n <= p.K;
+        fits = fits && start + n <= p.K;
+        if (!fits) n = p.K + 1;  // the levels after a misfit start past K as well
         s.size[l][0] = fits ? sz[0] : 0;
         s.size[l][1] = fits ? sz[1] : 0;
         s.size[l][2] = fits ? sz[2] : 0;

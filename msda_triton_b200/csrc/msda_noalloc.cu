@@ -10,8 +10,9 @@
 // part of this library's device image instead: it allocates nothing.
 //
 // The array (kStaticScratchBytes) is reserved on every GPU that loads the
-// library, for as long as the process lives.  Every call shares it, so calls
-// whose GPU work overlaps -- on different streams, or from different host
+// library, for as long as the process lives (a device reset gives a new
+// context and a new array, which the next call looks up).  Every call shares
+// it, so calls whose GPU work overlaps -- on different streams, or from different host
 // threads, on the same device -- race on it; serialise them (one stream) or
 // use msda{2,3}d_bwd with separate workspaces.  The region a call uses is
 // cleared by that call (the previous call's contents remain until then).
@@ -45,29 +46,58 @@ constexpr int kMaxDevices = 64;
 __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 std::mutex g_setup_mutex;
-void* g_scratch_addr[kMaxDevices] = {};
+// Per device: the driver context the address was looked up in, and the
+// address.  A device reset or another context current on the device gives a
+// new context, whose array has its own address: it is looked up again.
+struct ScratchAddr {
+  void* ctx = nullptr;
+  void* addr = nullptr;
+};
+ScratchAddr g_scratch_addr[kMaxDevices];
 
 int noalloc_fail(int code, const char* msg) { return msda::set_last_error(code, msg); }
 
+// The driver context current on the calling thread (cuCtxGetCurrent through
+// the runtime's entry-point lookup, so the library links no driver library).
+void* current_context() {
+  using GetCurrent = int (*)(void**);
+  static GetCurrent fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<GetCurrent>(f);
+  }();
+  void* ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
+
 // Device address of the scratch array on the current device.  In host code
 // the array's name is only a host-side stand-in; the real address must come
-// from cudaGetSymbolAddress with the device current.  Done once per device.
+// from cudaGetSymbolAddress with the device current.  Done once per device
+// and context.
 int scratch_address(void** out) {
   int dev = -1;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return noalloc_fail(MSDA_ERROR_CUDA, cudaGetErrorString(err));
   if (dev < 0 || dev >= kMaxDevices)
     return noalloc_fail(MSDA_ERROR_INVALID_ARGUMENT, "device ordinal out of range");
+  void* ctx = current_context();
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (g_scratch_addr[dev] == nullptr) {
+  ScratchAddr& c = g_scratch_addr[dev];
+  if (c.addr == nullptr || ctx == nullptr || c.ctx != ctx) {
     void* p = nullptr;
+    // with no context current yet, this makes the device's primary one current
     err = cudaGetSymbolAddress(&p, g_static_scratch);
     if (err != cudaSuccess || p == nullptr)
       return noalloc_fail(MSDA_ERROR_CUDA, err != cudaSuccess ? cudaGetErrorString(err)
                                                               : "null scratch address");
-    g_scratch_addr[dev] = p;
+    c.ctx = current_context();
+    c.addr = p;
   }
-  *out = g_scratch_addr[dev];
+  *out = c.addr;
   return MSDA_SUCCESS;
 }
 

@@ -71,17 +71,10 @@ static cudaError_t voxel_one(const Problem& p, const SortPlan& sp, const void* g
     default: return cudaErrorInvalidValue;                                          \
   }
 
-// A second stream of the calling thread, and the two events that fork work
-// onto it from the caller's stream and join it back (graph-capture safe).
-struct SideStream {
-  cudaStream_t stream = nullptr;
-  cudaEvent_t fork = nullptr, join = nullptr;
-};
-
 template <typename T, typename TS, int NDIM>
 static cudaError_t sorted_chunk(const LaunchShape& ls, const LaunchShape& lsd, const Problem& p,
                                 const SortPlan& sp, const void* go, float* gacc, void* gv,
-                                void* gl, void* ga, cudaStream_t st, const SideStream& side) {
+                                void* gl, void* ga, cudaStream_t st) {
   cudaError_t err =
       cudaMemsetAsync(sp.cnt, 0, (static_cast<size_t>(sp.nkeys) + 1) * sizeof(int32_t), st);
   if (err != cudaSuccess) return err;
@@ -100,24 +93,15 @@ static cudaError_t sorted_chunk(const LaunchShape& ls, const LaunchShape& lsd, c
   const unsigned sblocks = static_cast<unsigned>((int64_t{sp.n} + kThreads - 1) / kThreads);
   msda_place_kernel<TS, NDIM><<<sblocks, kThreads, 0, st>>>(p, sp);
   if ((err = cudaGetLastError()) != cudaSuccess) return err;
-  // The dense and the voxel kernels touch disjoint levels: with both present
-  // the dense one runs on the side stream, so the latency-bound voxel CTAs and
-  // the issue-bound dense CTAs share the SMs.
-  cudaStream_t sd = st;
-  if (sp.ndl > 0 && sp.nvl > 0 && side.stream != nullptr) {
-    if ((err = cudaEventRecord(side.fork, st)) != cudaSuccess) return err;
-    if ((err = cudaStreamWaitEvent(side.stream, side.fork, 0)) != cudaSuccess) return err;
-    sd = side.stream;
-  }
   if (sp.ndl > 0) {
     switch (lsd.vb * 16 + lsd.vpl) {
-      case 16 * 16 + 1: err = dense_one<T, NDIM, 16, 1>(p, sp, go, gacc, sd); break;
-      case 16 * 16 + 2: err = dense_one<T, NDIM, 16, 2>(p, sp, go, gacc, sd); break;
-      case 8 * 16 + 1: err = dense_one<T, NDIM, 8, 1>(p, sp, go, gacc, sd); break;
-      case 8 * 16 + 2: err = dense_one<T, NDIM, 8, 2>(p, sp, go, gacc, sd); break;
-      case 4 * 16 + 1: err = dense_one<T, NDIM, 4, 1>(p, sp, go, gacc, sd); break;
+      case 16 * 16 + 1: err = dense_one<T, NDIM, 16, 1>(p, sp, go, gacc, st); break;
+      case 16 * 16 + 2: err = dense_one<T, NDIM, 16, 2>(p, sp, go, gacc, st); break;
+      case 8 * 16 + 1: err = dense_one<T, NDIM, 8, 1>(p, sp, go, gacc, st); break;
+      case 8 * 16 + 2: err = dense_one<T, NDIM, 8, 2>(p, sp, go, gacc, st); break;
+      case 4 * 16 + 1: err = dense_one<T, NDIM, 4, 1>(p, sp, go, gacc, st); break;
       case 2 * 16 + 1:
-        if constexpr (sizeof(T) == 2) { err = dense_one<T, NDIM, 2, 1>(p, sp, go, gacc, sd); break; }
+        if constexpr (sizeof(T) == 2) { err = dense_one<T, NDIM, 2, 1>(p, sp, go, gacc, st); break; }
         return cudaErrorInvalidValue;
       default: return cudaErrorInvalidValue;
     }
@@ -129,10 +113,6 @@ static cudaError_t sorted_chunk(const LaunchShape& ls, const LaunchShape& lsd, c
 #undef MSDA_VOXEL_CALL
     if (err != cudaSuccess) return err;
   }
-  if (sd != st) {
-    if ((err = cudaEventRecord(side.join, sd)) != cudaSuccess) return err;
-    if ((err = cudaStreamWaitEvent(st, side.join, 0)) != cudaSuccess) return err;
-  }
   return cudaSuccess;
 }
 
@@ -142,20 +122,19 @@ static cudaError_t sorted_chunk(const LaunchShape& ls, const LaunchShape& lsd, c
 template <typename T, typename TS>
 cudaError_t launch_sorted_bwd(const LaunchShape& ls, const LaunchShape& lsd, const Problem& p,
                               const SortPlan& sp, const void* go, float* gacc, void* gv,
-                              void* gl, void* ga, cudaStream_t st, const SideStream& side) {
-  return ls.ndim == 2 ? sorted_chunk<T, TS, 2>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st, side)
-                      : sorted_chunk<T, TS, 3>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st, side);
+                              void* gl, void* ga, cudaStream_t st) {
+  return ls.ndim == 2 ? sorted_chunk<T, TS, 2>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st)
+                      : sorted_chunk<T, TS, 3>(ls, lsd, p, sp, go, gacc, gv, gl, ga, st);
 }
 
 #define MSDA_DECLARE_SORTED(T, TS)                                                            \
   extern template cudaError_t launch_sorted_bwd<T, TS>(const LaunchShape&, const LaunchShape&, \
                                                        const Problem&, const SortPlan&,        \
                                                        const void*, float*, void*, void*,      \
-                                                       void*, cudaStream_t, const SideStream&);
+                                                       void*, cudaStream_t);
 #define MSDA_INSTANTIATE_SORTED(T, TS)                                                        \
   template cudaError_t launch_sorted_bwd<T, TS>(const LaunchShape&, const LaunchShape&,        \
                                                 const Problem&, const SortPlan&, const void*,  \
-                                                float*, void*, void*, void*, cudaStream_t,     \
-                                                const SideStream&);
+                                                float*, void*, void*, void*, cudaStream_t);
 
 }  // namespace msda

@@ -292,6 +292,19 @@ def test_malformed_device_shapes_do_not_read_out_of_range():
     assert_close(out.cpu(), ref, TOL_FWD_F32, "disabled level")
 
 
+def test_malformed_device_shapes_huge_3d_level():
+    # A 3D level of (2^31-1)^3 cells: its size product would overflow int64;
+    # it is disabled and contributes nothing, the level before it is intact.
+    value, shp, loc, attn, _ = make_inputs(1, 8, 2, 8, 2, [(2, 3, 4), (1, 2, 2)], seed=3,
+                                           device="cuda")
+    big = 2**31 - 1
+    bad = torch.tensor([[2, 3, 4], [big, big, big]], dtype=torch.int32, device="cuda")
+    out = M.msda3d_fwd(value, bad, loc, attn)
+    keep = torch.tensor([1.0, 0.0]).view(1, 1, 1, 2, 1)
+    ref = msda_fwd_oracle(value.cpu(), shp, loc.cpu(), attn.cpu() * keep)
+    assert_close(out.cpu(), ref, TOL_FWD_F32, "disabled huge level")
+
+
 def test_multi_stream_and_device_guard():
     inp = make_inputs(2, 64, 8, 32, 4, SHAPES[2], seed=1300, device="cuda")
     value, shp, loc, attn, _ = inp

@@ -23,11 +23,27 @@ def _call_static(ndim, value, shapes, loc, attn, go):
     gv = torch.empty_like(value)
     gl = torch.empty_like(loc)
     ga = torch.empty_like(attn)
-    rc = lib.msda_bwd_static_scratch(
-        ndim, *_core._common_args(value, shapes, False, loc, attn), 1, 1e-4,
-        go.data_ptr(), gv.data_ptr(), gl.data_ptr(), ga.data_ptr(),
-        torch.cuda.current_stream().cuda_stream)
+    with torch.cuda.device(value.device):
+        rc = lib.msda_bwd_static_scratch(
+            ndim, *_core._common_args(value, shapes, shapes.is_cuda, loc, attn), 1, 1e-4,
+            go.data_ptr(), gv.data_ptr(), gl.data_ptr(), ga.data_ptr(),
+            torch.cuda.current_stream(value.device).cuda_stream)
     return rc, gv, gl, ga
+
+
+def _check_against_workspace_backward(ndim, dtype, dev, shapes, seed):
+    value, _, loc, attn, go = make_inputs(2, 300, 4, 32, 4, SHAPES[ndim], seed=seed,
+                                          dtype=dtype, device=dev)
+    host_shapes = torch.tensor(SHAPES[ndim], dtype=torch.int32)
+    with torch.cuda.device(dev):
+        ref = _core.backward(ndim, value, host_shapes, False, loc, attn, True, 1e-4, go)
+    rc, *got = _call_static(ndim, value, shapes, loc, attn, go)
+    assert rc == _lib.SUCCESS, _lib.last_error()
+    torch.cuda.synchronize(dev)
+    tol = TOL_GRAD_F32 if dtype == torch.float32 else TOL_HALF
+    for name, g, r in zip(("grad_value", "grad_loc", "grad_attn"), got, ref):
+        assert_close(g.float().cpu(), r.float().cpu(), tol,
+                     f"{ndim}D {dtype} {dev} shapes on {shapes.device} seed={seed} {name}")
 
 
 @pytest.mark.parametrize("ndim", [2, 3])
@@ -36,15 +52,30 @@ def test_static_scratch_matches_workspace_backward(ndim, dtype):
     dev = torch.device("cuda", 0)
     shapes = torch.tensor(SHAPES[ndim], dtype=torch.int32)
     for seed in (1, 2):  # two calls in a row; the second must not see the first's sums
-        value, _, loc, attn, go = make_inputs(2, 300, 4, 32, 4, SHAPES[ndim], seed=seed,
-                                              dtype=dtype, device=dev)
-        ref = _core.backward(ndim, value, shapes, False, loc, attn, True, 1e-4, go)
-        rc, *got = _call_static(ndim, value, shapes, loc, attn, go)
-        assert rc == _lib.SUCCESS, _lib.last_error()
-        torch.cuda.synchronize()
-        tol = TOL_GRAD_F32 if dtype == torch.float32 else TOL_HALF
-        for name, g, r in zip(("grad_value", "grad_loc", "grad_attn"), got, ref):
-            assert_close(g.float().cpu(), r.float().cpu(), tol, f"{ndim}D {dtype} seed={seed} {name}")
+        _check_against_workspace_backward(ndim, dtype, dev, shapes, seed)
+
+
+@pytest.mark.parametrize("ndim", [2, 3])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_static_scratch_device_resident_shapes(ndim, dtype):
+    """spatial_shapes on the device: the scratch size is then planned from the
+    problem's bounds (no host copy of the table), the kernels read the table
+    from device memory."""
+    dev = torch.device("cuda", 0)
+    shapes = torch.tensor(SHAPES[ndim], dtype=torch.int32, device=dev)
+    for seed in (3, 4):
+        _check_against_workspace_backward(ndim, dtype, dev, shapes, seed)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two visible GPUs")
+@pytest.mark.parametrize("ndim", [2, 3])
+def test_static_scratch_second_device(ndim):
+    """A call on device 1 uses device 1's copy of the array (its own slot of the
+    address cache), then device 0 again still gets its own."""
+    shapes = torch.tensor(SHAPES[ndim], dtype=torch.int32)
+    for i, seed in ((1, 5), (0, 6), (1, 7)):
+        _check_against_workspace_backward(ndim, torch.bfloat16, torch.device("cuda", i),
+                                          shapes, seed)
 
 
 def test_static_scratch_rejects_oversized_problem():
