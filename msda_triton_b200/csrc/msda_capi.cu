@@ -433,6 +433,10 @@ constexpr bool kSortedByDefault = true;
 // per voxel-kernel round.
 constexpr int64_t kDenseChunk = 512;
 constexpr int64_t kVoxelCap = 512;
+// Levels whose value slice of one batch entry is at least this large take
+// their dot products in sorted order (msda_sdots_kernel): in query order
+// their rows are fetched from DRAM on almost every touch.
+constexpr double kSortedDotsMinBytes = 96.0 * 1048576.0;
 
 FastDiv make_fdiv(uint32_t d) {
   if (d == 0) d = 1;
@@ -560,6 +564,24 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   sp.div_h = make_fdiv(static_cast<uint32_t>(a.H));
   sp.div_l = make_fdiv(static_cast<uint32_t>(a.L));
   sp.div_q = make_fdiv(static_cast<uint32_t>(a.Q));
+  // levels whose dot products run in sorted order: those whose value slice
+  // of one batch entry passes kSortedDotsMinBytes (MSDA_SORTED_DOTS_MB, MiB)
+  {
+    const char* sd_env = std::getenv("MSDA_SORTED_DOTS_MB");
+    const double min_bytes = sd_env ? std::atof(sd_env) * 1048576.0 : kSortedDotsMinBytes;
+    for (int64_t l = 0; l < a.L; ++l) {
+      int64_t nvox = 1;
+      for (int ax = 0; ax < a.ndim; ++ax) nvox *= p.lv.size[l][ax];
+      sp.div_cx[l] = make_fdiv(static_cast<uint32_t>(sp.cells[l][0]));
+      sp.div_cy[l] = make_fdiv(static_cast<uint32_t>(sp.cells[l][1]));
+      if (nvox > 0 && static_cast<double>(nvox * a.H * row_bytes) >= min_bytes) {
+        sp.sdots_mask |= 1 << l;
+        sp.sl_level[sp.nsl++] = static_cast<int32_t>(l);
+      }
+    }
+    sp.sd_chunks = static_cast<int32_t>((a.Q * a.P + kSdotsPer - 1) / kSdotsPer);
+    if (nb * a.H * sp.nsl * sp.sd_chunks >= INT32_MAX) return false;
+  }
   pl.sp = sp;
   pl.sorted = true;
   pl.chunk_b = nb;

@@ -257,6 +257,86 @@ __device__ __forceinline__ Corners<NDIM> make_corners(const Point<NDIM>& pt, con
   return cs;
 }
 
+// One sample as a lane group needs it to gather its chunks: resolved once
+// by one lane of the group and broadcast to the others (the scalar work of a
+// sample -- location loads, axis resolution, corner validity, key of the
+// lower corner -- then costs each lane a fraction, not all of it).
+struct SampleMeta {
+  int32_t key0;   // key of the lower corner (start + linear index; may lie
+                  // outside the level where that corner is invalid)
+  uint32_t info;  // bits 0-7: corner c valid; 8-10: clamp pass per axis;
+                  // 12-15: level; bit 16: sample skipped by this kernel
+  float f[3];     // fractional offsets
+  float a;        // attention weight
+};
+constexpr uint32_t kMetaSkip = 1u << 16;
+
+template <int NDIM>
+__device__ __forceinline__ SampleMeta make_meta(const Point<NDIM>& pt, const LevelGeom& g,
+                                                float a, int l) {
+  SampleMeta m;
+  bool v[3][2];
+#pragma unroll
+  for (int ax = 0; ax < 3; ++ax) {
+    if (ax < NDIM) {
+      v[ax][0] = static_cast<uint32_t>(pt.i0[ax]) < static_cast<uint32_t>(g.sz[ax]);
+      v[ax][1] = static_cast<uint32_t>(pt.i0[ax] + 1) < static_cast<uint32_t>(g.sz[ax]);
+    } else {
+      v[ax][0] = true;
+      v[ax][1] = false;
+    }
+  }
+  uint32_t info = static_cast<uint32_t>(l) << 12;
+#pragma unroll
+  for (int c = 0; c < (1 << NDIM); ++c)
+    if (v[0][c & 1] && v[1][(c >> 1) & 1] && v[2][(c >> 2) & 1]) info |= 1u << c;
+#pragma unroll
+  for (int ax = 0; ax < NDIM; ++ax)
+    if (pt.pass[ax]) info |= 1u << (8 + ax);
+  const int32_t zi = (NDIM == 3) ? pt.i0[2] : 0;
+  m.key0 = g.start + (zi * g.sz[1] + pt.i0[1]) * g.sz[0] + pt.i0[0];
+  m.info = info;
+  m.f[0] = pt.f[0];
+  m.f[1] = pt.f[1];
+  m.f[2] = NDIM == 3 ? pt.f[2] : 0.0f;
+  m.a = a;
+  return m;
+}
+
+// Lane `src` of each G-lane segment of the warp -> every lane of the segment
+// (all 32 lanes of the warp must take part).
+template <int NDIM>
+__device__ __forceinline__ SampleMeta shfl_meta(const SampleMeta& m, int src, int G) {
+  SampleMeta r;
+  r.key0 = __shfl_sync(0xffffffffu, m.key0, src, G);
+  r.info = __shfl_sync(0xffffffffu, m.info, src, G);
+#pragma unroll
+  for (int ax = 0; ax < NDIM; ++ax) r.f[ax] = __shfl_sync(0xffffffffu, m.f[ax], src, G);
+  if constexpr (NDIM == 2) r.f[2] = 0.0f;
+  r.a = __shfl_sync(0xffffffffu, m.a, src, G);
+  return r;
+}
+
+// The lane's chunks of the 2^d corner rows of a broadcast sample (corners
+// outside the level read as zero).
+template <typename T, int NDIM, int VB, int VPL>
+__device__ __forceinline__ void gather_meta_corners(const Problem& p, const SampleMeta& m,
+                                                    const LevelGeom& g, const char* vbase,
+                                                    int64_t key_bytes, int lane_off, int G,
+                                                    const bool* has,
+                                                    Raw<VB> (&raw)[1 << NDIM][VPL]) {
+  (void)p;
+  const char* p0 = vbase + static_cast<int64_t>(m.key0) * key_bytes + lane_off;
+#pragma unroll
+  for (int c = 0; c < (1 << NDIM); ++c) {
+    const char* pc = p0 + ((c & 1) ? g.dx : 0) + ((c & 2) ? g.dy : 0) + ((c & 4) ? g.dz : 0);
+    const bool ok = (m.info >> c) & 1u;
+#pragma unroll
+    for (int vv = 0; vv < VPL; ++vv)
+      raw[c][vv] = (ok && has[vv]) ? MSDA_LD_VALUE(VB, pc + vv * G * VB) : raw_zero<VB>();
+  }
+}
+
 // ------------------------------------------------------------------ forward
 template <typename T, typename TS, int NDIM, int VB, int VPL, bool FUSED>
 __device__ __forceinline__ void msda_fwd_body(const Problem p, T* __restrict__ out) {

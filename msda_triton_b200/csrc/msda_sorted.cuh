@@ -20,12 +20,15 @@
 //
 // grad_attn and grad_loc need no sort: msda_dots_kernel computes them in
 // query order (the forward's gather plus the corner dot products), and
-// counts the samples per cell on the way.
+// counts the samples per cell on the way -- except on the large sparse
+// levels, whose rows a query-order pass fetches from DRAM for every touch:
+// msda_sdots_kernel takes those in sorted (cell) order.
 //
 // Pipeline for one chunk of batch entries (all on one stream):
 //   msda_dots_kernel       grad_attn, grad_loc; rank = atomicAdd(count[key], 1)
 //   msda_scan_*            counts -> exclusive bucket starts
 //   msda_place_kernel      record (a, fractions, grad_out row, key) at start[key] + rank
+//   msda_sdots_kernel      grad_attn, grad_loc of the large sparse levels, in sorted order
 //   msda_dense_kernel      dense-level value gradient, per cell segment
 //   msda_voxel_kernel      sparse-level value gradient, gathered per value row
 //
@@ -71,7 +74,8 @@ struct __align__(16) SRec {
   float f[3];     // fractional offsets inside the cell
   uint32_t row;   // (b, q, h) row of grad_out
   int32_t key;    // bucket key
-  uint32_t pad[2];
+  uint32_t idx;   // sample index (b, q, h, l, p) inside the chunk
+  uint32_t pass;  // bit a: the location's gradient passes the clamp on axis a
 };
 
 // Everything the sorted pipeline adds to Problem (one chunk of batch
@@ -101,6 +105,11 @@ struct SortPlan {
   FastDiv div_nv;                  // / vnv
   int32_t vsmem;                   // its dynamic shared memory
   FastDiv div_lp, div_p, div_h, div_l, div_q;
+  int32_t sdots_mask;              // levels whose dot products msda_sdots_kernel takes in sorted order
+  int32_t nsl;                     // such levels
+  int32_t sl_level[kMaxLevels];    // k-th such level
+  int32_t sd_chunks;               // msda_sdots_kernel CTAs per (b, h, level)
+  FastDiv div_cx[kMaxLevels], div_cy[kMaxLevels];  // / cells[l][0], / cells[l][1]
   int32_t* cnt;                    // nkeys + 1: counts, then exclusive starts
   int32_t* bsum;                   // scan block sums
   int32_t* pos;                    // n: each sample's rank inside its bucket
@@ -193,7 +202,156 @@ __device__ __forceinline__ void stage_chunk(void* dst, const void* src) {
 // sample costs a few shuffles instead of a full butterfly of four values.
 // The lane that ends with a sample's grad_attn also counts the sample into
 // its bucket (the counting sort's histogram) and keeps its rank there.
+//
+// Levels in sp.sdots_mask (the large sparse ones, whose value rows do not
+// stay in L2 between the scattered touches of a query-order pass) are only
+// counted here; msda_sdots_kernel takes their dot products after the sort.
 constexpr int kDotBatch = 2;
+
+// Lane bookkeeping of the transposed reduction of NV = 4 * kDotBatch values
+// over a lane group of G lanes.
+struct DotLanes {
+  unsigned gmask;  // the group's lanes
+  int vbase;       // first of the values this lane keeps
+  int nkeep;       // values kept
+  bool writer;     // lanes above NV hold duplicates
+};
+
+__device__ __forceinline__ DotLanes dot_lanes(int G, int j, int lane) {
+  constexpr int NV = kDotBatch * 4;
+  DotLanes dl;
+  dl.gmask = G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane & ~(G - 1)));
+  int steps = 0;
+  dl.vbase = 0;
+#pragma unroll
+  for (int s = 1, half = NV / 2; s < NV; s <<= 1, half >>= 1)
+    if (s < G) {
+      ++steps;
+      if (j & s) dl.vbase += half;
+    }
+  dl.nkeep = NV >> steps;
+  dl.writer = G <= NV || j < NV;
+  return dl;
+}
+
+// v[4 i + comp] for sample i and comp (attn, x, y, z): each step halves the
+// values a lane keeps; afterwards lane j holds the group sums of
+// v[dl.vbase ... dl.vbase + dl.nkeep) in v[0 ... nkeep).
+__device__ __forceinline__ void dot_reduce(float* v, int G, int j, const DotLanes& dl) {
+  constexpr int NV = kDotBatch * 4;
+#pragma unroll
+  for (int s = 1, half = NV / 2; s < NV; s <<= 1, half >>= 1) {
+    if (s < G) {
+      const bool up = (j & s) != 0;
+#pragma unroll
+      for (int t = 0; t < NV / 2; ++t) {
+        if (t < half) {
+          const float send = up ? v[t] : v[t + half];
+          const float keep = up ? v[t + half] : v[t];
+          v[t] = keep + __shfl_xor_sync(dl.gmask, send, s);
+        }
+      }
+    }
+  }
+  for (int s = NV; s < G; s <<= 1) v[0] += __shfl_xor_sync(dl.gmask, v[0], s);
+}
+
+// One sample's lane partials of d out/d attn and d out/d index per axis from
+// its corner dot products D[c] = <grad_out row, corner row c> (lane partial),
+// factored axis by axis: ex = the x-interpolated dots, dx = their
+// x-differences.
+template <int NDIM>
+__device__ __forceinline__ void corner_dot_grads(const float* D, const float* f, float* out) {
+  constexpr int NC = 1 << NDIM;
+  const float fx = f[0], fy = f[1];
+  const float gx0 = __fsub_rn(1.0f, fx), gy0 = __fsub_rn(1.0f, fy);
+  float ex[NC / 2], dx[NC / 2];
+#pragma unroll
+  for (int t = 0; t < NC / 2; ++t) {
+    ex[t] = fmaf(fx, D[2 * t + 1], gx0 * D[2 * t]);
+    dx[t] = D[2 * t + 1] - D[2 * t];
+  }
+  if constexpr (NDIM == 2) {
+    out[0] = fmaf(fy, ex[1], gy0 * ex[0]);
+    out[1] = fmaf(fy, dx[1], gy0 * dx[0]);
+    out[2] = ex[1] - ex[0];
+    out[3] = 0.0f;
+  } else {
+    const float fz = f[2], gz0 = __fsub_rn(1.0f, fz);
+    // t = by + 2 * bz
+    const float ey0 = fmaf(fy, ex[1], gy0 * ex[0]);  // z = 0, y-interpolated
+    const float ey1 = fmaf(fy, ex[3], gy0 * ex[2]);  // z = 1
+    out[0] = fmaf(fz, ey1, gz0 * ey0);
+    out[1] = fmaf(fz, fmaf(fy, dx[3], gy0 * dx[2]), gz0 * fmaf(fy, dx[1], gy0 * dx[0]));
+    out[2] = fmaf(fz, ex[3] - ex[2], gz0 * (ex[1] - ex[0]));
+    out[3] = ey1 - ey0;
+  }
+}
+
+// Lane partial dot products of one sample: its 2^d corner chunks (corners
+// outside the level read the zero row: their dot is exactly 0) against the
+// lane's grad_out chunks.
+template <typename T, int NDIM, int VB, int VPL>
+__device__ __forceinline__ void corner_dots(const Corners<NDIM>& cs, const bool* has, int G,
+                                            const float (*go)[Chunk<T, VB>::EPV], float* D) {
+  using CK = Chunk<T, VB>;
+  constexpr int EPV = CK::EPV;
+  constexpr int NC = 1 << NDIM;
+  Raw<VB> raw[NC][VPL];
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int vv = 0; vv < VPL; ++vv)
+      raw[c][vv] = has[vv] ? MSDA_LD_VALUE(VB, cs.valid[c] ? cs.ptr[c] + vv * G * VB : cs.ptr[c])
+                           : raw_zero<VB>();
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    float dot = 0.0f;
+#pragma unroll
+    for (int vv = 0; vv < VPL; ++vv) {
+      float x[EPV];
+      CK::unpack(raw[c][vv], x);
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) dot = fmaf(go[vv][e], x[e], dot);
+    }
+    D[c] = dot;
+  }
+}
+
+// The lane's kept results (dot_reduce) stored as grad_attn / grad_loc of
+// their samples: batch slot i holds sample sidx[i] (kNoSample: none), its
+// attention weight sa[i] and sinfo[i] = level | clamp-pass bits << 8.
+constexpr uint32_t kNoSample = 0xffffffffu;
+
+template <typename TS, int NDIM>
+__device__ __forceinline__ void store_dot_results(const Problem& p, const float* v,
+                                                  const DotLanes& dl, const uint32_t* sidx,
+                                                  const float* sa, const int32_t* sinfo,
+                                                  TS* grad_loc, TS* grad_attn) {
+  constexpr int NV = kDotBatch * 4;
+#pragma unroll
+  for (int t = 0; t < NV; ++t) {
+    if (t < dl.nkeep) {
+      const int idx = dl.vbase + t;
+      const int slot = idx >> 2, comp = idx & 3;
+      float a = 0.0f;
+      uint32_t si = kNoSample;
+      int32_t info = 0;
+#pragma unroll
+      for (int i = 0; i < kDotBatch; ++i)
+        if (i == slot) { a = sa[i]; si = sidx[i]; info = sinfo[i]; }
+      if (si == kNoSample) continue;
+      if (comp == 0) {
+        grad_attn[si] = Elem<TS>::from_f(v[t]);
+      } else if (comp - 1 < NDIM) {
+        const int ax = comp - 1, ls = info & 0xff;
+        const float val = ((info >> (8 + ax)) & 1)
+                              ? a * v[t] * static_cast<float>(p.lv.size[ls][ax]) : 0.0f;
+        grad_loc[static_cast<int64_t>(si) * NDIM + ax] = Elem<TS>::from_f(val);
+      }
+    }
+  }
+}
 
 template <typename T, typename TS, int NDIM, int VB, int VPL>
 __global__ void __launch_bounds__(kThreads, 4)
@@ -208,7 +366,6 @@ __global__ void __launch_bounds__(kThreads, 4)
   const int G = 1 << p.log2g;
   const int j = static_cast<int>(tid & static_cast<uint64_t>(G - 1));
   const int lane = static_cast<int>(threadIdx.x & 31u);
-  const unsigned gmask = G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane & ~(G - 1)));
   // rows past the end stay (on row 0, storing nothing) for the group shuffles
   const bool active = r < static_cast<uint64_t>(p.B * p.Q * p.H);
   if (!active) r = 0;
@@ -236,143 +393,221 @@ __global__ void __launch_bounds__(kThreads, 4)
       CK::unpack(rg, go[v]);
     }
   }
-  // values this lane keeps after the transposed steps, and the first one
-  int vbase_i = 0, steps = 0;
-#pragma unroll
-  for (int s = 1, half = NV / 2; s < NV; s <<= 1, half >>= 1)
-    if (s < G) {
-      ++steps;
-      if (j & s) vbase_i += half;
-    }
-  const int nkeep = NV >> steps;
-  const bool writer = G <= NV || j < NV;  // lanes above NV hold duplicates
+  const DotLanes dl = dot_lanes(G, j, lane);
 
-  const int P = static_cast<int>(p.P);
-  int l = 0, pp = 0;
-  for (int s0 = 0; s0 < LP; s0 += kDotBatch) {
-    float v[NV];
-    float sa[kDotBatch];
-    int32_t sinfo[kDotBatch], skey[kDotBatch];
-#pragma unroll
-    for (int i = 0; i < kDotBatch; ++i) {
-      v[4 * i] = v[4 * i + 1] = v[4 * i + 2] = v[4 * i + 3] = 0.0f;
-      sa[i] = 0.0f;
-      sinfo[i] = 0;
-      skey[i] = 0;
-      const int s = s0 + i;
-      if (s < LP) {
-        const LevelGeom g = level_geom_tab(p, l, key_bytes);
-        const Point<NDIM> pt = load_point<TS, NDIM>(lrow + s * NDIM, g.sz, p);
-        const float a = Elem<TS>::to_f(arow[s]);
-        const Corners<NDIM> cs = make_corners<NDIM>(pt, g, vbase, key_bytes, j * VB);
-        Raw<VB> raw[NC][VPL];
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-#pragma unroll
-          for (int vv = 0; vv < VPL; ++vv)
-            raw[c][vv] = has[vv] ? MSDA_LD_VALUE(VB, cs.valid[c] ? cs.ptr[c] + vv * G * VB : cs.ptr[c])
-                                 : raw_zero<VB>();
-        // lane partial dot products with the corner rows (corners outside
-        // the level read the zero row: their dot is exactly 0)
-        float D[NC];
-#pragma unroll
-        for (int c = 0; c < NC; ++c) {
-          float dot = 0.0f;
-#pragma unroll
-          for (int vv = 0; vv < VPL; ++vv) {
-            float x[EPV];
-            CK::unpack(raw[c][vv], x);
-#pragma unroll
-            for (int e = 0; e < EPV; ++e) dot = fmaf(go[vv][e], x[e], dot);
-          }
-          D[c] = dot;
-        }
-        // sum over corners of w_c * D_c and of d(w_c)/d(index) * D_c, factored
-        // axis by axis: ex = the x-interpolated dots, dx = their x-differences
-        const float fx = pt.f[0], fy = pt.f[1];
-        const float gx0 = __fsub_rn(1.0f, fx), gy0 = __fsub_rn(1.0f, fy);
-        float ex[NC / 2], dx[NC / 2];
-#pragma unroll
-        for (int t = 0; t < NC / 2; ++t) {
-          ex[t] = fmaf(fx, D[2 * t + 1], gx0 * D[2 * t]);
-          dx[t] = D[2 * t + 1] - D[2 * t];
-        }
-        float g_attn, g_x, g_y, g_z = 0.0f;
-        if constexpr (NDIM == 2) {
-          g_attn = fmaf(fy, ex[1], gy0 * ex[0]);
-          g_x = fmaf(fy, dx[1], gy0 * dx[0]);
-          g_y = ex[1] - ex[0];
-        } else {
-          const float fz = pt.f[2], gz0 = __fsub_rn(1.0f, fz);
-          // t = by + 2 * bz
-          const float ey0 = fmaf(fy, ex[1], gy0 * ex[0]);  // z = 0, y-interpolated
-          const float ey1 = fmaf(fy, ex[3], gy0 * ex[2]);  // z = 1
-          g_attn = fmaf(fz, ey1, gz0 * ey0);
-          g_x = fmaf(fz, fmaf(fy, dx[3], gy0 * dx[2]), gz0 * fmaf(fy, dx[1], gy0 * dx[0]));
-          g_y = fmaf(fz, ex[3] - ex[2], gz0 * (ex[1] - ex[0]));
-          g_z = ey1 - ey0;
-        }
-        v[4 * i] = g_attn;
-        v[4 * i + 1] = g_x;
-        v[4 * i + 2] = g_y;
-        v[4 * i + 3] = g_z;
-        sa[i] = a;
-        int32_t pass = 0;
-#pragma unroll
-        for (int ax = 0; ax < NDIM; ++ax) pass |= pt.pass[ax] ? (1 << ax) : 0;
-        sinfo[i] = l | (pass << 8);
-        // the sample's rank in its bucket, taken now by the lane that will
-        // store the sample's results, so the atomic's latency hides behind
-        // the corner loads
-        const int vi = 4 * i;
-        if (active && writer && vi >= vbase_i && vi < vbase_i + nkeep)
-          skey[i] = atomicAdd(sp.cnt + bucket_key<NDIM>(pt, g.sz, sp.cells[l],
-                                                        kbh + sp.lvl_base[l]), 1);
-        if (++pp == P) { pp = 0; ++l; }
-      }
+  // Rounds of G samples: lane j resolves sample r0 + j (and takes its rank
+  // in its bucket), then the group walks the round's samples kDotBatch at a
+  // time with the resolved samples broadcast from their lanes.
+  for (int r0 = 0; r0 < LP; r0 += G) {
+    SampleMeta mine;
+    mine.key0 = 0;
+    mine.info = kMetaSkip;
+    mine.f[0] = mine.f[1] = mine.f[2] = 0.0f;
+    mine.a = 0.0f;
+    int32_t rank = -1;
+    const int sj = r0 + j;
+    if (sj < LP) {
+      const int l = static_cast<int>(fdiv(static_cast<uint32_t>(sj), sp.div_p));
+      const LevelGeom g = level_geom_tab(p, l, key_bytes);
+      const Point<NDIM> pt = load_point<TS, NDIM>(lrow + sj * NDIM, g.sz, p);
+      mine = make_meta<NDIM>(pt, g, Elem<TS>::to_f(arow[sj]), l);
+      if ((sp.sdots_mask >> l) & 1) mine.info |= kMetaSkip;
+      if (active)
+        rank = atomicAdd(sp.cnt + bucket_key<NDIM>(pt, g.sz, sp.cells[l], kbh + sp.lvl_base[l]),
+                         1);
     }
-    // transposed reduction over the group
+    const int nr = LP - r0 < G ? LP - r0 : G;
+    for (int t0 = 0; t0 < nr; t0 += kDotBatch) {
+      float v[NV];
+      float sa[kDotBatch];
+      uint32_t sidx[kDotBatch];
+      int32_t sinfo[kDotBatch];
 #pragma unroll
-    for (int s = 1, half = NV / 2; s < NV; s <<= 1, half >>= 1) {
-      if (s < G) {
-        const bool up = (j & s) != 0;
+      for (int i = 0; i < kDotBatch; ++i) {
+        v[4 * i] = v[4 * i + 1] = v[4 * i + 2] = v[4 * i + 3] = 0.0f;
+        sa[i] = 0.0f;
+        sidx[i] = kNoSample;
+        sinfo[i] = 0;
+        const int t = t0 + i;
+        if (t < nr) {
+          const SampleMeta m = shfl_meta<NDIM>(mine, t, G);
+          if (!(m.info & kMetaSkip)) {
+            const int l = static_cast<int>((m.info >> 12) & 0xfu);
+            const LevelGeom g = level_geom_tab(p, l, key_bytes);
+            Raw<VB> raw[NC][VPL];
+            gather_meta_corners<T, NDIM, VB, VPL>(p, m, g, vbase, key_bytes, j * VB, G, has, raw);
+            float D[NC];
 #pragma unroll
-        for (int t = 0; t < NV / 2; ++t) {
-          if (t < half) {
-            const float send = up ? v[t] : v[t + half];
-            const float keep = up ? v[t + half] : v[t];
-            v[t] = keep + __shfl_xor_sync(gmask, send, s);
+            for (int c = 0; c < NC; ++c) {
+              float dot = 0.0f;
+#pragma unroll
+              for (int vv = 0; vv < VPL; ++vv) {
+                float x[EPV];
+                CK::unpack(raw[c][vv], x);
+#pragma unroll
+                for (int e = 0; e < EPV; ++e) dot = fmaf(go[vv][e], x[e], dot);
+              }
+              D[c] = dot;
+            }
+            corner_dot_grads<NDIM>(D, m.f, v + 4 * i);
+            sa[i] = m.a;
+            sinfo[i] = l | static_cast<int32_t>(((m.info >> 8) & 7u) << 8);
+            sidx[i] = static_cast<uint32_t>(row * LP + r0 + t);
           }
         }
       }
+      dot_reduce(v, G, j, dl);
+      if (active && dl.writer)
+        store_dot_results<TS, NDIM>(p, v, dl, sidx, sa, sinfo, grad_loc, grad_attn);
     }
-    for (int s = NV; s < G; s <<= 1) v[0] += __shfl_xor_sync(gmask, v[0], s);
-    if (active && writer) {
+    if (rank >= 0) sp.pos[row * LP + sj] = rank;
+  }
+}
+
+// ------------------------------------------------------------------ sdots
+// grad_attn and grad_loc of the levels in sp.sdots_mask, in sorted order: a
+// lane group per record, kDotBatch records at a time, with the dot products
+// and reduction of msda_dots_kernel.  The records of a (b, h, level) run
+// through the level's cells z-major, so the value rows a CTA touches lie in
+// a few consecutive planes and stay in L2; consecutive CTAs take the same
+// stretch of positions of the eight heads (CTA index: head fastest), whose
+// rows share the value lines.  The sample's grad_out row is gathered per
+// record (grad_out of a batch entry is a few tens of MB and stays in L2).
+constexpr int kSdotsPer = 512;  // sorted positions per msda_sdots_kernel CTA
+
+template <typename T, typename TS, int NDIM, int VB, int VPL>
+__global__ void __launch_bounds__(kThreads, 4)
+    msda_sdots_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
+                      TS* __restrict__ grad_loc, TS* __restrict__ grad_attn) {
+  using CK = Chunk<T, VB>;
+  constexpr int EPV = CK::EPV;
+  constexpr int NC = 1 << NDIM;
+  constexpr int NV = kDotBatch * 4;
+  // CTA -> (b, level, stretch, h), h fastest
+  uint32_t u = blockIdx.x;
+  const int32_t h = static_cast<int32_t>(u % static_cast<uint32_t>(p.H));
+  u /= static_cast<uint32_t>(p.H);
+  const int32_t k = static_cast<int32_t>(u % static_cast<uint32_t>(sp.sd_chunks));
+  u /= static_cast<uint32_t>(sp.sd_chunks);
+  const int32_t li = static_cast<int32_t>(u % static_cast<uint32_t>(sp.nsl));
+  const int64_t b = u / static_cast<uint32_t>(sp.nsl);
+  const int l = sp.sl_level[li];
+  const int64_t QP = p.Q * p.P;
+  const int64_t bh = b * p.H + h;
+  const SRec* recs = sp.srec + (bh * p.L + l) * QP;  // the (b, h, l) block of positions
+  const int64_t q_end = int64_t{k + 1} * kSdotsPer < QP ? int64_t{k + 1} * kSdotsPer : QP;
+
+  const int G = 1 << p.log2g;
+  const int j = static_cast<int>(threadIdx.x) & (G - 1);
+  const int grp = static_cast<int>(threadIdx.x) >> p.log2g;
+  const int groups = kThreads >> p.log2g;
+  const int lane = static_cast<int>(threadIdx.x & 31u);
+  const DotLanes dl = dot_lanes(G, j, lane);
+  bool has[VPL];
 #pragma unroll
-      for (int t = 0; t < NV; ++t) {
-        if (t < nkeep) {
-          const int idx = vbase_i + t;
-          const int slot = idx >> 2, comp = idx & 3;
-          const int s = s0 + slot;
-          if (s < LP) {
-            float a = 0.0f;
-            int32_t info = 0, key = 0;
+  for (int v = 0; v < VPL; ++v) has[v] = j + v * G < p.nv;
+
+  const int64_t e = static_cast<int64_t>(sizeof(T));
+  const int64_t key_bytes = p.H * p.C * e;
+  const char* vbase = static_cast<const char*>(p.value) + (b * p.K * p.H + h) * p.C * e;
+  const LevelGeom g = level_geom_tab(p, l, key_bytes);
+  const int32_t kb = static_cast<int32_t>(bh) * sp.seg_keys + sp.lvl_base[l];
+  const uint32_t ncell = static_cast<uint32_t>(sp.cells[l][0]) *
+                         static_cast<uint32_t>(sp.cells[l][1]) *
+                         static_cast<uint32_t>(sp.cells[l][2]);
+
+  // Rounds (CTA-uniform, so every lane of a warp takes every shuffle): each
+  // group takes G consecutive records; lane j decodes record q0 + j, then the
+  // group walks them kDotBatch at a time.
+  for (int64_t qr = int64_t{k} * kSdotsPer; qr < q_end; qr += int64_t{groups} * G) {
+    const int64_t q0 = qr + int64_t{grp} * G;
+    SampleMeta mine;
+    mine.key0 = 0;
+    mine.info = kMetaSkip;
+    mine.f[0] = mine.f[1] = mine.f[2] = 0.0f;
+    mine.a = 0.0f;
+    uint32_t my_row = 0, my_idx = kNoSample;
+    if (q0 + j < q_end) {
+      const SRec* rp = recs + q0 + j;
+      const uint4 r0 = __ldg(reinterpret_cast<const uint4*>(rp));
+      const uint4 r1 = __ldg(reinterpret_cast<const uint4*>(rp) + 1);
+      // r0 = (a, f0, f1, f2), r1 = (row, key, idx, pass)
+      const uint32_t c = static_cast<uint32_t>(static_cast<int32_t>(r1.y) - kb);
+      Point<NDIM> pt;
+      pt.f[0] = __uint_as_float(r0.y);
+      pt.f[1] = __uint_as_float(r0.z);
+      pt.f[2] = __uint_as_float(r0.w);
+      const uint32_t t = fdiv(c, sp.div_cx[l]);
+      pt.i0[0] = static_cast<int32_t>(c - t * static_cast<uint32_t>(sp.cells[l][0])) - 1;
+      if constexpr (NDIM == 3) {
+        const uint32_t z = fdiv(t, sp.div_cy[l]);
+        pt.i0[1] = static_cast<int32_t>(t - z * static_cast<uint32_t>(sp.cells[l][1])) - 1;
+        pt.i0[2] = static_cast<int32_t>(z) - 1;
+      } else {
+        pt.i0[1] = static_cast<int32_t>(t) - 1;
+        pt.i0[2] = 0;
+      }
+      // the level's dead bucket: no corner inside the level
+      if (c >= ncell) pt.i0[0] = pt.i0[1] = pt.i0[2] = -2;
 #pragma unroll
-            for (int i = 0; i < kDotBatch; ++i)
-              if (i == slot) { a = sa[i]; info = sinfo[i]; key = skey[i]; }
-            const int64_t si = row * LP + s;
-            if (comp == 0) {
-              grad_attn[si] = Elem<TS>::from_f(v[t]);
-              sp.pos[si] = key;  // the rank taken above
-            } else if (comp - 1 < NDIM) {
-              const int ax = comp - 1, ls = info & 0xff;
-              const float val = ((info >> (8 + ax)) & 1)
-                                    ? a * v[t] * static_cast<float>(p.lv.size[ls][ax]) : 0.0f;
-              grad_loc[si * NDIM + ax] = Elem<TS>::from_f(val);
+      for (int ax = 0; ax < 3; ++ax) pt.pass[ax] = (r1.w >> ax) & 1u;
+      mine = make_meta<NDIM>(pt, g, __uint_as_float(r0.x), l);
+      my_row = r1.x;
+      my_idx = r1.z;
+    }
+    const int64_t left = q_end - q0;
+    const int nr = left <= 0 ? 0 : (left < G ? static_cast<int>(left) : G);
+    for (int t0 = 0; t0 < G; t0 += kDotBatch) {
+      float v[NV];
+      float sa[kDotBatch];
+      uint32_t sidx[kDotBatch];
+      int32_t sinfo[kDotBatch];
+#pragma unroll
+      for (int i = 0; i < kDotBatch; ++i) {
+        v[4 * i] = v[4 * i + 1] = v[4 * i + 2] = v[4 * i + 3] = 0.0f;
+        sa[i] = 0.0f;
+        sidx[i] = kNoSample;
+        sinfo[i] = 0;
+        const int t = t0 + i;
+        const SampleMeta m = shfl_meta<NDIM>(mine, t, G);
+        const uint32_t grow = __shfl_sync(0xffffffffu, my_row, t, G);
+        const uint32_t gidx = __shfl_sync(0xffffffffu, my_idx, t, G);
+        if (t < nr) {
+          float go[VPL][EPV];
+          {
+            const char* gorow = reinterpret_cast<const char*>(grad_out) +
+                                static_cast<int64_t>(grow) * p.C * e;
+#pragma unroll
+            for (int vv = 0; vv < VPL; ++vv) {
+              const Raw<VB> rg =
+                  has[vv] ? ld_chunk<VB>(gorow + (j + vv * G) * VB) : raw_zero<VB>();
+              CK::unpack(rg, go[vv]);
             }
           }
+          Raw<VB> raw[NC][VPL];
+          gather_meta_corners<T, NDIM, VB, VPL>(p, m, g, vbase, key_bytes, j * VB, G, has, raw);
+          float D[NC];
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            float dot = 0.0f;
+#pragma unroll
+            for (int vv = 0; vv < VPL; ++vv) {
+              float x[EPV];
+              CK::unpack(raw[c][vv], x);
+#pragma unroll
+              for (int ee = 0; ee < EPV; ++ee) dot = fmaf(go[vv][ee], x[ee], dot);
+            }
+            D[c] = dot;
+          }
+          corner_dot_grads<NDIM>(D, m.f, v + 4 * i);
+          sa[i] = m.a;
+          sinfo[i] = l | static_cast<int32_t>(((m.info >> 8) & 7u) << 8);
+          sidx[i] = gidx;
         }
       }
+      dot_reduce(v, G, j, dl);
+      if (dl.writer)
+        store_dot_results<TS, NDIM>(p, v, dl, sidx, sa, sinfo, grad_loc, grad_attn);
     }
   }
 }
@@ -400,7 +635,10 @@ __global__ void __launch_bounds__(kThreads) msda_place_kernel(const Problem p, c
   rec.key = bucket_key<NDIM>(pt, p.lv.size[l], sp.cells[l],
                              (static_cast<int32_t>(b) * static_cast<int32_t>(p.H) + h) *
                                  sp.seg_keys + sp.lvl_base[l]);
-  rec.pad[0] = rec.pad[1] = 0u;
+  rec.idx = s;
+  rec.pass = 0u;
+#pragma unroll
+  for (int ax = 0; ax < NDIM; ++ax) rec.pass |= pt.pass[ax] ? (1u << ax) : 0u;
   const int32_t at = __ldg(sp.cnt + rec.key) + sp.pos[s];
   uint4* dst = reinterpret_cast<uint4*>(sp.srec + at);
   const uint4* src = reinterpret_cast<const uint4*>(&rec);

@@ -24,6 +24,19 @@ static cudaError_t dots_one(const Problem& p, const SortPlan& sp, const void* go
   return cudaErrorInvalidValue;
 }
 
+template <typename T, typename TS, int NDIM, int VB, int VPL>
+static cudaError_t sdots_one(const Problem& p, const SortPlan& sp, const void* go, void* gl,
+                             void* ga, cudaStream_t st) {
+  if constexpr (kAllowed<VB, VPL> && VB != 8) {
+    const int64_t grid = p.B * p.H * int64_t{sp.nsl} * sp.sd_chunks;
+    msda_sdots_kernel<T, TS, NDIM, VB, VPL><<<dim3(static_cast<unsigned>(grid)), kThreads, 0, st>>>(
+        p, sp, static_cast<const T*>(go), static_cast<TS*>(gl), static_cast<TS*>(ga));
+    return cudaGetLastError();
+  }
+  (void)p; (void)sp; (void)go; (void)gl; (void)ga; (void)st;
+  return cudaErrorInvalidValue;
+}
+
 template <typename T, int NDIM, int VB, int VPL>
 static cudaError_t dense_one(const Problem& p, const SortPlan& sp, const void* go, float* gacc,
                              cudaStream_t st) {
@@ -93,6 +106,12 @@ static cudaError_t sorted_chunk(const LaunchShape& ls, const LaunchShape& lsd, c
   const unsigned sblocks = static_cast<unsigned>((int64_t{sp.n} + kThreads - 1) / kThreads);
   msda_place_kernel<TS, NDIM><<<sblocks, kThreads, 0, st>>>(p, sp);
   if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  if (sp.nsl > 0) {
+#define MSDA_SDOTS_CALL(VB, VPL) err = sdots_one<T, TS, NDIM, VB, VPL>(p, sp, go, gl, ga, st); break
+    MSDA_FWD_SHAPE_SWITCH(ls.vb, ls.vpl, MSDA_SDOTS_CALL)
+#undef MSDA_SDOTS_CALL
+    if (err != cudaSuccess) return err;
+  }
   if (sp.ndl > 0) {
     switch (lsd.vb * 16 + lsd.vpl) {
       case 16 * 16 + 1: err = dense_one<T, NDIM, 16, 1>(p, sp, go, gacc, st); break;
@@ -117,7 +136,8 @@ static cudaError_t sorted_chunk(const LaunchShape& ls, const LaunchShape& lsd, c
 }
 
 // One chunk of the sorted backward: dots (+ histogram), scan, place, the
-// dense and voxel value-gradient kernels.  gacc receives the dense levels'
+// sorted-order dots of the large sparse levels, the dense and voxel
+// value-gradient kernels.  gacc receives the dense levels'
 // value gradient (+=); the caller zero-fills it before and rounds it after.
 template <typename T, typename TS>
 cudaError_t launch_sorted_bwd(const LaunchShape& ls, const LaunchShape& lsd, const Problem& p,

@@ -25,8 +25,17 @@ pytestmark = pytest.mark.gpu
 SPLITS = {"voxel": "1e9", "auto": None, "cell": "0"}
 
 
-def _env(monkeypatch, split="auto", chunk=None, path="sorted"):
+# levels whose grad_attn / grad_loc run in sorted order (msda_sdots_kernel):
+# the default (only value slices of 96 MiB and more: none at these sizes) or all
+SDOTS = {"query": None, "sorted": "0"}
+
+
+def _env(monkeypatch, split="auto", chunk=None, path="sorted", sdots="query"):
     monkeypatch.setenv("MSDA_BWD_PATH", path)
+    if SDOTS[sdots] is None:
+        monkeypatch.delenv("MSDA_SORTED_DOTS_MB", raising=False)
+    else:
+        monkeypatch.setenv("MSDA_SORTED_DOTS_MB", SDOTS[sdots])
     if SPLITS[split] is None:
         monkeypatch.delenv("MSDA_VOXEL_DENSITY", raising=False)
     else:
@@ -50,12 +59,13 @@ def _upcast(inp):
     return [x.float() if x.is_floating_point() else x for x in inp]
 
 
-@pytest.mark.parametrize("split", ["voxel", "cell"])
+@pytest.mark.parametrize("split,sdots", [("voxel", "query"), ("cell", "sorted")])
 @pytest.mark.parametrize("name", golden_names())
-def test_golden_parity_sorted(monkeypatch, name, split):
-    """Every golden fixture through the sorted backward, each level formed
-    both ways, against the reference's own outputs."""
-    _env(monkeypatch, split)
+def test_golden_parity_sorted(monkeypatch, name, split, sdots):
+    """Every golden fixture through the sorted backward, each level's value
+    gradient formed both ways and its dot products taken in both orders,
+    against the reference's own outputs."""
+    _env(monkeypatch, split, sdots=sdots)
     z = load_golden(name)
     t = {k: torch.from_numpy(z[k]) for k in ("value", "loc", "attn", "grad_out", "shapes")}
     ndim = t["shapes"].shape[1]
@@ -77,12 +87,13 @@ DTYPES = [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16),
           (torch.float16, torch.float32)]
 
 
+@pytest.mark.parametrize("sdots", ["query", "sorted"])
 @pytest.mark.parametrize("split", ["voxel", "auto", "cell"])
 @pytest.mark.parametrize("dt", DTYPES, ids=lambda d: f"{str(d[0])[6:]}-{str(d[1])[6:]}")
 @pytest.mark.parametrize("case", CASES, ids=[f"{c[0]}d-{len(c[6])}lvl-q{c[2]}" for c in CASES])
-def test_sorted_matches_oracle(monkeypatch, case, dt, split):
+def test_sorted_matches_oracle(monkeypatch, case, dt, split, sdots):
     ndim, B, Q, H, C, P, shapes = case
-    _env(monkeypatch, split)
+    _env(monkeypatch, split, sdots=sdots)
     tf, tg = _tols(dt[0])
     for clamp, rng in ((True, (0.0, 1.0)), (False, (-0.15, 1.15))):
         inp = _cast(make_inputs(B, Q, H, C, P, shapes, seed=Q + C + ndim, loc_range=rng), *dt)
@@ -100,10 +111,10 @@ def test_chunks_match_one_pass(monkeypatch, ndim, dtype):
     inp = _cast(make_inputs(5, 300, 4, 32, 4, shapes, seed=7 + ndim), dtype, dtype)
     ref = oracle_all(*_upcast(inp))
     tf, tg = _tols(dtype)
-    for chunk in (1, 2, None):
-        _env(monkeypatch, "auto", chunk)
+    for chunk, sdots in ((1, "sorted"), (2, "query"), (2, "sorted"), (None, "sorted")):
+        _env(monkeypatch, "auto", chunk, sdots=sdots)
         got = cuda_fwd_bwd(ndim, *inp)
-        check_all(got, ref, tf, tg, f"chunk={chunk}")
+        check_all(got, ref, tf, tg, f"chunk={chunk} {sdots}")
 
 
 @pytest.mark.parametrize("ndim", [2, 3])
@@ -138,14 +149,15 @@ def _clustered(ndim, B, Q, H, C, P, shapes, box, seed, dtype):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("ndim", [2, 3])
-@pytest.mark.parametrize("path", ["sorted", "scatter"])
+@pytest.mark.parametrize("path", ["sorted", "sorted-sdots", "scatter"])
 def test_clustered_samples_half_precision(monkeypatch, ndim, dtype, path):
     """Hundreds of contributions per grad_value element on a level the
     density plan rates sparse: every fp16/bf16 backward stays within the
     half-precision bar of the fp32 oracle."""
     shapes = [(64, 96), (32, 48), (16, 24)] if ndim == 2 else [(24, 32, 32), (12, 16, 16), (6, 8, 8)]
     inp = _clustered(ndim, 2, 2000, 4, 32, 4, shapes, 4, 11 + ndim, dtype)
-    _env(monkeypatch, "auto", path=path)
+    _env(monkeypatch, "auto", path=path.split("-")[0],
+         sdots="sorted" if path.endswith("sdots") else "query")
     got = cuda_fwd_bwd(ndim, *inp)
     ref = oracle_all(*_upcast(inp))
     check_all(got, ref, TOL_HALF, TOL_HALF, f"clustered {dtype} {path}")
