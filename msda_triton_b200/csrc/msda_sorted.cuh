@@ -69,7 +69,7 @@ struct VoxTile {
 };
 
 // One sample at its sorted position (32 bytes: one sector).
-struct __align__(16) SRec {
+struct __align__(32) SRec {
   float a;        // attention weight
   float f[3];     // fractional offsets inside the cell
   uint32_t row;   // (b, q, h) row of grad_out
@@ -190,6 +190,21 @@ template <int VB>
 __device__ __forceinline__ void stage_chunk(void* dst, const void* src) {
   if constexpr (VB >= 4) cp_async<VB>(dst, src);
   else st_chunk<VB>(dst, ld_chunk<VB>(src));
+}
+
+// A whole 32-byte record as one 256-bit access (ld/st .v8.b32, sm_100):
+// one memory request per record instead of two.
+__device__ __forceinline__ void st_rec(SRec* dst, const SRec& r) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(&r);
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(w[0]),
+               "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+__device__ __forceinline__ void ld_rec(const SRec* src, uint4& r0, uint4& r1) {
+  asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r0.x), "=r"(r0.y), "=r"(r0.z), "=r"(r0.w), "=r"(r1.x), "=r"(r1.y),
+                 "=r"(r1.z), "=r"(r1.w)
+               : "l"(src));
 }
 
 // ------------------------------------------------------------------ dots
@@ -528,9 +543,8 @@ __global__ void __launch_bounds__(kThreads, 4)
     mine.a = 0.0f;
     uint32_t my_row = 0, my_idx = kNoSample;
     if (q0 + j < q_end) {
-      const SRec* rp = recs + q0 + j;
-      const uint4 r0 = __ldg(reinterpret_cast<const uint4*>(rp));
-      const uint4 r1 = __ldg(reinterpret_cast<const uint4*>(rp) + 1);
+      uint4 r0, r1;
+      ld_rec(recs + q0 + j, r0, r1);
       // r0 = (a, f0, f1, f2), r1 = (row, key, idx, pass)
       const uint32_t c = static_cast<uint32_t>(static_cast<int32_t>(r1.y) - kb);
       Point<NDIM> pt;
@@ -640,10 +654,7 @@ __global__ void __launch_bounds__(kThreads) msda_place_kernel(const Problem p, c
 #pragma unroll
   for (int ax = 0; ax < NDIM; ++ax) rec.pass |= pt.pass[ax] ? (1u << ax) : 0u;
   const int32_t at = __ldg(sp.cnt + rec.key) + sp.pos[s];
-  uint4* dst = reinterpret_cast<uint4*>(sp.srec + at);
-  const uint4* src = reinterpret_cast<const uint4*>(&rec);
-  dst[0] = src[0];
-  dst[1] = src[1];
+  st_rec(sp.srec + at, rec);
 }
 
 // ------------------------------------------------------------------ scan
