@@ -51,6 +51,9 @@ WORKLOADS = {
     # BASELINE configs[1].
     "2d_enc_bf16": dict(ndim=2, B=4, Q=19947, H=8, C=32, P=4, dtype=torch.bfloat16, shapes=SHAPES_2D),
     "2d_enc_fp32": dict(ndim=2, B=4, Q=19947, H=8, C=32, P=4, dtype=torch.float32, shapes=SHAPES_2D),
+    # the reference's own CPU-runnable case.
+    "2d_cfg0_fp32": dict(ndim=2, B=1, Q=300, H=8, C=32, P=4, dtype=torch.float32,
+                         shapes=[(32, 32), (16, 16), (8, 8), (4, 4)]),
     # BASELINE configs[2] (inference: forward only).
     "2d_dec_bf16": dict(ndim=2, B=8, Q=900, H=8, C=32, P=4, dtype=torch.bfloat16, shapes=SHAPES_2D,
                         fwd_only=True),
@@ -229,6 +232,9 @@ def run_ours(args, wl, rank, world, local_rank):
     else:
         global_b = wl["B"] * world
     value, shapes, loc, attn, go = make_inputs(wl, dev, seed=1234 + rank)
+    if args.value_layout == "bhkc":
+        # the same values stored head-major, handed over as the (B, K, H, C) view
+        value = value.permute(0, 2, 1, 3).contiguous().permute(0, 2, 1, 3)
     v = value.requires_grad_(True)
     lo = loc.requires_grad_(True)
     a = attn.requires_grad_(True)
@@ -287,7 +293,7 @@ def run_ours(args, wl, rank, world, local_rank):
         # The backward entry exactly as the autograd path calls it: zero-fill
         # of the value-gradient targets, the scatter kernel and (16-bit
         # values with an fp32 accumulator) the cast kernel.
-        ws_bytes = lib.msda_bwd_workspace_bytes(wl["ndim"], _core._DTYPE_CODE[wl["dtype"]], B, K,
+        ws_bytes = lib.msda_bwd_workspace_bytes(wl["ndim"], _core.value_code(value), B, K,
                                                 H, C, shp.data_ptr(), int(on_dev), L, Q, P)
         ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
         gv = torch.empty_like(value)
@@ -346,6 +352,7 @@ def run_ours(args, wl, rank, world, local_rank):
             "global_batch": global_b, "num_queries": Q, "num_heads": H, "channels": C,
             "num_levels": L, "num_points": P, "spatial_shapes": wl["shapes"],
             "parallelism": f"batch-sharded dp{world} (no collective)",
+            "value_layout": "(B, K, H, C)" if args.value_layout == "bkhc" else "(B, H, K, C)",
             "l2": f"inputs larger than L2 (value {value.numel() * value.element_size() / 1e9:.2f} GB"
                   f" > {L2_BYTES / 1e6:.0f} MB); no flush",
         },
@@ -857,6 +864,9 @@ def main():
     ap.add_argument("--workload", default="3d_xl_bf16", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-triton"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--value-layout", default="bkhc", choices=["bkhc", "bhkc"],
+                    help="device-resident value of the timed step: the reference's (B, K, H, C) "
+                         "or head-major (B, H, K, C) storage (end-to-end leg: always bkhc)")
     ap.add_argument("--shard", default="batch", choices=["batch", "query"],
                     help="batch: one instance of the workload per GPU (weak scaling); query: "
                          "one instance split by queries across the GPUs (strong scaling)")

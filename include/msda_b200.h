@@ -73,6 +73,16 @@ typedef enum msda_dtype {
   MSDA_BFLOAT16 = 2
 } msda_dtype;
 
+/* Flag ORed into any `value_dtype` argument: value (and grad_value) are laid
+ * out head-major, (B, H, K, C) -- each head's keys contiguous -- instead of
+ * the reference's (B, K, H, C).  This is the layout a value projection can
+ * write per head (pytorch/msda_3d.py:302-305 views its output as
+ * (B, K, H, C)); one head's slice of a level is then one contiguous range,
+ * which stays in L2 while the kernels walk that head.  Every other argument
+ * keeps its meaning; workspace sizes do not change.  No counterpart in the
+ * reference. */
+#define MSDA_VALUE_HEAD_MAJOR 0x100
+
 typedef enum msda_status {
   MSDA_SUCCESS = 0,
   MSDA_ERROR_INVALID_ARGUMENT = 1,   /* null pointer, negative size, bad clamp_eps */

@@ -126,6 +126,28 @@ def sampling_pair(
     return loc.contiguous(), attn.contiguous()
 
 
+def is_head_major(value: torch.Tensor) -> bool:
+    """value (B, K, H, C) as a view of a contiguous (B, H, K, C) tensor: each
+    head's keys contiguous (what `prepare_value` passes through uncopied)."""
+    return (value.dim() == 4 and not value.is_contiguous()
+            and value.permute(0, 2, 1, 3).is_contiguous())
+
+
+def prepare_value(value: torch.Tensor) -> torch.Tensor:
+    """value in a layout the kernels read in place: the reference's dense
+    (B, K, H, C), or the head-major view of a dense (B, H, K, C) tensor.
+    Any other strides are copied to (B, K, H, C)."""
+    if value.is_contiguous() or is_head_major(value):
+        return value
+    return value.contiguous()
+
+
+def value_code(value: torch.Tensor) -> int:
+    """The C ABI's value dtype argument: dtype code, plus the head-major flag."""
+    code = _DTYPE_CODE[value.dtype]
+    return code | _lib.VALUE_HEAD_MAJOR if is_head_major(value) else code
+
+
 def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
@@ -134,7 +156,7 @@ def _common_args(value, shapes, on_dev, loc, attn):
     B, K, H, C = value.shape
     _, Q, _, L, P, _ = loc.shape
     return (
-        value.data_ptr(), _DTYPE_CODE[value.dtype], B, K, H, C,
+        value.data_ptr(), value_code(value), B, K, H, C,
         shapes.data_ptr(), int(on_dev), L,
         loc.data_ptr(), attn.data_ptr(), _DTYPE_CODE[loc.dtype], Q, P,
     )
@@ -188,7 +210,7 @@ def backward(
     grad_attn = torch.empty_like(attn)
     lib = _lib.lib()
     Q, L, P = loc.shape[1], loc.shape[3], loc.shape[4]
-    ws_bytes = lib.msda_bwd_workspace_bytes(ndim, _DTYPE_CODE[value.dtype], B, K, H, C,
+    ws_bytes = lib.msda_bwd_workspace_bytes(ndim, value_code(value), B, K, H, C,
                                             shapes.data_ptr(), int(on_dev), L, Q, P)
     ws = torch.empty((ws_bytes,), device=value.device, dtype=torch.uint8) if ws_bytes else None
     fn = lib.msda2d_bwd if ndim == 2 else lib.msda3d_bwd
@@ -221,6 +243,8 @@ def backward_accumulate(
     value gradients are summed before one final cast (query sharding)."""
     if grad_value_accum.dtype != torch.float32 or grad_value_accum.shape != value.shape:
         raise ValueError("grad_value_accum must be an fp32 tensor shaped like value")
+    if grad_value_accum.stride() != value.stride():
+        raise ValueError("grad_value_accum must have value's layout")
     go = grad_output
     if go.dtype != value.dtype:
         go = go.to(value.dtype)
@@ -258,7 +282,7 @@ def fwd_entry(ndim, value, value_spatial_shapes, sampling_locations, attention_w
     validate_inputs(ndim, value, value_spatial_shapes, sampling_locations, attention_weights)
     shapes, on_dev = prepare_spatial(value_spatial_shapes)
     loc, attn = sampling_pair(value, sampling_locations, attention_weights)
-    return forward(ndim, value.contiguous(), shapes, on_dev, loc, attn, clamp_grid, clamp_eps)
+    return forward(ndim, prepare_value(value), shapes, on_dev, loc, attn, clamp_grid, clamp_eps)
 
 
 def fn_forward(ndim, ctx, value, value_spatial_shapes, sampling_locations, attention_weights,
@@ -267,7 +291,7 @@ def fn_forward(ndim, ctx, value, value_spatial_shapes, sampling_locations, atten
     validate_inputs(ndim, value, value_spatial_shapes, sampling_locations, attention_weights)
     shapes, on_dev = prepare_spatial(value_spatial_shapes)
     loc, attn = sampling_pair(value, sampling_locations, attention_weights)
-    value_c = value.contiguous()
+    value_c = prepare_value(value)
     out = forward(ndim, value_c, shapes, on_dev, loc, attn, clamp_grid, clamp_eps)
     ctx.save_for_backward(value_c, loc, attn, shapes)
     ctx.on_dev = on_dev

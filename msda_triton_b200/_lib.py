@@ -31,6 +31,8 @@ ERROR_CUDA = 9
 FLOAT32 = 0
 FLOAT16 = 1
 BFLOAT16 = 2
+# ORed into a value dtype code: value / grad_value laid out (B, H, K, C)
+VALUE_HEAD_MAJOR = 0x100
 
 MAX_LEVELS = 16
 ABI_VERSION = 3

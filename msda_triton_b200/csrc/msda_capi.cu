@@ -102,7 +102,16 @@ struct Args {
   // keep the backward on the gather/scatter plan (the static-scratch entry:
   // its workspace bound was set for that plan)
   bool scatter_only = false;
+  // value / grad_value laid out (B, H, K, C): MSDA_VALUE_HEAD_MAJOR was set in
+  // the value dtype argument (with_layout strips it from vdt)
+  bool hm = false;
 };
+
+Args with_layout(Args a) {
+  a.hm = (a.vdt & MSDA_VALUE_HEAD_MAJOR) != 0;
+  a.vdt &= ~MSDA_VALUE_HEAD_MAJOR;
+  return a;
+}
 
 // Validate arguments, fill the Problem (except the launch shape) and pick
 // the launch shape.  `bufs` are the row-strided buffers whose alignment bounds
@@ -145,6 +154,7 @@ int prepare(const Args& a, const void* const* bufs, int nbufs, Problem& p, Launc
   p.B = a.B; p.K = a.K; p.H = a.H; p.C = a.C; p.Q = a.Q; p.L = a.L; p.P = a.P;
   p.acc_keys = a.K;  // accumulator in value's key layout unless a plan compacts it
   p.clamp = a.clamp ? 1 : 0;
+  p.head_major = a.hm ? 1 : 0;
   p.lo = static_cast<float>(-1.0 + a.eps);
   p.hi = static_cast<float>(1.0 - a.eps);
   p.shapes_dev = nullptr;
@@ -246,6 +256,18 @@ int prepare(const Args& a, const void* const* bufs, int nbufs, Problem& p, Launc
 
 int cuda_fail(cudaError_t err, const char* what) {
   return fail(MSDA_ERROR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+}
+
+// Zero keys [start, start + nkeys) of every (batch entry[, head]) of a buffer
+// in value's layout (elem_bytes per element, K keys per batch entry).
+cudaError_t zero_key_range(const Args& a, void* base, int64_t start, int64_t nkeys, int64_t nb,
+                           int64_t elem_bytes, cudaStream_t st) {
+  if (nkeys <= 0 || nb <= 0) return cudaSuccess;
+  const int64_t run = (a.hm ? a.C : a.H * a.C) * elem_bytes;  // bytes per key of one span
+  const int64_t spans = a.hm ? nb * a.H : nb;
+  return cudaMemset2DAsync(static_cast<char*>(base) + start * run,
+                           static_cast<size_t>(a.K * run), 0, static_cast<size_t>(nkeys * run),
+                           static_cast<size_t>(spans), st);
 }
 
 template <bool F>
@@ -413,7 +435,7 @@ struct BwdPlan {
   int64_t chunk_b = 0;    // batch entries per chunk
   int64_t smp_per_b = 0;  // samples per batch entry
   int64_t keys_per_b = 0; // bucket keys per batch entry
-  size_t soff[5] = {};    // bucket counts, bsum, ranks, srec, acc
+  size_t soff[6] = {};    // bucket counts, bsum, ranks, srec, acc, sorted-dots stage
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
@@ -592,12 +614,13 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   pl.direct16 = 0;
   const int64_t nblk = (int64_t{sp.nkeys} + kScanTile - 1) / kScanTile;
   const int64_t n = sp.n;
-  const size_t sizes[5] = {
+  const size_t sizes[6] = {
       static_cast<size_t>(sp.nkeys + 1) * 4, static_cast<size_t>(nblk + 1) * 4,
       static_cast<size_t>(n) * 4, static_cast<size_t>(n) * sizeof(SRec),
-      f32 ? 0 : static_cast<size_t>(nb * acc_keys * a.H * a.C) * sizeof(float)};
+      f32 ? 0 : static_cast<size_t>(nb * acc_keys * a.H * a.C) * sizeof(float),
+      static_cast<size_t>(nb * a.Q * a.H * sp.nsl * a.P) * 16};
   size_t off = 0;
-  for (int i = 0; i < 5; ++i) {
+  for (int i = 0; i < 6; ++i) {
     pl.soff[i] = off;
     off += align256(sizes[i]);
   }
@@ -675,6 +698,7 @@ int run_bwd_sorted(const Args& a, Problem p, LaunchShape ls, const BwdPlan& pl, 
   sp.bsum = reinterpret_cast<int32_t*>(w + pl.soff[1]);
   sp.pos = reinterpret_cast<int32_t*>(w + pl.soff[2]);
   sp.srec = reinterpret_cast<SRec*>(w + pl.soff[3]);
+  sp.sd_stage = reinterpret_cast<float4*>(w + pl.soff[5]);
   float* acc = f32 ? nullptr : reinterpret_cast<float*>(w + pl.soff[4]);
   p.acc_compact = pl.compact ? 1 : 0;
   p.acc_keys = pl.acc_keys;
@@ -706,9 +730,7 @@ int run_bwd_sorted(const Args& a, Problem p, LaunchShape ls, const BwdPlan& pl, 
       const int64_t nvox = int64_t{p.lv.size[l][0]} * p.lv.size[l][1] * p.lv.size[l][2];
       dense_keys += nvox;
       if (f32 && nvox > 0) {
-        err = cudaMemset2DAsync(gv_c + p.lv.start[l] * row_bytes,
-                                static_cast<size_t>(a.K * row_bytes), 0,
-                                static_cast<size_t>(nvox * row_bytes), static_cast<size_t>(nb), st);
+        err = zero_key_range(a, gv_c, p.lv.start[l], nvox, nb, e, st);
         if (err != cudaSuccess) return cuda_fail(err, "zeroing grad_value rows");
       }
     }
@@ -781,9 +803,7 @@ int run_bwd(const Args& a, const void* go, void* gv, void* gl, void* ga, void* w
     if (!((pl.direct16 >> l) & 1)) continue;
     const int64_t nvox = int64_t{p.lv.size[l][0]} * p.lv.size[l][1] * p.lv.size[l][2];
     if (nvox == 0) continue;
-    err = cudaMemset2DAsync(static_cast<char*>(gv) + p.lv.start[l] * row_bytes,
-                            static_cast<size_t>(a.K * row_bytes), 0,
-                            static_cast<size_t>(nvox * row_bytes), static_cast<size_t>(a.B), st);
+    err = zero_key_range(a, gv, p.lv.start[l], nvox, a.B, dtype_bytes(a.vdt), st);
     if (err != cudaSuccess) return cuda_fail(err, "zeroing grad_value rows");
   }
   bwd_gather_shape(a, p, ls);
@@ -825,9 +845,10 @@ int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
 using msda::Args;
 
 #define MSDA_ARGS(ND)                                                                      \
-  Args a{ND,    value, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes, \
-         spatial_shapes_on_device, num_levels, sampling_locations, attention_weights,      \
-         sampling_dtype, num_queries, num_points, clamp_grid, clamp_eps}
+  Args a = msda::with_layout(Args{                                                         \
+      ND, value, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,        \
+      spatial_shapes_on_device, num_levels, sampling_locations, attention_weights,         \
+      sampling_dtype, num_queries, num_points, clamp_grid, clamp_eps})
 
 extern "C" {
 
@@ -904,10 +925,10 @@ int msda3d_bwd_accumulate(const void* value, int value_dtype, int64_t batch, int
 }
 
 #define MSDA_FUSED_ARGS(ND)                                                                \
-  Args a{ND,          value,           value_dtype,     batch,        num_keys,               \
-         num_heads,   channels,        spatial_shapes,  spatial_shapes_on_device, num_levels, \
-         sampling_offsets, attention_logits, sampling_dtype, num_queries, num_points,          \
-         clamp_grid,  clamp_eps,       reference_points, 1}
+  Args a = msda::with_layout(Args{                                                         \
+      ND, value, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,        \
+      spatial_shapes_on_device, num_levels, sampling_offsets, attention_logits,            \
+      sampling_dtype, num_queries, num_points, clamp_grid, clamp_eps, reference_points, 1})
 
 int msda2d_fused_fwd(const void* value, int value_dtype, int64_t batch, int64_t num_keys,
                      int64_t num_heads, int64_t channels, const int32_t* spatial_shapes,
@@ -979,9 +1000,10 @@ static size_t workspace_bytes(int ndim, int value_dtype, int64_t batch, int64_t 
                               bool scatter_only = false) {
   // Plan with 256-byte aligned stand-in pointers (never dereferenced).
   void* fake = reinterpret_cast<void*>(uintptr_t{256});
-  Args a{ndim, fake, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,
-         spatial_shapes_on_device, num_levels, fake, fake, value_dtype, num_queries, num_points,
-         1, 1e-4, static_cast<const float*>(fake), fused, scatter_only};
+  const Args a = with_layout(Args{
+      ndim, fake, value_dtype, batch, num_keys, num_heads, channels, spatial_shapes,
+      spatial_shapes_on_device, num_levels, fake, fake, value_dtype & ~MSDA_VALUE_HEAD_MAJOR,
+      num_queries, num_points, 1, 1e-4, static_cast<const float*>(fake), fused, scatter_only});
   msda::Problem p;
   msda::LaunchShape ls;
   const void* bufs[2] = {fake, fake};

@@ -32,7 +32,7 @@ struct LevelTable {
 
 // Everything a launch needs, passed by value as one kernel parameter.
 struct Problem {
-  const void* value;          // (B, K, H, C) of T
+  const void* value;          // (B, K, H, C) of T, or (B, H, K, C) with head_major
   const void* loc;            // (B, Q, H, L, P, d) of TS
   const void* attn;           // (B, Q, H, L, P) of TS
   const int32_t* shapes_dev;  // (L, d) int32 on device, or nullptr
@@ -41,6 +41,7 @@ struct Problem {
   int32_t log2g;      // lanes per row = 1 << log2g
   int32_t hg;         // heads per scheduling group (divides H)
   int32_t clamp;      // clamp_grid
+  int32_t head_major; // value / grad_value / fp32 accumulators laid out (B, H, K, C)
   float lo, hi;       // clamp window in grid space
   LevelTable lv;      // host-resolved table (used when shapes_dev == nullptr)
   // Backward value-gradient targets of the gather/scatter kernel (16-bit
@@ -67,6 +68,21 @@ struct Problem {
   // otherwise; nullptr in the normal build).
   unsigned int* check_flag;
 };
+
+// ---------------------------------------------------------------- layout
+// Element offsets into value, grad_value and the fp32 value-gradient
+// accumulators.  Channel-last, the reference's tensor contract: (B, K, H, C),
+// the H heads of a key side by side.  Head-major: (B, H, K, C), each head's
+// keys contiguous (what a value projection can write directly,
+// pytorch/msda_3d.py:302-305 reshapes its output to (B, K, H, C)).  An
+// accumulator has the layout of value with `keys` keys per batch entry.
+__host__ __device__ __forceinline__ int64_t key_stride(const Problem& p) {
+  return p.head_major ? p.C : p.H * p.C;
+}
+__host__ __device__ __forceinline__ int64_t bh_base(const Problem& p, int64_t b, int64_t h,
+                                                    int64_t keys) {
+  return p.head_major ? (b * p.H + h) * keys * p.C : (b * keys * p.H + h) * p.C;
+}
 
 // ---------------------------------------------------------------- types
 template <typename T> struct Elem;

@@ -364,9 +364,9 @@ __device__ __forceinline__ void msda_fwd_body(const Problem p, T* __restrict__ o
 
   const RowCoord rc = decode_row(static_cast<uint32_t>(r), p);
   const int64_t row = (rc.b * p.Q + rc.q) * p.H + rc.h;
-  const int64_t key_bytes = p.H * p.C * static_cast<int64_t>(sizeof(T));
+  const int64_t key_bytes = key_stride(p) * static_cast<int64_t>(sizeof(T));
   const char* vbase = static_cast<const char*>(p.value) +
-                      (rc.b * p.K * p.H + rc.h) * p.C * static_cast<int64_t>(sizeof(T));
+                      bh_base(p, rc.b, rc.h, p.K) * static_cast<int64_t>(sizeof(T));
   const int LP = static_cast<int>(p.L * p.P);
   const TS* lrow = static_cast<const TS*>(p.loc) + row * LP * NDIM;
   const TS* arow = static_cast<const TS*>(p.attn) + row * LP;
@@ -571,10 +571,9 @@ __device__ __forceinline__ void msda_bwd_body(const Problem p, const T* __restri
   RowCoord rc{0, 0, 0};
   if (active) rc = decode_row(static_cast<uint32_t>(r), p);
   const int64_t row = (rc.b * p.Q + rc.q) * p.H + rc.h;
-  const int64_t HC = p.H * p.C;
-  const int64_t key_bytes = HC * static_cast<int64_t>(sizeof(T));
+  const int64_t key_bytes = key_stride(p) * static_cast<int64_t>(sizeof(T));
   const char* vbase = static_cast<const char*>(p.value) +
-                      (rc.b * p.K * p.H + rc.h) * p.C * static_cast<int64_t>(sizeof(T));
+                      bh_base(p, rc.b, rc.h, p.K) * static_cast<int64_t>(sizeof(T));
   const int LP = static_cast<int>(p.L * p.P);
   const TS* lrow = static_cast<const TS*>(p.loc) + row * LP * NDIM;
   const TS* arow = static_cast<const TS*>(p.attn) + row * LP;
@@ -610,7 +609,7 @@ __device__ __forceinline__ void msda_bwd_body(const Problem p, const T* __restri
   // The same key's fp32 accumulator row is at vo * 4 / sizeof(T) from the
   // level's accumulator base (keys shifted to the compacted layout), and its
   // grad_value row (direct levels) at the same byte offset vo.
-  const int64_t vrow = (rc.b * p.K * p.H + rc.h) * p.C;
+  const int64_t vrow = bh_base(p, rc.b, rc.h, p.K);
   char* g16lane = static_cast<char*>(p.grad_value16) + vrow * static_cast<int64_t>(sizeof(T)) +
                   j * VB;
   for (int l = 0; l < p.L; ++l) {
@@ -626,7 +625,7 @@ __device__ __forceinline__ void msda_bwd_body(const Problem p, const T* __restri
     }
     const int64_t kshift = p.acc_compact ? p.acc_start[l] - g.start : 0;
     char* acc_lane = reinterpret_cast<char*>(
-        gacc + ((rc.b * p.acc_keys + kshift) * p.H + rc.h) * p.C + j * EPV);
+        gacc + bh_base(p, rc.b, rc.h, p.acc_keys) + kshift * key_stride(p) + j * EPV);
     for (int pp = 0; pp < P; ++pp) {
       const int s = l * P + pp;
       Point<NDIM> pt;
@@ -795,30 +794,40 @@ __global__ void __launch_bounds__(kThreads)
 
 // Compacted fp32 accumulator (the keys of the levels not in p.direct16,
 // p.acc_keys per batch entry) -> their grad_value rows in the input dtype.
-// One warp per key row: the row's batch entry, level and destination key are
-// resolved once per row, then the lanes stream its H*C elements.
+// One lane group per row (a key's H*C elements, or a (head, key)'s C
+// elements head-major): the row's batch entry, level and destination key are
+// resolved once per row, then the lanes stream its elements.
 // V = 4: float4 in, one 8-byte store out (16-bit T, H*C % 4 == 0, grad_value
 // 8-byte aligned); V = 1 otherwise.
 template <typename T, int V>
 __global__ void __launch_bounds__(kThreads)
     msda_compact_cast_kernel(const Problem p, const float* __restrict__ acc, T* __restrict__ gv) {
-  const int64_t row = p.H * p.C;  // elements per key
+  // A row: one key's H*C elements (channel-last) or one (head, key)'s C
+  // elements (head-major); rows run batch entry, [head,] key.
+  // Lane groups of lpr lanes (the power of two covering a row's vectors, at
+  // most 32) take one row each.
+  const int64_t row = key_stride(p);
   const int64_t rv = row / V;
-  const int64_t nrows = p.B * p.acc_keys;
-  const int lane = static_cast<int>(threadIdx.x & 31u);
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
-  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / 32; r < nrows;
-       r += nwarps) {
-    const int64_t b = r / p.acc_keys;
-    const int64_t ak = r - b * p.acc_keys;
+  const int64_t rows_b = p.head_major ? p.H * p.acc_keys : p.acc_keys;  // rows per batch entry
+  const int64_t nrows = p.B * rows_b;
+  int lpr = 1;
+  while (lpr < 32 && lpr < rv) lpr <<= 1;
+  const int lane = static_cast<int>(threadIdx.x) & (lpr - 1);
+  const int64_t ngroups = static_cast<int64_t>(gridDim.x) * (kThreads / lpr);
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / lpr; r < nrows;
+       r += ngroups) {
+    const int64_t b = r / rows_b;
+    const int64_t rr = r - b * rows_b;
+    const int64_t h = p.head_major ? rr / p.acc_keys : 0;
+    const int64_t ak = rr - h * p.acc_keys;
     int64_t shift = 0;  // key - accumulator key of the level holding ak
 #pragma unroll
     for (int k = 0; k < kMaxLevels; ++k)
       if (k < p.L && !((p.direct16 >> k) & 1) && ak >= p.acc_start[k])
         shift = static_cast<int64_t>(p.lv.start[k]) - p.acc_start[k];
     const float* src = acc + r * row;
-    T* dst = gv + (b * p.K + ak + shift) * row;
-    for (int64_t e = lane; e < rv; e += 32) {
+    T* dst = gv + bh_base(p, b, h, p.K) + (ak + shift) * row;
+    for (int64_t e = lane; e < rv; e += lpr) {
       if constexpr (V == 4) {
         const float4 v = *reinterpret_cast<const float4*>(src + e * 4);
         struct alignas(8) Quad { T h[4]; } o;

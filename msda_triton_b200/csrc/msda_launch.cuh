@@ -133,11 +133,11 @@ cudaError_t launch_cast(const float* src, void* dst, int64_t n, cudaStream_t st)
 // Compacted accumulator -> grad_value rows of the non-direct levels (16-bit T).
 template <typename T>
 cudaError_t launch_compact_cast(const Problem& p, const float* acc, void* gv, cudaStream_t st) {
-  const int64_t row = p.H * p.C;
+  const int64_t row = key_stride(p);
   const bool vec = row % 4 == 0 && reinterpret_cast<uintptr_t>(gv) % 8 == 0;
-  const int64_t nrows = p.B * p.acc_keys;  // one warp per key row
+  const int64_t nrows = p.B * p.acc_keys * (p.head_major ? p.H : 1);
   if (nrows <= 0 || row <= 0) return cudaSuccess;
-  int64_t blocks = (nrows + kThreads / 32 - 1) / (kThreads / 32);
+  int64_t blocks = (nrows + kThreads / 32 - 1) / (kThreads / 32);  // a grid-stride loop covers the rest
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (vec)
     msda_compact_cast_kernel<T, 4><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(

@@ -29,6 +29,7 @@
 //   msda_scan_*            counts -> exclusive bucket starts
 //   msda_place_kernel      record (a, fractions, grad_out row, key) at start[key] + rank
 //   msda_sdots_kernel      grad_attn, grad_loc of the large sparse levels, in sorted order
+//   msda_sdots_finish_kernel  ... staged, then written out in query order
 //   msda_dense_kernel      dense-level value gradient, per cell segment
 //   msda_voxel_kernel      sparse-level value gradient, gathered per value row
 //
@@ -114,6 +115,7 @@ struct SortPlan {
   int32_t* bsum;                   // scan block sums
   int32_t* pos;                    // n: each sample's rank inside its bucket
   SRec* srec;                      // n: the samples in sorted order
+  float4* sd_stage;                // B*Q*H*nsl*P: msda_sdots_kernel's results in query order
 };
 
 // Bucket key of a resolved sample: the (b, h) block, the level's key range,
@@ -368,6 +370,45 @@ __device__ __forceinline__ void store_dot_results(const Problem& p, const float*
   }
 }
 
+// msda_sdots_kernel's variant of store_dot_results: the results land in the
+// (row, sorted-dots level, point) slot of sp.sd_stage as fp32 (grad_attn,
+// grad_loc per axis), which msda_sdots_finish_kernel then writes out in query
+// order.  Scattered 2-byte stores straight into grad_attn / grad_loc would
+// each touch a line the query-order pass filled long before: a DRAM
+// read-modify-write per store.
+template <int NDIM>
+__device__ __forceinline__ void stage_dot_results(const Problem& p, const SortPlan& sp,
+                                                  const float* v, const DotLanes& dl,
+                                                  const uint32_t* sidx, const float* sa,
+                                                  const int32_t* sinfo, int li) {
+  constexpr int NV = kDotBatch * 4;
+#pragma unroll
+  for (int t = 0; t < NV; ++t) {
+    if (t < dl.nkeep) {
+      const int idx = dl.vbase + t;
+      const int slot = idx >> 2, comp = idx & 3;
+      float a = 0.0f;
+      uint32_t si = kNoSample;
+      int32_t info = 0;
+#pragma unroll
+      for (int i = 0; i < kDotBatch; ++i)
+        if (i == slot) { a = sa[i]; si = sidx[i]; info = sinfo[i]; }
+      if (si == kNoSample || comp > NDIM) continue;
+      const int ls = info & 0xff;
+      float val = v[t];
+      if (comp > 0) {
+        const int ax = comp - 1;
+        val = ((info >> (8 + ax)) & 1) ? a * val * static_cast<float>(p.lv.size[ls][ax]) : 0.0f;
+      }
+      const uint32_t row = fdiv(si, sp.div_lp);
+      const uint32_t pp = si - row * static_cast<uint32_t>(p.L * p.P) -
+                          static_cast<uint32_t>(ls) * static_cast<uint32_t>(p.P);
+      const int64_t e = (static_cast<int64_t>(row) * sp.nsl + li) * p.P + pp;
+      reinterpret_cast<float*>(sp.sd_stage + e)[comp] = val;
+    }
+  }
+}
+
 template <typename T, typename TS, int NDIM, int VB, int VPL>
 __global__ void __launch_bounds__(kThreads, 4)
     msda_dots_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
@@ -386,9 +427,9 @@ __global__ void __launch_bounds__(kThreads, 4)
   if (!active) r = 0;
   const RowCoord rc = decode_row(static_cast<uint32_t>(r), p);
   const int64_t row = (rc.b * p.Q + rc.q) * p.H + rc.h;
-  const int64_t key_bytes = p.H * p.C * static_cast<int64_t>(sizeof(T));
+  const int64_t key_bytes = key_stride(p) * static_cast<int64_t>(sizeof(T));
   const char* vbase = static_cast<const char*>(p.value) +
-                      (rc.b * p.K * p.H + rc.h) * p.C * static_cast<int64_t>(sizeof(T));
+                      bh_base(p, rc.b, rc.h, p.K) * static_cast<int64_t>(sizeof(T));
   const int LP = static_cast<int>(p.L * p.P);
   const TS* lrow = static_cast<const TS*>(p.loc) + row * LP * NDIM;
   const TS* arow = static_cast<const TS*>(p.attn) + row * LP;
@@ -498,12 +539,23 @@ __global__ void __launch_bounds__(kThreads, 4)
   constexpr int EPV = CK::EPV;
   constexpr int NC = 1 << NDIM;
   constexpr int NV = kDotBatch * 4;
-  // CTA -> (b, level, stretch, h), h fastest
+  // CTA -> (b, level, stretch, h) with h fastest: the heads' rows of a key
+  // share value lines.  Head-major value: (b, level, h, stretch), one head's
+  // slice of the level at a time.
   uint32_t u = blockIdx.x;
-  const int32_t h = static_cast<int32_t>(u % static_cast<uint32_t>(p.H));
-  u /= static_cast<uint32_t>(p.H);
-  const int32_t k = static_cast<int32_t>(u % static_cast<uint32_t>(sp.sd_chunks));
-  u /= static_cast<uint32_t>(sp.sd_chunks);
+  const uint32_t H = static_cast<uint32_t>(p.H), nch = static_cast<uint32_t>(sp.sd_chunks);
+  int32_t h, k;
+  if (p.head_major) {
+    k = static_cast<int32_t>(u % nch);
+    u /= nch;
+    h = static_cast<int32_t>(u % H);
+    u /= H;
+  } else {
+    h = static_cast<int32_t>(u % H);
+    u /= H;
+    k = static_cast<int32_t>(u % nch);
+    u /= nch;
+  }
   const int32_t li = static_cast<int32_t>(u % static_cast<uint32_t>(sp.nsl));
   const int64_t b = u / static_cast<uint32_t>(sp.nsl);
   const int l = sp.sl_level[li];
@@ -523,8 +575,8 @@ __global__ void __launch_bounds__(kThreads, 4)
   for (int v = 0; v < VPL; ++v) has[v] = j + v * G < p.nv;
 
   const int64_t e = static_cast<int64_t>(sizeof(T));
-  const int64_t key_bytes = p.H * p.C * e;
-  const char* vbase = static_cast<const char*>(p.value) + (b * p.K * p.H + h) * p.C * e;
+  const int64_t key_bytes = key_stride(p) * e;
+  const char* vbase = static_cast<const char*>(p.value) + bh_base(p, b, h, p.K) * e;
   const LevelGeom g = level_geom_tab(p, l, key_bytes);
   const int32_t kb = static_cast<int32_t>(bh) * sp.seg_keys + sp.lvl_base[l];
   const uint32_t ncell = static_cast<uint32_t>(sp.cells[l][0]) *
@@ -620,10 +672,30 @@ __global__ void __launch_bounds__(kThreads, 4)
         }
       }
       dot_reduce(v, G, j, dl);
-      if (dl.writer)
-        store_dot_results<TS, NDIM>(p, v, dl, sidx, sa, sinfo, grad_loc, grad_attn);
+      if (dl.writer) stage_dot_results<NDIM>(p, sp, v, dl, sidx, sa, sinfo, li);
     }
   }
+}
+
+// The staged sorted-order results written to grad_attn / grad_loc, one
+// thread per (row, sorted-dots level, point), in query order.
+template <typename TS, int NDIM>
+__global__ void __launch_bounds__(kThreads)
+    msda_sdots_finish_kernel(const Problem p, const SortPlan sp, TS* __restrict__ grad_loc,
+                             TS* __restrict__ grad_attn) {
+  const int64_t e = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int64_t total = p.B * p.Q * p.H * sp.nsl * p.P;
+  if (e >= total) return;
+  const int64_t t = e / p.P;
+  const int64_t pp = e - t * p.P;
+  const int64_t row = t / sp.nsl;
+  const int li = static_cast<int>(t - row * sp.nsl);
+  const int64_t si = row * p.L * p.P + static_cast<int64_t>(sp.sl_level[li]) * p.P + pp;
+  const float4 r = sp.sd_stage[e];
+  grad_attn[si] = Elem<TS>::from_f(r.x);
+  grad_loc[si * NDIM] = Elem<TS>::from_f(r.y);
+  grad_loc[si * NDIM + 1] = Elem<TS>::from_f(r.z);
+  if constexpr (NDIM == 3) grad_loc[si * NDIM + 2] = Elem<TS>::from_f(r.w);
 }
 
 // ------------------------------------------------------------------ place
@@ -840,7 +912,7 @@ __global__ void __launch_bounds__(kThreads)
   const int32_t b = static_cast<int32_t>(bh / static_cast<uint32_t>(p.H));
   const int32_t h = static_cast<int32_t>(bh - static_cast<uint32_t>(b) * static_cast<uint32_t>(p.H));
   const int64_t kshift = p.acc_compact ? p.acc_start[l] : p.lv.start[l];
-  float* gbase = gacc + ((static_cast<int64_t>(b) * p.acc_keys + kshift) * p.H + h) * p.C + j * EPV;
+  float* gbase = gacc + bh_base(p, b, h, p.acc_keys) + kshift * key_stride(p) + j * EPV;
   bool has[VPL];
 #pragma unroll
   for (int v = 0; v < VPL; ++v) has[v] = (j + v * G < nv);
@@ -899,7 +971,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int cc = 0; cc < NC; ++cc) {
       if (!((vbits >> cc) & 1u)) continue;
       const int32_t k = k0 + (cc & 1) + ((cc >> 1) & 1) * sz0 + ((cc >> 2) & 1) * sz0 * sz1;
-      float* dst = gbase + static_cast<int64_t>(k) * p.H * p.C;
+      float* dst = gbase + static_cast<int64_t>(k) * key_stride(p);
 #pragma unroll
       for (int v = 0; v < VPL; ++v)
         if (has[v]) red_add_f32<EPV>(dst + v * G * EPV, acc[cc][v]);
@@ -1081,10 +1153,11 @@ __global__ void __launch_bounds__(kThreads)
     if (wactive && lact) {
       const int32_t y = y0 + ry;
       const int64_t key0 = static_cast<int64_t>(p.lv.start[l]) + (static_cast<int64_t>(vz) * Hs + y) * W;
-      T* gvb = grad_value + (static_cast<int64_t>(b) * p.K) * p.H * p.C + h * p.C + ch;
+      T* gvb = grad_value + bh_base(p, b, h, p.K) + ch;
+      const int64_t ks = key_stride(p);
       const int nvox = min(32, W - xw);
       for (int v = 0; v < nvox; ++v)
-        gvb[(key0 + xw + v) * p.H * p.C] = Elem<T>::from_f(acc[v * 32 + lane]);
+        gvb[(key0 + xw + v) * ks] = Elem<T>::from_f(acc[v * 32 + lane]);
     }
     if (cb + 1 < ncb) __syncwarp();
   }

@@ -31,6 +31,10 @@ static cudaError_t sdots_one(const Problem& p, const SortPlan& sp, const void* g
     const int64_t grid = p.B * p.H * int64_t{sp.nsl} * sp.sd_chunks;
     msda_sdots_kernel<T, TS, NDIM, VB, VPL><<<dim3(static_cast<unsigned>(grid)), kThreads, 0, st>>>(
         p, sp, static_cast<const T*>(go), static_cast<TS*>(gl), static_cast<TS*>(ga));
+    const int64_t n = p.B * p.Q * p.H * int64_t{sp.nsl} * p.P;
+    msda_sdots_finish_kernel<TS, NDIM>
+        <<<dim3(static_cast<unsigned>((n + kThreads - 1) / kThreads)), kThreads, 0, st>>>(
+            p, sp, static_cast<TS*>(gl), static_cast<TS*>(ga));
     return cudaGetLastError();
   }
   (void)p; (void)sp; (void)go; (void)gl; (void)ga; (void)st;

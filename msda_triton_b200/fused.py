@@ -47,7 +47,7 @@ def _prepare(ndim, value, spatial_shapes, reference_points, offsets, logits):
 def _args(value, shapes, on_dev, ref, off, lg):
     B, K, H, C = value.shape
     _, Q, _, L, P, _ = off.shape
-    return (value.data_ptr(), _core._DTYPE_CODE[value.dtype], B, K, H, C,
+    return (value.data_ptr(), _core.value_code(value), B, K, H, C,
             shapes.data_ptr(), int(on_dev), L, ref.data_ptr(), off.data_ptr(), lg.data_ptr(),
             _core._DTYPE_CODE[off.dtype], Q, P)
 
@@ -61,7 +61,7 @@ class MSDAFusedFn(torch.autograd.Function):
                 attention_logits, clamp_grid=True, clamp_eps=1e-4):
         shapes, on_dev, ref, off, lg = _prepare(ndim, value, spatial_shapes, reference_points,
                                                 sampling_offsets, attention_logits)
-        value_c = value.contiguous()
+        value_c = _core.prepare_value(value)
         B, _, H, C = value_c.shape
         out = torch.empty((B, off.shape[1], H * C), device=value.device, dtype=value.dtype)
         fn = _lib.lib().msda2d_fused_fwd if ndim == 2 else _lib.lib().msda3d_fused_fwd
@@ -91,7 +91,7 @@ def _backward(ndim, grad_output, value, shapes, on_dev, ref, off, lg, clamp, eps
     B, K, H, C = value.shape
     _, Q, _, L, P, _ = off.shape
     lib = _lib.lib()
-    ws_bytes = lib.msda_fused_bwd_workspace_bytes(ndim, _core._DTYPE_CODE[value.dtype], B, K,
+    ws_bytes = lib.msda_fused_bwd_workspace_bytes(ndim, _core.value_code(value), B, K,
                                                   H, C, shapes.data_ptr(), int(on_dev), L, Q,
                                                   P)
     ws = torch.empty((ws_bytes,), device=value.device, dtype=torch.uint8) if ws_bytes else None

@@ -78,8 +78,10 @@ def test_workspace_bytes_sorted_path(monkeypatch):
     # Host shapes and >= 2^20 samples: the cell-sorted backward.  Its
     # workspace: bucket counts (one per cell of the (W+1)(H+1)(D+1) grid plus
     # a dead bucket, per level and (b, h), plus one), scan block sums, a rank
-    # and a 32-byte record per sample, and the fp32 accumulator of the levels
-    # with more than 2 samples per cell.
+    # and a 32-byte record per sample, the fp32 accumulator of the levels
+    # with more than 2 samples per cell, and 16 bytes per sample of the levels
+    # whose value slice per batch entry reaches 96 MiB (their dot products
+    # run in sorted order and are staged).
     monkeypatch.setenv("MSDA_BWD_PATH", "sorted")
     monkeypatch.delenv("MSDA_VOXEL_DENSITY", raising=False)
     monkeypatch.delenv("MSDA_SORTED_CHUNK_B", raising=False)
@@ -94,9 +96,13 @@ def test_workspace_bytes_sorted_path(monkeypatch):
     nblk = (nkeys + 4095) // 4096
     expect = (_align((nkeys + 1) * 4) + _align((nblk + 1) * 4) + _align(n * 4)
               + _align(n * 32) + _align(B * acc_keys * H * C * 4))
+    # bf16: the finest level holds 64 MiB of value per batch entry, no staging
     assert _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P) == expect
-    # fp32 values reduce the dense levels straight into grad_value: no accumulator
-    assert _ws(_lib.FLOAT32, B, shapes, H, C, Q, P) == expect - _align(B * acc_keys * H * C * 4)
+    # fp32 values reduce the dense levels straight into grad_value: no
+    # accumulator; the finest level's 128 MiB slice takes the sorted-order dots
+    stage = _align(B * Q * H * 1 * P * 16)
+    assert _ws(_lib.FLOAT32, B, shapes, H, C, Q, P) == (
+        expect - _align(B * acc_keys * H * C * 4) + stage)
     # device-resident shapes cannot be planned on the host: gather path
     K = sum(int(np.prod(s)) for s in shapes)
     assert _ws(_lib.BFLOAT16, B, shapes, H, C, Q, P, on_dev=1) == B * K * H * C * 4
