@@ -698,8 +698,9 @@ def run_module(args, wl, rank, world, local_rank):
     B, K, H, C, Q, L, P = dims(wl)
     d, dt, E = wl["ndim"], wl["dtype"], H * C
     torch.manual_seed(0)
+    kw = {} if impl != "ours" else {"fused_prologue": not args.module_unfused}
     m = (MSDA3D if d == 3 else MSDA2D)(embed_dims=E, num_heads=H, num_levels=L, num_points=P,
-                                       dropout=0.0, batch_first=True)
+                                       dropout=0.0, batch_first=True, **kw)
     m.init_weights()
     m = m.to(dev, dt)
     g = torch.Generator(device=dev).manual_seed(1234)
@@ -734,7 +735,9 @@ def run_module(args, wl, rank, world, local_rank):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": DTYPE_NAME[dt], "data": "synthetic (seeded; init_weights parameters)",
             "config": {"workload": args.workload, "embed_dims": E, "batch": B, "num_queries": Q,
-                       "num_keys": K, "num_heads": H, "num_levels": L, "num_points": P},
+                       "num_keys": K, "num_heads": H, "num_levels": L, "num_points": P,
+                       "prologue": ("unfused" if args.module_unfused else "fused")
+                       if impl == "ours" else "reference"},
             "clocks": clk.summary()}
 
 
@@ -864,6 +867,9 @@ def main():
     ap.add_argument("--workload", default="3d_xl_bf16", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-triton"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--module-unfused", action="store_true",
+                    help="module workloads: form locations and weights with torch ops and call "
+                         "msda2d/msda3d (fused_prologue=False)")
     ap.add_argument("--value-layout", default="bkhc", choices=["bkhc", "bhkc"],
                     help="device-resident value of the timed step: the reference's (B, K, H, C) "
                          "or head-major (B, H, K, C) storage (end-to-end leg: always bkhc)")

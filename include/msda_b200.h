@@ -166,14 +166,17 @@ MSDA_API int msda_cast_from_f32(const float* src, void* dst, int dst_dtype, int6
 
 /* Workspace bytes msda{2,3}d_bwd needs for this problem (it depends on the
  * level shapes, which must be the same pointer/residency as in the call).
- * fp32 values need none.  For fp16/bf16 values the gather/scatter backward
- * reduces levels with at most 8 expected contributions per element
- * (2^d*Q*P / voxels) straight into grad_value and accumulates the others in
- * an fp32 buffer of B * (their keys) * H * C * 4 bytes; with device-resident
- * shapes the host cannot plan levels and the buffer covers all K keys.  (The
- * opt-in binned backward, MSDA_BWD_PATH=binned, needs sample bins instead.)
- * The plan assumes value, grad_output and grad_value are 16-byte aligned.
- * The reference allocates its gradient buffers with torch.zeros_like
+ * The plan it sizes:
+ *  - host-resident shapes and at least 2^20 samples: the cell-sorted
+ *    backward -- bucket counts per cell of every level and (b, h), a rank
+ *    and a 32-byte record per sample, 16 bytes per sample of the levels whose
+ *    dot products run in sorted order, and (fp16/bf16 values) an fp32
+ *    accumulator for the levels with more than 2 samples per cell;
+ *  - otherwise the gather/scatter backward: none for fp32 values, an fp32
+ *    accumulator of B*K*H*C*4 bytes for fp16/bf16 values.
+ * Every value-gradient sum is carried in fp32 and rounded once.  The plan
+ * assumes value, grad_output and grad_value are 16-byte aligned.  The
+ * reference allocates its gradient buffers with torch.zeros_like
  * (triton/msda_3d.py:941-944); here the caller allocates.
  * Returns 0 when no workspace is needed or the arguments are invalid. */
 MSDA_API size_t msda_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batch,

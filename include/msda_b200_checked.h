@@ -7,8 +7,9 @@
  * gather and value-gradient scatter: an address outside its buffer is not
  * accessed and sets a bit of a per-device word (1: value gather, 2: 16-bit
  * grad_value scatter, 4: fp32 accumulator scatter).  It stands in for a
- * memory checker and is for tests and debugging; it is slower.  The binned
- * backward path is not instrumented.
+ * memory checker and is for tests and debugging; it is slower.  In the
+ * cell-sorted backward the value gathers are checked; its record, fp32
+ * accumulator and grad_value stores are not instrumented.
  */
 #ifndef MSDA_B200_CHECKED_H_
 #define MSDA_B200_CHECKED_H_
