@@ -548,7 +548,9 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   // dense kernel: up to 512 positions per CTA, records + grad_out rows in
   // at most 64 KB of shared memory
   {
-    const int64_t per = static_cast<int64_t>(sizeof(SRec)) + row_bytes + 4;
+    // per position: its record (later its corner weights), grad_out row,
+    // segment start and segment cell
+    const int64_t per = static_cast<int64_t>(sizeof(SRec)) + row_bytes + 8;
     int64_t dchunk = std::min<int64_t>(kDenseChunk, (64 * 1024 - 4) / per);
     dchunk = std::max<int64_t>(dchunk, 2 * kSegMax) & ~int64_t{1};
     sp.dchunk = static_cast<int32_t>(dchunk);

@@ -838,14 +838,18 @@ static __global__ void __launch_bounds__(kScanThreads)
 // of one (b, h, dense level) -- each owns exactly Q*P consecutive positions.
 // The CTA stages the positions' records and their grad_out rows in shared
 // memory (cp.async: two memory round trips), cuts the positions into
-// segments of one cell, at most kSegMax long, and gives each segment to a
-// lane group: per sample a * w_corner * grad_out is added to the cell's 2^d
-// corner gradients in fp32 registers, flushed with one vector reduction per
-// corner.
+// segments of one cell, at most kSegMax long, and replaces each record by
+// its 2^d corner weights a * w (computed once per sample, not once per lane).
+// Each segment goes to a lane group: per sample a * w_corner * grad_out is
+// added to the cell's 2^d corner gradients in fp32 registers, flushed with
+// one vector reduction per corner.
 constexpr int kSegMax = 16;
 
+// Rows of at most 32 fp32 accumulators per lane are held to 4 CTAs per SM
+// (64 registers); wider ones keep the registers they need.
 template <typename T, int NDIM, int VB, int VPL>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads,
+                                  ((1 << NDIM) * VPL * Chunk<T, VB>::EPV <= 32) ? 4 : 1)
     msda_dense_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
                       float* __restrict__ gacc) {
   using CK = Chunk<T, VB>;
@@ -858,6 +862,7 @@ __global__ void __launch_bounds__(kThreads)
   const int rowb = static_cast<int>(row_bytes);
   unsigned char* go_s = dsm + static_cast<size_t>(chunkn) * sizeof(SRec);  // chunkn * rowb
   int32_t* seg = reinterpret_cast<int32_t*>(go_s + static_cast<size_t>(chunkn) * rowb);
+  int32_t* segc = seg + chunkn + 1;  // the cell (level-relative key) of each segment
   __shared__ int32_t warp_tot[kThreads / 32];
 
   const uint32_t u = blockIdx.x;
@@ -869,6 +874,7 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t qp = p.Q * p.P;
   const int64_t base = (static_cast<int64_t>(bh) * p.L + l) * qp + int64_t{chunk} * chunkn;
   const int cnt = static_cast<int>(min(static_cast<int64_t>(chunkn), qp - int64_t{chunk} * chunkn));
+  const int32_t kl = static_cast<int32_t>(bh) * sp.seg_keys + sp.lvl_base[l];
   // records, then the grad_out rows they name
   for (int idx = threadIdx.x; idx < cnt * 2; idx += kThreads)
     cp_async<16>(reinterpret_cast<char*>(rec_s) + idx * 16,
@@ -891,12 +897,40 @@ __global__ void __launch_bounds__(kThreads)
     int32_t total;
     const int32_t off = block_exclusive_scan(static_cast<int32_t>(h0) + static_cast<int32_t>(h1),
                                              warp_tot, total);
-    if (h0) seg[off] = t0;
-    if (h1) seg[off + (h0 ? 1 : 0)] = t0 + 1;
+    if (h0) {
+      seg[off] = t0;
+      segc[off] = rec_s[t0].key - kl;
+    }
+    if (h1) {
+      seg[off + (h0 ? 1 : 0)] = t0 + 1;
+      segc[off + (h0 ? 1 : 0)] = rec_s[t0 + 1].key - kl;
+    }
     if (threadIdx.x == 0) seg[total] = cnt;
     cp_async_wait_all();
     __syncthreads();
     if (threadIdx.x == 0) warp_tot[0] = total;
+    // every grad_out copy has been issued and every key read: the records
+    // become their corner weights a * w (the reference's product order)
+    for (int t = threadIdx.x; t < cnt; t += kThreads) {
+      const float4 af = *reinterpret_cast<const float4*>(rec_s + t);  // a, f0, f1, f2
+      float wt[3][2];
+      const float f[3] = {af.y, af.z, af.w};
+#pragma unroll
+      for (int ax = 0; ax < 3; ++ax) {
+        if (ax < NDIM) { wt[ax][0] = __fsub_rn(1.0f, f[ax]); wt[ax][1] = f[ax]; }
+        else { wt[ax][0] = 1.0f; wt[ax][1] = 0.0f; }
+      }
+      float aw[8];
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        float w = __fmul_rn(wt[0][cc & 1], wt[1][(cc >> 1) & 1]);
+        if (NDIM == 3) w = __fmul_rn(w, wt[2][(cc >> 2) & 1]);
+        aw[cc] = cc < NC ? af.x * w : 0.0f;
+      }
+      float4* dst = reinterpret_cast<float4*>(rec_s + t);
+      dst[0] = make_float4(aw[0], aw[1], aw[2], aw[3]);
+      if (NDIM == 3) dst[1] = make_float4(aw[4], aw[5], aw[6], aw[7]);
+    }
     __syncthreads();
   }
   const int nseg = warp_tot[0];
@@ -907,7 +941,6 @@ __global__ void __launch_bounds__(kThreads)
   const int j = static_cast<int>(threadIdx.x) & (G - 1);
   const int32_t cx = sp.cells[l][0], cy = sp.cells[l][1];
   const int32_t ncell = cx * cy * sp.cells[l][2];
-  const int32_t kl = static_cast<int32_t>(bh) * sp.seg_keys + sp.lvl_base[l];
   const int32_t sz0 = p.lv.size[l][0], sz1 = p.lv.size[l][1], sz2 = p.lv.size[l][2];
   const int32_t b = static_cast<int32_t>(bh / static_cast<uint32_t>(p.H));
   const int32_t h = static_cast<int32_t>(bh - static_cast<uint32_t>(b) * static_cast<uint32_t>(p.H));
@@ -919,12 +952,14 @@ __global__ void __launch_bounds__(kThreads)
 
   for (int sg = grp; sg < nseg; sg += ng) {
     const int ta = seg[sg], tb = seg[sg + 1];
-    const int32_t c = rec_s[ta].key - kl;
+    const int32_t c = segc[sg];
     if (c >= ncell) continue;  // the dead bucket: no corner inside the level
     // the cell's lower corner and which of its corners lie inside the level
-    const int32_t ix = c % cx - 1;
-    const int32_t iy = (c / cx) % cy - 1;
-    const int32_t iz = NDIM == 3 ? c / (cx * cy) - 1 : 0;
+    const uint32_t cyz = fdiv(static_cast<uint32_t>(c), sp.div_cx[l]);
+    const uint32_t czz = fdiv(cyz, sp.div_cy[l]);
+    const int32_t ix = c - static_cast<int32_t>(cyz) * cx - 1;
+    const int32_t iy = static_cast<int32_t>(cyz - czz * static_cast<uint32_t>(cy)) - 1;
+    const int32_t iz = NDIM == 3 ? static_cast<int32_t>(czz) - 1 : 0;
     uint32_t vbits = 0;
 #pragma unroll
     for (int cc = 0; cc < NC; ++cc) {
@@ -947,23 +982,18 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
       for (int v = 0; v < VPL; ++v)
         CK::unpack(has[v] ? ld_shared_chunk<VB>(gq + v * G * VB) : raw_zero<VB>(), go[v]);
-      const float a = rec_s[t].a;
-      float wt[3][2];
-#pragma unroll
-      for (int ax = 0; ax < 3; ++ax) {
-        const float f = rec_s[t].f[ax];
-        if (ax < NDIM) { wt[ax][0] = __fsub_rn(1.0f, f); wt[ax][1] = f; }
-        else { wt[ax][0] = 1.0f; wt[ax][1] = 0.0f; }
+      const float4 w03 = *reinterpret_cast<const float4*>(rec_s + t);
+      float aw[8] = {w03.x, w03.y, w03.z, w03.w, 0.0f, 0.0f, 0.0f, 0.0f};
+      if constexpr (NDIM == 3) {
+        const float4 w47 = *(reinterpret_cast<const float4*>(rec_s + t) + 1);
+        aw[4] = w47.x; aw[5] = w47.y; aw[6] = w47.z; aw[7] = w47.w;
       }
 #pragma unroll
       for (int cc = 0; cc < NC; ++cc) {
-        float w = __fmul_rn(wt[0][cc & 1], wt[1][(cc >> 1) & 1]);
-        if (NDIM == 3) w = __fmul_rn(w, wt[2][(cc >> 2) & 1]);
-        const float aw = a * w;
 #pragma unroll
         for (int v = 0; v < VPL; ++v)
 #pragma unroll
-          for (int e = 0; e < EPV; ++e) acc[cc][v][e] = fmaf(aw, go[v][e], acc[cc][v][e]);
+          for (int e = 0; e < EPV; ++e) acc[cc][v][e] = fmaf(aw[cc], go[v][e], acc[cc][v][e]);
       }
     }
     const int32_t k0 = (iz * sz1 + iy) * sz0 + ix;
