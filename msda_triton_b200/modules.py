@@ -9,7 +9,11 @@ head chunking, gradient checkpointing and errors.  The deformable sampling
 itself is msda2d / msda3d of this package; with fused_prologue=True (the
 default, an extra keyword the reference's modules ignore) the locations and
 softmax weights are formed inside the kernels from the raw projections
-(msda2d_fused / msda3d_fused) instead of as separate tensors.
+(msda2d_fused / msda3d_fused) instead of as separate tensors -- for calls
+below FUSED_MAX_SAMPLES samples.  Larger calls form them with torch ops and
+call msda2d / msda3d, whose backward is then the cell-sorted pipeline: on
+the 3D xl module step (B=8, Q=100000) that is 40.6 ms against 41.8 ms for
+the fused prologue, whose backward is the gather/scatter kernel.
 
 Forward, with q the (batch-first) query and v the projected value:
     offsets = Linear(q) -> (B, Q, H, L, P, d)
@@ -30,6 +34,10 @@ from torch.utils.checkpoint import checkpoint
 from msda_triton_b200.fused import msda2d_fused, msda3d_fused
 from msda_triton_b200.msda_2d import msda2d
 from msda_triton_b200.msda_3d import msda3d
+
+# Samples (B*Q*H*L*P) per call from which the unfused composition is used
+# (the size from which the library's backward takes the cell-sorted plan).
+FUSED_MAX_SAMPLES = 1 << 20
 
 
 class _MSDAModule(nn.Module):
@@ -145,7 +153,7 @@ class _MSDAModule(nn.Module):
             qq = q[:, q0:q1]
             offsets = self.sampling_offsets(qq).view(bs, q1 - q0, H, L, P, d)
             logits = self.attention_weights(qq).view(bs, q1 - q0, H, L, P)
-            if self.fused_prologue:
+            if self.fused_prologue and bs * (q1 - q0) * hc * L * P < FUSED_MAX_SAMPLES:
                 # (loc, weights) formed per sample inside the kernels
                 ref = reference_points[:, q0:q1]
                 run = lambda h0, h1: self._run(self._sample_fused, v[:, :, h0:h1], shapes_host,
