@@ -603,7 +603,11 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
         sp.sl_level[sp.nsl++] = static_cast<int32_t>(l);
       }
     }
-    sp.sd_chunks = static_cast<int32_t>((a.Q * a.P + kSdotsPer - 1) / kSdotsPer);
+    // MSDA_SDOTS_PER (tuning): sorted positions per msda_sdots_kernel CTA
+    const char* per_env = std::getenv("MSDA_SDOTS_PER");
+    const int64_t per = per_env && std::atoll(per_env) > 0 ? std::atoll(per_env) : kSdotsPer;
+    sp.sd_per = static_cast<int32_t>(std::min<int64_t>(per, 1 << 20));
+    sp.sd_chunks = static_cast<int32_t>((a.Q * a.P + sp.sd_per - 1) / sp.sd_per);
     if (nb * a.H * sp.nsl * sp.sd_chunks >= INT32_MAX) return false;
   }
   pl.sp = sp;

@@ -109,6 +109,7 @@ struct SortPlan {
   int32_t sdots_mask;              // levels whose dot products msda_sdots_kernel takes in sorted order
   int32_t nsl;                     // such levels
   int32_t sl_level[kMaxLevels];    // k-th such level
+  int32_t sd_per;                  // sorted positions per msda_sdots_kernel CTA
   int32_t sd_chunks;               // msda_sdots_kernel CTAs per (b, h, level)
   FastDiv div_cx[kMaxLevels], div_cy[kMaxLevels];  // / cells[l][0], / cells[l][1]
   int32_t* cnt;                    // nkeys + 1: counts, then exclusive starts
@@ -529,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 4)
 // stretch of positions of the eight heads (CTA index: head fastest), whose
 // rows share the value lines.  The sample's grad_out row is gathered per
 // record (grad_out of a batch entry is a few tens of MB and stays in L2).
-constexpr int kSdotsPer = 512;  // sorted positions per msda_sdots_kernel CTA
+constexpr int kSdotsPer = 256;  // default sorted positions per msda_sdots_kernel CTA (one round)
 
 template <typename T, typename TS, int NDIM, int VB, int VPL>
 __global__ void __launch_bounds__(kThreads, 4)
@@ -562,7 +563,8 @@ __global__ void __launch_bounds__(kThreads, 4)
   const int64_t QP = p.Q * p.P;
   const int64_t bh = b * p.H + h;
   const SRec* recs = sp.srec + (bh * p.L + l) * QP;  // the (b, h, l) block of positions
-  const int64_t q_end = int64_t{k + 1} * kSdotsPer < QP ? int64_t{k + 1} * kSdotsPer : QP;
+  const int64_t per = sp.sd_per;
+  const int64_t q_end = int64_t{k + 1} * per < QP ? int64_t{k + 1} * per : QP;
 
   const int G = 1 << p.log2g;
   const int j = static_cast<int>(threadIdx.x) & (G - 1);
@@ -586,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 4)
   // Rounds (CTA-uniform, so every lane of a warp takes every shuffle): each
   // group takes G consecutive records; lane j decodes record q0 + j, then the
   // group walks them kDotBatch at a time.
-  for (int64_t qr = int64_t{k} * kSdotsPer; qr < q_end; qr += int64_t{groups} * G) {
+  for (int64_t qr = int64_t{k} * per; qr < q_end; qr += int64_t{groups} * G) {
     const int64_t q0 = qr + int64_t{grp} * G;
     SampleMeta mine;
     mine.key0 = 0;
