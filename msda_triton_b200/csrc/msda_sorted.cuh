@@ -474,6 +474,18 @@ __global__ void __launch_bounds__(kThreads, 4)
                          1);
     }
     const int nr = LP - r0 < G ? LP - r0 : G;
+    // a round wholly inside levels taken in sorted order has no dot products
+    // here (uniform across the warp: every row has the same level layout)
+    bool skip_round = true;
+    {
+      const int lf = static_cast<int>(fdiv(static_cast<uint32_t>(r0), sp.div_p));
+      const int ll = static_cast<int>(fdiv(static_cast<uint32_t>(r0 + nr - 1), sp.div_p));
+      for (int lv = lf; lv <= ll; ++lv) skip_round = skip_round && ((sp.sdots_mask >> lv) & 1);
+    }
+    if (skip_round) {
+      if (rank >= 0) sp.pos[row * LP + sj] = rank;
+      continue;
+    }
     for (int t0 = 0; t0 < nr; t0 += kDotBatch) {
       float v[NV];
       float sa[kDotBatch];
