@@ -306,36 +306,6 @@ __device__ __forceinline__ void corner_dot_grads(const float* D, const float* f,
   }
 }
 
-// Lane partial dot products of one sample: its 2^d corner chunks (corners
-// outside the level read the zero row: their dot is exactly 0) against the
-// lane's grad_out chunks.
-template <typename T, int NDIM, int VB, int VPL>
-__device__ __forceinline__ void corner_dots(const Corners<NDIM>& cs, const bool* has, int G,
-                                            const float (*go)[Chunk<T, VB>::EPV], float* D) {
-  using CK = Chunk<T, VB>;
-  constexpr int EPV = CK::EPV;
-  constexpr int NC = 1 << NDIM;
-  Raw<VB> raw[NC][VPL];
-#pragma unroll
-  for (int c = 0; c < NC; ++c)
-#pragma unroll
-    for (int vv = 0; vv < VPL; ++vv)
-      raw[c][vv] = has[vv] ? MSDA_LD_VALUE(VB, cs.valid[c] ? cs.ptr[c] + vv * G * VB : cs.ptr[c])
-                           : raw_zero<VB>();
-#pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    float dot = 0.0f;
-#pragma unroll
-    for (int vv = 0; vv < VPL; ++vv) {
-      float x[EPV];
-      CK::unpack(raw[c][vv], x);
-#pragma unroll
-      for (int e = 0; e < EPV; ++e) dot = fmaf(go[vv][e], x[e], dot);
-    }
-    D[c] = dot;
-  }
-}
-
 // The lane's kept results (dot_reduce) stored as grad_attn / grad_loc of
 // their samples: batch slot i holds sample sidx[i] (kNoSample: none), its
 // attention weight sa[i] and sinfo[i] = level | clamp-pass bits << 8.
