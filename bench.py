@@ -343,7 +343,7 @@ def run_ours(args, wl, rank, world, local_rank):
         "warmup": args.warmup,
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "strong" if args.scaling == "strong" and world > 1 else "weak",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": DTYPE_NAME[wl["dtype"]],
         "data": "synthetic (seeded N(0,1) value/grad_out, U[0,1) locations, softmax weights)",
@@ -848,7 +848,7 @@ def run_reference(args, wl, rank):
         "metric": "MSDA fwd+bwd Gsamples/s" if not fwd_only else "MSDA fwd Gsamples/s",
         "value": val, "unit": "Gsamples/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-        "scaling": "strong" if args.gpus > 1 and args.scaling == "strong" else "weak",
+        "scaling": args.scaling,
         "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
         "config": {"workload": args.workload, "ndim": wl["ndim"], "batch_per_gpu": 1,
                    "num_queries": swl["Q"], "note": "bounded CPU sample of the workload"},
