@@ -556,6 +556,12 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
     sp.dchunk = static_cast<int32_t>(dchunk);
     sp.dchunks = static_cast<int32_t>((a.Q * a.P + dchunk - 1) / dchunk);
     sp.dsmem = static_cast<int32_t>(dchunk * per + 4);
+    // 16-bit values with C = 16, 32 or 64: the tensor-core dense kernel
+    // (MSDA_DENSE_MMA=0 keeps the CUDA-core one); it also keeps 16 zero bytes
+    const char* mma_env = std::getenv("MSDA_DENSE_MMA");
+    sp.dmma = (dtype_bytes(a.vdt) == 2 && (a.C == 16 || a.C == 32 || a.C == 64) &&
+               !(mma_env && std::strcmp(mma_env, "0") == 0)) ? 1 : 0;
+    if (sp.dmma) sp.dsmem += 32;
   }
   sp.dlog2g = pw.log2g;
   sp.dnv = static_cast<int32_t>(a.C * dtype_bytes(a.vdt) / lw.vb);

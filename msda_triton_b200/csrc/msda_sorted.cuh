@@ -96,6 +96,7 @@ struct SortPlan {
   int32_t dlog2g, dnv;             // msda_dense_kernel lane group: 2^dlog2g lanes, dnv chunks per row
   FastDiv div_dnv;                 // / dnv
   int32_t dsmem;                   // msda_dense_kernel dynamic shared memory
+  int32_t dmma;                    // dense levels on msda_dense_mma_kernel (16-bit, C = 16/32/64)
   int32_t nvl;                     // voxel levels
   int32_t vl_level[kMaxLevels];    // k-th voxel level
   VoxTile vl_tile[kMaxLevels];     // msda_voxel_kernel tile of the k-th voxel level
@@ -989,6 +990,232 @@ __global__ void __launch_bounds__(kThreads,
 #pragma unroll
       for (int v = 0; v < VPL; ++v)
         if (has[v]) red_add_f32<EPV>(dst + v * G * EPV, acc[cc][v]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ dense levels, tensor cores
+// The same value gradient for 16-bit values (C a multiple of 16 bytes' worth
+// of channels, C/8 = NT n-tiles of 8 channels) on the tensor cores.  Within
+// one cell the gradient of its corners is a small product:
+//   G[corner][ch] = sum over the cell's samples s of W[s][corner] * go[s][ch]
+// with W = a * w_corner.  A warp takes one cell run (all its samples inside
+// the CTA's positions, not capped) and walks it 16 samples at a time with
+// mma.sync m16n8k16 (rows: corners, K: samples, N: channels): grad_out rows
+// come from shared memory with ldmatrix.trans, the weights as two 16-bit
+// halves W = W_hi + W_lo (two products per tile, fp32 accumulation), which
+// keeps the weight's error near 2^-16 of W.  The corners are flushed with one
+// fp32 vector reduction per lane, corner and n-tile, once per cell run.
+template <typename T> struct MmaT;
+template <> struct MmaT<__nv_bfloat16> {
+  static __device__ __forceinline__ uint16_t bits(float x) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+  }
+  static __device__ __forceinline__ float value(uint16_t b) {
+    return __bfloat162float(__ushort_as_bfloat16(b));
+  }
+  static __device__ __forceinline__ void mma(float* d, uint32_t a0, uint32_t a2, uint32_t b0,
+                                             uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  }
+};
+template <> struct MmaT<__half> {
+  static __device__ __forceinline__ uint16_t bits(float x) {
+    return __half_as_ushort(__float2half_rn(x));
+  }
+  static __device__ __forceinline__ float value(uint16_t b) {
+    return __half2float(__ushort_as_half(b));
+  }
+  static __device__ __forceinline__ void mma(float* d, uint32_t a0, uint32_t a2, uint32_t b0,
+                                             uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  }
+};
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                                  uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <typename T, int NDIM, int NT>
+__global__ void __launch_bounds__(kThreads, 4)
+    msda_dense_mma_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
+                          float* __restrict__ gacc) {
+  constexpr int NC = 1 << NDIM;
+  constexpr int ROWB = NT * 16;  // grad_out row bytes (C 16-bit channels)
+  extern __shared__ __align__(16) unsigned char dsm[];
+  const int chunkn = sp.dchunk;
+  SRec* rec_s = reinterpret_cast<SRec*>(dsm);                              // chunkn
+  unsigned char* go_s = dsm + static_cast<size_t>(chunkn) * sizeof(SRec);  // chunkn * ROWB
+  int32_t* seg = reinterpret_cast<int32_t*>(go_s + static_cast<size_t>(chunkn) * ROWB);
+  int32_t* segc = seg + chunkn + 1;
+  // 16 zero bytes: the ldmatrix row of samples past a run's end
+  unsigned char* zrow = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(segc + chunkn) + 15) & ~uintptr_t{15});
+  __shared__ int32_t warp_tot[kThreads / 32];
+
+  const uint32_t u = blockIdx.x;
+  const uint32_t chunk = u % static_cast<uint32_t>(sp.dchunks);
+  const uint32_t r1 = u / static_cast<uint32_t>(sp.dchunks);
+  const int kd = static_cast<int>(r1 % static_cast<uint32_t>(sp.ndl));
+  const uint32_t bh = r1 / static_cast<uint32_t>(sp.ndl);
+  const int l = sp.dl_level[kd];
+  const int64_t qp = p.Q * p.P;
+  const int64_t base = (static_cast<int64_t>(bh) * p.L + l) * qp + int64_t{chunk} * chunkn;
+  const int cnt = static_cast<int>(min(static_cast<int64_t>(chunkn), qp - int64_t{chunk} * chunkn));
+  const int32_t kl = static_cast<int32_t>(bh) * sp.seg_keys + sp.lvl_base[l];
+  if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(zrow)[threadIdx.x] = 0u;
+  // records, then the grad_out rows they name
+  for (int idx = threadIdx.x; idx < cnt * 2; idx += kThreads)
+    cp_async<16>(reinterpret_cast<char*>(rec_s) + idx * 16,
+                 reinterpret_cast<const char*>(sp.srec + base) + idx * 16);
+  cp_async_wait_all();
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < cnt * NT; idx += kThreads) {
+    const int t = idx / NT;
+    const int c = idx - t * NT;
+    cp_async<16>(go_s + static_cast<size_t>(t) * ROWB + c * 16,
+                 reinterpret_cast<const char*>(grad_out) +
+                     static_cast<int64_t>(rec_s[t].row) * ROWB + c * 16);
+  }
+  {
+    // runs of one cell (no length cap)
+    const int t0 = 2 * threadIdx.x;
+    bool h0 = false, h1 = false;
+    if (t0 < cnt) h0 = t0 == 0 || rec_s[t0].key != rec_s[t0 - 1].key;
+    if (t0 + 1 < cnt) h1 = rec_s[t0 + 1].key != rec_s[t0].key;
+    int32_t total;
+    const int32_t off = block_exclusive_scan(static_cast<int32_t>(h0) + static_cast<int32_t>(h1),
+                                             warp_tot, total);
+    if (h0) {
+      seg[off] = t0;
+      segc[off] = rec_s[t0].key - kl;
+    }
+    if (h1) {
+      seg[off + (h0 ? 1 : 0)] = t0 + 1;
+      segc[off + (h0 ? 1 : 0)] = rec_s[t0 + 1].key - kl;
+    }
+    if (threadIdx.x == 0) seg[total] = cnt;
+    cp_async_wait_all();
+    __syncthreads();
+    if (threadIdx.x == 0) warp_tot[0] = total;
+    // every grad_out copy issued and every key read: the records become their
+    // corner weights, 16-bit high halves in bytes 0-15, low halves in 16-31
+    for (int t = threadIdx.x; t < cnt; t += kThreads) {
+      const float4 af = *reinterpret_cast<const float4*>(rec_s + t);  // a, f0, f1, f2
+      float wt[3][2];
+      const float f[3] = {af.y, af.z, af.w};
+#pragma unroll
+      for (int ax = 0; ax < 3; ++ax) {
+        if (ax < NDIM) { wt[ax][0] = __fsub_rn(1.0f, f[ax]); wt[ax][1] = f[ax]; }
+        else { wt[ax][0] = 1.0f; wt[ax][1] = 0.0f; }
+      }
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int cp = 0; cp < 4; ++cp) {
+        uint32_t h2 = 0u, l2 = 0u;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int cc = 2 * cp + e;
+          float w = __fmul_rn(wt[0][cc & 1], wt[1][(cc >> 1) & 1]);
+          if (NDIM == 3) w = __fmul_rn(w, wt[2][(cc >> 2) & 1]);
+          const float aw = cc < NC ? af.x * w : 0.0f;
+          const uint16_t bh16 = MmaT<T>::bits(aw);
+          const uint16_t bl16 = MmaT<T>::bits(aw - MmaT<T>::value(bh16));
+          h2 |= static_cast<uint32_t>(bh16) << (16 * e);
+          l2 |= static_cast<uint32_t>(bl16) << (16 * e);
+        }
+        hi[cp] = h2;
+        lo[cp] = l2;
+      }
+      uint4* dst = reinterpret_cast<uint4*>(rec_s + t);
+      dst[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      dst[1] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    __syncthreads();
+  }
+  const int nseg = warp_tot[0];
+
+  const int lane = static_cast<int>(threadIdx.x & 31u);
+  const int warp = static_cast<int>(threadIdx.x >> 5);
+  const int g = lane >> 2, t4 = lane & 3;
+  const int32_t cx = sp.cells[l][0], cy = sp.cells[l][1];
+  const int32_t ncell = cx * cy * sp.cells[l][2];
+  const int32_t sz0 = p.lv.size[l][0], sz1 = p.lv.size[l][1], sz2 = p.lv.size[l][2];
+  const int32_t b = static_cast<int32_t>(bh / static_cast<uint32_t>(p.H));
+  const int32_t h = static_cast<int32_t>(bh - static_cast<uint32_t>(b) * static_cast<uint32_t>(p.H));
+  const int64_t kshift = p.acc_compact ? p.acc_start[l] : p.lv.start[l];
+  const int64_t ks = key_stride(p);
+  float* gbase = gacc + bh_base(p, b, h, p.acc_keys) + kshift * ks + 2 * t4;
+  const uint16_t* wts = reinterpret_cast<const uint16_t*>(rec_s);  // 16 halves per record
+  // this lane's ldmatrix row: sample kr of the 16-sample step, n-tile offset jo
+  const int kr = (lane & 7) + ((lane >> 3) & 1) * 8;
+  const int jo = lane >> 4;
+
+  for (int sg = warp; sg < nseg; sg += kThreads / 32) {
+    const int ta = seg[sg], len = seg[sg + 1] - ta;
+    const int32_t c = segc[sg];
+    if (c >= ncell) continue;  // the dead bucket: no corner inside the level
+    const uint32_t cyz = fdiv(static_cast<uint32_t>(c), sp.div_cx[l]);
+    const uint32_t czz = fdiv(cyz, sp.div_cy[l]);
+    const int32_t ix = c - static_cast<int32_t>(cyz) * cx - 1;
+    const int32_t iy = static_cast<int32_t>(cyz - czz * static_cast<uint32_t>(cy)) - 1;
+    const int32_t iz = NDIM == 3 ? static_cast<int32_t>(czz) - 1 : 0;
+    float d[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0.0f;
+    for (int kk = 0; kk < len; kk += 16) {
+      // A: rows = corners (g < NC), K = samples kk + 2*t4 + {0, 1} and + 8
+      uint32_t ah0 = 0u, ah2 = 0u, al0 = 0u, al2 = 0u;
+      if (g < NC) {
+        const int s0 = kk + 2 * t4;
+        uint32_t w[4][2];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int s = s0 + (e & 1) + (e >> 1) * 8;
+          const bool in = s < len;
+          const uint16_t* wr = wts + static_cast<size_t>(ta + (in ? s : 0)) * 16 + g;
+          w[e][0] = in ? wr[0] : 0u;
+          w[e][1] = in ? wr[8] : 0u;
+        }
+        ah0 = w[0][0] | (w[1][0] << 16);
+        ah2 = w[2][0] | (w[3][0] << 16);
+        al0 = w[0][1] | (w[1][1] << 16);
+        al2 = w[2][1] | (w[3][1] << 16);
+      }
+      const bool rin = kk + kr < len;
+      const unsigned char* rowp = rin ? go_s + static_cast<size_t>(ta + kk + kr) * ROWB : nullptr;
+#pragma unroll
+      for (int jj = 0; jj < NT; jj += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(smem_addr(rin ? rowp + (jj + jo) * 16 : zrow), b0, b1, b2, b3);
+        MmaT<T>::mma(d[jj], ah0, ah2, b0, b1);
+        MmaT<T>::mma(d[jj], al0, al2, b0, b1);
+        MmaT<T>::mma(d[jj + 1], ah0, ah2, b2, b3);
+        MmaT<T>::mma(d[jj + 1], al0, al2, b2, b3);
+      }
+    }
+    if (g < NC) {
+      const int x = ix + (g & 1), y = iy + ((g >> 1) & 1), z = iz + ((g >> 2) & 1);
+      const bool ok = static_cast<uint32_t>(x) < static_cast<uint32_t>(sz0) &&
+                      static_cast<uint32_t>(y) < static_cast<uint32_t>(sz1) &&
+                      (NDIM == 2 || static_cast<uint32_t>(z) < static_cast<uint32_t>(sz2));
+      if (ok) {
+        const int32_t k = (z * sz1 + y) * sz0 + x;
+        float* dst = gbase + static_cast<int64_t>(k) * ks;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) red_add_f32<2>(dst + 8 * j, d[j]);
+      }
     }
   }
 }
