@@ -195,3 +195,35 @@ def test_dense_cuda_core_and_tensor_core_agree(monkeypatch, case, dtype):
         monkeypatch.setenv("MSDA_DENSE_MMA", mma)
         got = cuda_fwd_bwd(ndim, *inp)
         check_all(got, ref, TOL_HALF, TOL_HALF, f"{case} {dtype} dense mma={mma}")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("path", ["sorted", "scatter"])
+def test_module_like_clustered_half_precision(monkeypatch, path, dtype):
+    """Sampling points the way the MSDA3D module forms them -- reference point
+    per query plus init_weights' per-head offset pattern (with per-query
+    jitter of half a cell) divided by the level size -- with every reference
+    point inside a 4-cell box of the finest level: hundreds of contributions
+    per value-gradient element on every level.  16-bit values against the
+    fp32 oracle at the half-precision bar."""
+    from msda_triton_b200.modules import MSDA3D
+
+    shapes = [(12, 16, 16), (6, 8, 8), (3, 4, 4)]
+    B, Q, H, C, L, P = 2, 3000, 8, 32, len(shapes), 4
+    g = torch.Generator().manual_seed(17)
+    m = MSDA3D(embed_dims=H * C, num_heads=H, num_levels=L, num_points=P)
+    m.init_weights()
+    pattern = m.sampling_offsets.bias.detach().view(H, L, P, 3)           # (H, L, P, 3) in cells
+    off = pattern + 0.5 * torch.randn(B, Q, H, L, P, 3, generator=g)
+    box = torch.tensor([4.0 / s for s in (16, 16, 12)])                   # 4 cells of level 0 (x, y, z)
+    ref = 0.5 - box / 2 + torch.rand(B, Q, L, 3, generator=g) * box
+    norm = torch.tensor([[w, h, d] for d, h, w in shapes], dtype=torch.float32)
+    loc = ref[:, :, None, :, None, :] + off / norm[None, None, None, :, None, :]
+    attn = torch.randn(B, Q, H, L * P, generator=g).softmax(-1).view(B, Q, H, L, P)
+    value = torch.randn(B, sum(d * h * w for d, h, w in shapes), H, C, generator=g)
+    go = torch.randn(B, Q, H * C, generator=g)
+    inp = _cast((value, torch.tensor(shapes), loc, attn, go), dtype, dtype)
+    _env(monkeypatch, "auto", path=path)
+    got = cuda_fwd_bwd(3, *inp)
+    ref_out = oracle_all(*_upcast(inp))
+    check_all(got, ref_out, TOL_HALF, TOL_HALF, f"module-like clustered {dtype} {path}")
