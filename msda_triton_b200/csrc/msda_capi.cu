@@ -459,6 +459,11 @@ constexpr int64_t kVoxelCap = 512;
 // their dot products in sorted order (msda_sdots_kernel): in query order
 // their rows are fetched from DRAM on almost every touch.
 constexpr double kSortedDotsMinBytes = 96.0 * 1048576.0;
+// Dense levels with at least this many samples per cell and (b, h) aggregate
+// on the tensor cores (16-bit values).  Measured on 3D xl (B=8, bf16): level 1
+// (2.9 per cell) 1.96 ms on the CUDA cores against 2.43 ms on the tensor
+// cores; levels 2-3 (22 and 154 per cell) 2.35 against 1.52 ms.
+constexpr double kDenseMmaMinDensity = 8.0;
 
 FastDiv make_fdiv(uint32_t d) {
   if (d == 0) d = 1;
@@ -499,6 +504,14 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   cap = std::min<int64_t>(cap, kVoxelCap) & ~int64_t{1};
   if (cap < 16) max_dens = -1.0;
   SortPlan sp{};
+  // 16-bit values with C = 16, 32 or 64: dense levels with at least
+  // kDenseMmaMinDensity samples per cell and (b, h) go to the tensor-core
+  // kernel (MSDA_DENSE_MMA=0: none; MSDA_DENSE_MMA_DENSITY: the threshold)
+  const char* mma_env = std::getenv("MSDA_DENSE_MMA");
+  const bool mma_ok = dtype_bytes(a.vdt) == 2 && (a.C == 16 || a.C == 32 || a.C == 64) &&
+                      !(mma_env && std::strcmp(mma_env, "0") == 0);
+  const char* mma_dens_env = std::getenv("MSDA_DENSE_MMA_DENSITY");
+  const double mma_dens = mma_dens_env ? std::atof(mma_dens_env) : kDenseMmaMinDensity;
   int64_t seg = 0, vox = 0, acc_keys = 0, units = 0, max_bounds = 0;
   int nvl = 0;
   const bool f32 = a.vdt == MSDA_FLOAT32;
@@ -541,7 +554,10 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
     } else {
       pl.acc_start[l] = static_cast<int32_t>(f32 ? p.lv.start[l] : acc_keys);
       acc_keys += nvox;
-      sp.dl_level[sp.ndl++] = static_cast<int32_t>(l);
+      if (mma_ok && dens >= mma_dens)
+        sp.ml_level[sp.nml++] = static_cast<int32_t>(l);
+      else
+        sp.dl_level[sp.ndl++] = static_cast<int32_t>(l);
     }
   }
   sp.vl_ubase[nvl] = static_cast<int32_t>(units);
@@ -556,12 +572,11 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
     sp.dchunk = static_cast<int32_t>(dchunk);
     sp.dchunks = static_cast<int32_t>((a.Q * a.P + dchunk - 1) / dchunk);
     sp.dsmem = static_cast<int32_t>(dchunk * per + 4);
-    // 16-bit values with C = 16, 32 or 64: the tensor-core dense kernel
-    // (MSDA_DENSE_MMA=0 keeps the CUDA-core one); it also keeps 16 zero bytes
-    const char* mma_env = std::getenv("MSDA_DENSE_MMA");
-    sp.dmma = (dtype_bytes(a.vdt) == 2 && (a.C == 16 || a.C == 32 || a.C == 64) &&
-               !(mma_env && std::strcmp(mma_env, "0") == 0)) ? 1 : 0;
-    if (sp.dmma) sp.dsmem += 32;
+    // the tensor-core kernel: the records' area also holds the corner-weight
+    // table, and 16 zero bytes follow
+    const int64_t area0 =
+        (std::max<int64_t>(dchunk * int64_t{sizeof(SRec)}, kWBytes) + 15) & ~int64_t{15};
+    sp.dsmem_mma = static_cast<int32_t>(area0 + dchunk * (row_bytes + 8) + 4 + 32);
   }
   sp.dlog2g = pw.log2g;
   sp.dnv = static_cast<int32_t>(a.C * dtype_bytes(a.vdt) / lw.vb);

@@ -89,14 +89,16 @@ struct SortPlan {
   int32_t lvl_base[kMaxLevels];    // first key of level l inside a (b, h) block
   int32_t cells[kMaxLevels][3];    // cell-grid extent per axis (size + 1; 1 for z in 2D)
   int32_t voxel_mask;              // levels whose value gradient msda_voxel_kernel gathers
-  int32_t ndl;                     // dense levels (msda_dense_kernel)
-  int32_t dl_level[kMaxLevels];    // k-th dense level
+  int32_t ndl;                     // dense levels on msda_dense_kernel (CUDA cores)
+  int32_t dl_level[kMaxLevels];    // k-th such level
   int32_t dchunk;                  // sorted positions per msda_dense_kernel CTA
   int32_t dchunks;                 // msda_dense_kernel CTAs per (b, h, dense level)
   int32_t dlog2g, dnv;             // msda_dense_kernel lane group: 2^dlog2g lanes, dnv chunks per row
   FastDiv div_dnv;                 // / dnv
   int32_t dsmem;                   // msda_dense_kernel dynamic shared memory
-  int32_t dmma;                    // dense levels on msda_dense_mma_kernel (16-bit, C = 16/32/64)
+  int32_t nml;                     // dense levels on msda_dense_mma_kernel (16-bit, C = 16/32/64)
+  int32_t ml_level[kMaxLevels];    // k-th such level
+  int32_t dsmem_mma;               // its dynamic shared memory
   int32_t nvl;                     // voxel levels
   int32_t vl_level[kMaxLevels];    // k-th voxel level
   VoxTile vl_tile[kMaxLevels];     // msda_voxel_kernel tile of the k-th voxel level
@@ -1047,6 +1049,12 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, u
                : "r"(addr));
 }
 
+// Row stride (16-bit values) of the corner-weight table in shared memory:
+// the CTA's positions (at most 2 * kThreads) plus 8 halves of padding (a
+// 4-bank shift per row) and 8 of slack for the last row's paired loads.
+constexpr int kWStride = 2 * kThreads + 8;
+constexpr int kWBytes = (16 * kWStride + 8) * 2;
+
 template <typename T, int NDIM, int NT>
 __global__ void __launch_bounds__(kThreads, 4)
     msda_dense_mma_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
@@ -1055,11 +1063,14 @@ __global__ void __launch_bounds__(kThreads, 4)
   constexpr int ROWB = NT * 16;  // grad_out row bytes (C 16-bit channels)
   extern __shared__ __align__(16) unsigned char dsm[];
   const int chunkn = sp.dchunk;
-  SRec* rec_s = reinterpret_cast<SRec*>(dsm);                              // chunkn
-  unsigned char* go_s = dsm + static_cast<size_t>(chunkn) * sizeof(SRec);  // chunkn * ROWB
+  // the records (chunkn * 32 bytes), later the corner-weight table (kWBytes)
+  SRec* rec_s = reinterpret_cast<SRec*>(dsm);
+  const size_t area0 = (max(static_cast<size_t>(chunkn) * sizeof(SRec),
+                            static_cast<size_t>(kWBytes)) + 15) & ~size_t{15};
+  unsigned char* go_s = dsm + area0;                                       // chunkn * ROWB
   int32_t* seg = reinterpret_cast<int32_t*>(go_s + static_cast<size_t>(chunkn) * ROWB);
   int32_t* segc = seg + chunkn + 1;
-  // 16 zero bytes: the ldmatrix row of samples past a run's end
+  // 16 zero bytes: the ldmatrix row of samples outside a run
   unsigned char* zrow = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(segc + chunkn) + 15) & ~uintptr_t{15});
   __shared__ int32_t warp_tot[kThreads / 32];
@@ -1067,9 +1078,9 @@ __global__ void __launch_bounds__(kThreads, 4)
   const uint32_t u = blockIdx.x;
   const uint32_t chunk = u % static_cast<uint32_t>(sp.dchunks);
   const uint32_t r1 = u / static_cast<uint32_t>(sp.dchunks);
-  const int kd = static_cast<int>(r1 % static_cast<uint32_t>(sp.ndl));
-  const uint32_t bh = r1 / static_cast<uint32_t>(sp.ndl);
-  const int l = sp.dl_level[kd];
+  const int kd = static_cast<int>(r1 % static_cast<uint32_t>(sp.nml));
+  const uint32_t bh = r1 / static_cast<uint32_t>(sp.nml);
+  const int l = sp.ml_level[kd];
   const int64_t qp = p.Q * p.P;
   const int64_t base = (static_cast<int64_t>(bh) * p.L + l) * qp + int64_t{chunk} * chunkn;
   const int cnt = static_cast<int>(min(static_cast<int64_t>(chunkn), qp - int64_t{chunk} * chunkn));
@@ -1109,38 +1120,39 @@ __global__ void __launch_bounds__(kThreads, 4)
     cp_async_wait_all();
     __syncthreads();
     if (threadIdx.x == 0) warp_tot[0] = total;
-    // every grad_out copy issued and every key read: the records become their
-    // corner weights, 16-bit high halves in bytes 0-15, low halves in 16-31
-    for (int t = threadIdx.x; t < cnt; t += kThreads) {
-      const float4 af = *reinterpret_cast<const float4*>(rec_s + t);  // a, f0, f1, f2
+    // every grad_out copy issued and every key read: the record area becomes
+    // the corner weights, 16 rows of 16-bit values (rows 0-7: high halves of
+    // corners 0-7, rows 8-15: low halves) of kWStride samples each; the row
+    // padding makes the A-fragment loads of a warp hit 32 distinct banks.
+    // Each thread first takes its (at most two) records into registers.
+    float4 af[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int t = threadIdx.x + i * kThreads;
+      af[i] = t < cnt ? *reinterpret_cast<const float4*>(rec_s + t) : make_float4(0, 0, 0, 0);
+    }
+    __syncthreads();
+    uint16_t* wts_w = reinterpret_cast<uint16_t*>(rec_s);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int t = threadIdx.x + i * kThreads;
+      if (t >= cnt) continue;
       float wt[3][2];
-      const float f[3] = {af.y, af.z, af.w};
+      const float f[3] = {af[i].y, af[i].z, af[i].w};
 #pragma unroll
       for (int ax = 0; ax < 3; ++ax) {
         if (ax < NDIM) { wt[ax][0] = __fsub_rn(1.0f, f[ax]); wt[ax][1] = f[ax]; }
         else { wt[ax][0] = 1.0f; wt[ax][1] = 0.0f; }
       }
-      uint32_t hi[4], lo[4];
 #pragma unroll
-      for (int cp = 0; cp < 4; ++cp) {
-        uint32_t h2 = 0u, l2 = 0u;
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int cc = 2 * cp + e;
-          float w = __fmul_rn(wt[0][cc & 1], wt[1][(cc >> 1) & 1]);
-          if (NDIM == 3) w = __fmul_rn(w, wt[2][(cc >> 2) & 1]);
-          const float aw = cc < NC ? af.x * w : 0.0f;
-          const uint16_t bh16 = MmaT<T>::bits(aw);
-          const uint16_t bl16 = MmaT<T>::bits(aw - MmaT<T>::value(bh16));
-          h2 |= static_cast<uint32_t>(bh16) << (16 * e);
-          l2 |= static_cast<uint32_t>(bl16) << (16 * e);
-        }
-        hi[cp] = h2;
-        lo[cp] = l2;
+      for (int cc = 0; cc < 8; ++cc) {
+        float w = __fmul_rn(wt[0][cc & 1], wt[1][(cc >> 1) & 1]);
+        if (NDIM == 3) w = __fmul_rn(w, wt[2][(cc >> 2) & 1]);
+        const float aw = cc < NC ? af[i].x * w : 0.0f;
+        const uint16_t bh16 = MmaT<T>::bits(aw);
+        wts_w[cc * kWStride + t] = bh16;
+        wts_w[(8 + cc) * kWStride + t] = MmaT<T>::bits(aw - MmaT<T>::value(bh16));
       }
-      uint4* dst = reinterpret_cast<uint4*>(rec_s + t);
-      dst[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      dst[1] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
     __syncthreads();
   }
@@ -1157,13 +1169,13 @@ __global__ void __launch_bounds__(kThreads, 4)
   const int64_t kshift = p.acc_compact ? p.acc_start[l] : p.lv.start[l];
   const int64_t ks = key_stride(p);
   float* gbase = gacc + bh_base(p, b, h, p.acc_keys) + kshift * ks + 2 * t4;
-  const uint16_t* wts = reinterpret_cast<const uint16_t*>(rec_s);  // 16 halves per record
+  const uint16_t* wts = reinterpret_cast<const uint16_t*>(rec_s);  // [16][kWStride]
   // this lane's ldmatrix row: sample kr of the 16-sample step, n-tile offset jo
   const int kr = (lane & 7) + ((lane >> 3) & 1) * 8;
   const int jo = lane >> 4;
 
   for (int sg = warp; sg < nseg; sg += kThreads / 32) {
-    const int ta = seg[sg], len = seg[sg + 1] - ta;
+    const int ta = seg[sg], tb = seg[sg + 1];
     const int32_t c = segc[sg];
     if (c >= ncell) continue;  // the dead bucket: no corner inside the level
     const uint32_t cyz = fdiv(static_cast<uint32_t>(c), sp.div_cx[l]);
@@ -1174,27 +1186,31 @@ __global__ void __launch_bounds__(kThreads, 4)
     float d[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0.0f;
-    for (int kk = 0; kk < len; kk += 16) {
-      // A: rows = corners (g < NC), K = samples kk + 2*t4 + {0, 1} and + 8
+    // 16-sample steps from an even position (32-bit weight pairs); samples
+    // outside the run [ta, tb) get weight 0 and the zero grad_out row
+    for (int k0 = ta & ~1; k0 < tb; k0 += 16) {
       uint32_t ah0 = 0u, ah2 = 0u, al0 = 0u, al2 = 0u;
       if (g < NC) {
-        const int s0 = kk + 2 * t4;
-        uint32_t w[4][2];
+        const int s0 = k0 + 2 * t4;
+        uint32_t w[2][2];  // [step half][hi / lo]
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int s = s0 + (e & 1) + (e >> 1) * 8;
-          const bool in = s < len;
-          const uint16_t* wr = wts + static_cast<size_t>(ta + (in ? s : 0)) * 16 + g;
-          w[e][0] = in ? wr[0] : 0u;
-          w[e][1] = in ? wr[8] : 0u;
+        for (int e = 0; e < 2; ++e) {
+          const int s = s0 + 8 * e;  // even: samples s, s + 1
+          const uint32_t keep = (s >= ta && s < tb ? 0x0000ffffu : 0u) |
+                                (s + 1 >= ta && s + 1 < tb ? 0xffff0000u : 0u);
+          const bool any = keep != 0u;
+          w[e][0] = any ? *reinterpret_cast<const uint32_t*>(wts + g * kWStride + s) & keep : 0u;
+          w[e][1] = any ? *reinterpret_cast<const uint32_t*>(wts + (8 + g) * kWStride + s) & keep
+                        : 0u;
         }
-        ah0 = w[0][0] | (w[1][0] << 16);
-        ah2 = w[2][0] | (w[3][0] << 16);
-        al0 = w[0][1] | (w[1][1] << 16);
-        al2 = w[2][1] | (w[3][1] << 16);
+        ah0 = w[0][0];
+        ah2 = w[1][0];
+        al0 = w[0][1];
+        al2 = w[1][1];
       }
-      const bool rin = kk + kr < len;
-      const unsigned char* rowp = rin ? go_s + static_cast<size_t>(ta + kk + kr) * ROWB : nullptr;
+      const int sr = k0 + kr;
+      const bool rin = sr >= ta && sr < tb;
+      const unsigned char* rowp = go_s + static_cast<size_t>(rin ? sr : 0) * ROWB;
 #pragma unroll
       for (int jj = 0; jj < NT; jj += 2) {
         uint32_t b0, b1, b2, b3;

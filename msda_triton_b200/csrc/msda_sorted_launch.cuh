@@ -62,12 +62,13 @@ template <typename T, int NDIM, int NT>
 static cudaError_t dense_mma_one(const Problem& p, const SortPlan& sp, const void* go,
                                  float* gacc, cudaStream_t st) {
   if constexpr (sizeof(T) == 2) {
-    const int64_t grid = p.B * p.H * int64_t{sp.ndl} * sp.dchunks;
+    const int64_t grid = p.B * p.H * int64_t{sp.nml} * sp.dchunks;
     cudaError_t err = cudaFuncSetAttribute(msda_dense_mma_kernel<T, NDIM, NT>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, sp.dsmem);
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           sp.dsmem_mma);
     if (err != cudaSuccess) return err;
     msda_dense_mma_kernel<T, NDIM, NT>
-        <<<dim3(static_cast<unsigned>(grid)), kThreads, static_cast<size_t>(sp.dsmem), st>>>(
+        <<<dim3(static_cast<unsigned>(grid)), kThreads, static_cast<size_t>(sp.dsmem_mma), st>>>(
             p, sp, static_cast<const T*>(go), gacc);
     return cudaGetLastError();
   }
@@ -133,7 +134,7 @@ static cudaError_t sorted_chunk(const LaunchShape& ls, const LaunchShape& lsd, c
 #undef MSDA_SDOTS_CALL
     if (err != cudaSuccess) return err;
   }
-  if (sp.ndl > 0 && sp.dmma) {
+  if (sp.nml > 0) {
     switch (p.C) {
       case 16: err = dense_mma_one<T, NDIM, 2>(p, sp, go, gacc, st); break;
       case 32: err = dense_mma_one<T, NDIM, 4>(p, sp, go, gacc, st); break;
@@ -141,7 +142,8 @@ static cudaError_t sorted_chunk(const LaunchShape& ls, const LaunchShape& lsd, c
       default: return cudaErrorInvalidValue;
     }
     if (err != cudaSuccess) return err;
-  } else if (sp.ndl > 0) {
+  }
+  if (sp.ndl > 0) {
     switch (lsd.vb * 16 + lsd.vpl) {
       case 16 * 16 + 1: err = dense_one<T, NDIM, 16, 1>(p, sp, go, gacc, st); break;
       case 16 * 16 + 2: err = dense_one<T, NDIM, 16, 2>(p, sp, go, gacc, st); break;

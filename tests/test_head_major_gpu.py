@@ -50,6 +50,8 @@ PLANS = {
     "sorted-voxel": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "1e9"},
     "sorted-cell-sdots": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "0",
                           "MSDA_SORTED_DOTS_MB": "0"},
+    "sorted-cell-mma": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "0",
+                        "MSDA_DENSE_MMA_DENSITY": "0"},
     "sorted-auto-sdots": {"MSDA_BWD_PATH": "sorted", "MSDA_SORTED_DOTS_MB": "0",
                           "MSDA_SORTED_CHUNK_B": "1"},
 }
@@ -64,7 +66,7 @@ DTYPES = [torch.float32, torch.bfloat16, torch.float16]
 
 def _set_env(monkeypatch, plan):
     for k in ("MSDA_BWD_PATH", "MSDA_BWD_DIRECT16", "MSDA_VOXEL_DENSITY", "MSDA_SORTED_DOTS_MB",
-              "MSDA_SORTED_CHUNK_B"):
+              "MSDA_SORTED_CHUNK_B", "MSDA_DENSE_MMA_DENSITY"):
         monkeypatch.delenv(k, raising=False)
     for k, v in PLANS[plan].items():
         monkeypatch.setenv(k, v)

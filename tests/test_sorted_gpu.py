@@ -184,15 +184,17 @@ def test_workspace_reports_sorted_plan(monkeypatch):
 @pytest.mark.parametrize("case", CASES, ids=[f"{c[0]}d-{len(c[6])}lvl-q{c[2]}" for c in CASES])
 def test_dense_cuda_core_and_tensor_core_agree(monkeypatch, case, dtype):
     """16-bit values: the per-cell aggregation of dense levels on the tensor
-    cores (default, weights split into two 16-bit halves) and on the CUDA
-    cores (MSDA_DENSE_MMA=0) both meet the half-precision bar against the
-    oracle, with every level aggregated per cell."""
+    cores (weights split into two 16-bit halves; by default for levels with
+    at least 8 samples per cell, here for all) and on the CUDA cores
+    (MSDA_DENSE_MMA=0) both meet the half-precision bar against the oracle,
+    with every level aggregated per cell."""
     ndim, B, Q, H, C, P, shapes = case
     inp = _cast(make_inputs(B, Q, H, C, P, shapes, seed=3 * Q + C), dtype, dtype)
     ref = oracle_all(*_upcast(inp))
     for mma in ("1", "0"):
         _env(monkeypatch, "cell")
         monkeypatch.setenv("MSDA_DENSE_MMA", mma)
+        monkeypatch.setenv("MSDA_DENSE_MMA_DENSITY", "0")  # every dense level
         got = cuda_fwd_bwd(ndim, *inp)
         check_all(got, ref, TOL_HALF, TOL_HALF, f"{case} {dtype} dense mma={mma}")
 
