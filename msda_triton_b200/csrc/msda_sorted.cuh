@@ -1332,8 +1332,10 @@ __global__ void __launch_bounds__(kThreads)
   for (int cb = 0; cb < ncb; ++cb) {
     const int ch = cb * 32 + lane;
     const bool lact = ch < p.C;
-#pragma unroll 4
-    for (int v = 0; v < 32; ++v) acc[v * 32 + lane] = 0.0f;
+#pragma unroll
+    for (int v = lane; v < 32 * 32 / 4; v += 32)
+      reinterpret_cast<float4*>(acc)[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    __syncwarp();
     for (int32_t q0 = 0; q0 < total; q0 += sp.vcap) {
       const int nr = min(sp.vcap, total - q0);
       if (cb == 0 || total > sp.vcap) {
@@ -1407,14 +1409,36 @@ __global__ void __launch_bounds__(kThreads)
         }
       }
     }
-    if (wactive && lact) {
+    if (wactive) {
       const int32_t y = y0 + ry;
       const int64_t key0 = static_cast<int64_t>(p.lv.start[l]) + (static_cast<int64_t>(vz) * Hs + y) * W;
-      T* gvb = grad_value + bh_base(p, b, h, p.K) + ch;
       const int64_t ks = key_stride(p);
       const int nvox = min(32, W - xw);
-      for (int v = 0; v < nvox; ++v)
-        gvb[(key0 + xw + v) * ks] = Elem<T>::from_f(acc[v * 32 + lane]);
+      if (p.C % 32 == 0) {
+        // whole 32-channel blocks: lanes as (voxel, 8-channel chunk), one
+        // 8-element vector store per lane and voxel
+        __syncwarp();
+        const int vv = lane >> 2, qq = lane & 3;
+        T* gvb = grad_value + bh_base(p, b, h, p.K) + cb * 32 + qq * 8;
+#pragma unroll
+        for (int pass = 0; pass < 4; ++pass) {
+          const int v = pass * 8 + vv;
+          if (v < nvox) {
+            const float4 a0 = *reinterpret_cast<const float4*>(acc + v * 32 + qq * 8);
+            const float4 a1 = *reinterpret_cast<const float4*>(acc + v * 32 + qq * 8 + 4);
+            struct alignas(16) Oct { T e[8]; } o;
+            o.e[0] = Elem<T>::from_f(a0.x); o.e[1] = Elem<T>::from_f(a0.y);
+            o.e[2] = Elem<T>::from_f(a0.z); o.e[3] = Elem<T>::from_f(a0.w);
+            o.e[4] = Elem<T>::from_f(a1.x); o.e[5] = Elem<T>::from_f(a1.y);
+            o.e[6] = Elem<T>::from_f(a1.z); o.e[7] = Elem<T>::from_f(a1.w);
+            *reinterpret_cast<Oct*>(gvb + (key0 + xw + v) * ks) = o;
+          }
+        }
+      } else if (lact) {
+        T* gvb = grad_value + bh_base(p, b, h, p.K) + ch;
+        for (int v = 0; v < nvox; ++v)
+          gvb[(key0 + xw + v) * ks] = Elem<T>::from_f(acc[v * 32 + lane]);
+      }
     }
     if (cb + 1 < ncb) __syncwarp();
   }
