@@ -219,6 +219,42 @@ template <> struct Chunk<__half, 2> {
   }
 };
 
+// acc + <g, x> over one chunk's elements in element order, each product
+// exact and each step rounded once (an fp32 FMA on the widened operands).
+// 16-bit chunks use the mixed-precision FMA (fma.rn.f32.{bf16,f16}, sm_100),
+// which takes the 16-bit operands as they are: no unpacking.
+template <typename T, int VB> struct DotChunk {
+  static __device__ __forceinline__ float fma(const Raw<VB>& g, const Raw<VB>& x, float acc) {
+    float gf[Chunk<T, VB>::EPV], xf[Chunk<T, VB>::EPV];
+    Chunk<T, VB>::unpack(g, gf);
+    Chunk<T, VB>::unpack(x, xf);
+#pragma unroll
+    for (int e = 0; e < Chunk<T, VB>::EPV; ++e) acc = fmaf(gf[e], xf[e], acc);
+    return acc;
+  }
+};
+#define MSDA_MIXED_DOT(TY, SUF)                                                             \
+  template <int VB> struct DotChunk<TY, VB> {                                                \
+    static __device__ __forceinline__ float fma(const Raw<VB>& g, const Raw<VB>& x,          \
+                                                float acc) {                                \
+      _Pragma("unroll") for (int i = 0; i < VB / 4; ++i)                                    \
+        asm("{\n .reg .b16 gl, gh, xl, xh;\n mov.b32 {gl, gh}, %1;\n mov.b32 {xl, xh}, %2;\n" \
+            " fma.rn.f32." SUF " %0, gl, xl, %0;\n fma.rn.f32." SUF " %0, gh, xh, %0;\n}"  \
+            : "+f"(acc) : "r"(g.w[i]), "r"(x.w[i]));                                        \
+      return acc;                                                                            \
+    }                                                                                        \
+  };                                                                                         \
+  template <> struct DotChunk<TY, 2> {                                                       \
+    static __device__ __forceinline__ float fma(const Raw<2>& g, const Raw<2>& x,            \
+                                                float acc) {                                \
+      asm("fma.rn.f32." SUF " %0, %1, %2, %0;" : "+f"(acc) : "h"(g.h), "h"(x.h));            \
+      return acc;                                                                            \
+    }                                                                                        \
+  };
+MSDA_MIXED_DOT(__nv_bfloat16, "bf16")
+MSDA_MIXED_DOT(__half, "f16")
+#undef MSDA_MIXED_DOT
+
 // ---------------------------------------------------------------- levels
 struct LevelSmem {
   int32_t size[kMaxLevels][3];

@@ -413,15 +413,13 @@ __global__ void __launch_bounds__(kThreads, 4)
   bool has[VPL];
 #pragma unroll
   for (int v = 0; v < VPL; ++v) has[v] = j + v * G < p.nv;
-  float go[VPL][EPV];
+  Raw<VB> gor[VPL];  // the row's grad_out chunks
   {
     const char* gorow = reinterpret_cast<const char*>(grad_out) +
                         row * p.C * static_cast<int64_t>(sizeof(T));
 #pragma unroll
-    for (int v = 0; v < VPL; ++v) {
-      const Raw<VB> rg = has[v] ? ld_chunk<VB>(gorow + (j + v * G) * VB) : raw_zero<VB>();
-      CK::unpack(rg, go[v]);
-    }
+    for (int v = 0; v < VPL; ++v)
+      gor[v] = has[v] ? ld_chunk<VB>(gorow + (j + v * G) * VB) : raw_zero<VB>();
   }
   const DotLanes dl = dot_lanes(G, j, lane);
 
@@ -483,12 +481,7 @@ __global__ void __launch_bounds__(kThreads, 4)
             for (int c = 0; c < NC; ++c) {
               float dot = 0.0f;
 #pragma unroll
-              for (int vv = 0; vv < VPL; ++vv) {
-                float x[EPV];
-                CK::unpack(raw[c][vv], x);
-#pragma unroll
-                for (int e = 0; e < EPV; ++e) dot = fmaf(go[vv][e], x[e], dot);
-              }
+              for (int vv = 0; vv < VPL; ++vv) dot = DotChunk<T, VB>::fma(gor[vv], raw[c][vv], dot);
               D[c] = dot;
             }
             corner_dot_grads<NDIM>(D, m.f, v + 4 * i);
@@ -626,16 +619,13 @@ __global__ void __launch_bounds__(kThreads, 4)
         const uint32_t grow = __shfl_sync(0xffffffffu, my_row, t, G);
         const uint32_t gidx = __shfl_sync(0xffffffffu, my_idx, t, G);
         if (t < nr) {
-          float go[VPL][EPV];
+          Raw<VB> gor[VPL];
           {
             const char* gorow = reinterpret_cast<const char*>(grad_out) +
                                 static_cast<int64_t>(grow) * p.C * e;
 #pragma unroll
-            for (int vv = 0; vv < VPL; ++vv) {
-              const Raw<VB> rg =
-                  has[vv] ? ld_chunk<VB>(gorow + (j + vv * G) * VB) : raw_zero<VB>();
-              CK::unpack(rg, go[vv]);
-            }
+            for (int vv = 0; vv < VPL; ++vv)
+              gor[vv] = has[vv] ? ld_chunk<VB>(gorow + (j + vv * G) * VB) : raw_zero<VB>();
           }
           Raw<VB> raw[NC][VPL];
           gather_meta_corners<T, NDIM, VB, VPL>(p, m, g, vbase, key_bytes, j * VB, G, has, raw);
@@ -644,12 +634,7 @@ __global__ void __launch_bounds__(kThreads, 4)
           for (int c = 0; c < NC; ++c) {
             float dot = 0.0f;
 #pragma unroll
-            for (int vv = 0; vv < VPL; ++vv) {
-              float x[EPV];
-              CK::unpack(raw[c][vv], x);
-#pragma unroll
-              for (int ee = 0; ee < EPV; ++ee) dot = fmaf(go[vv][ee], x[ee], dot);
-            }
+            for (int vv = 0; vv < VPL; ++vv) dot = DotChunk<T, VB>::fma(gor[vv], raw[c][vv], dot);
             D[c] = dot;
           }
           corner_dot_grads<NDIM>(D, m.f, v + 4 * i);
