@@ -770,36 +770,45 @@ static __global__ void __launch_bounds__(kScanThreads)
 static __global__ void __launch_bounds__(kScanThreads)
     msda_scan_down_kernel(int32_t* __restrict__ data, int64_t n, const int32_t* __restrict__ bsum,
                           int32_t nblk) {
-  __shared__ int32_t tile[kScanTile];
   __shared__ int32_t wt[kScanThreads / 32];
+  // each thread scans kScanPer consecutive counts: four 16-byte loads and
+  // stores when the tile is whole (tiles start 16 KB apart in a 256-byte
+  // aligned buffer)
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile;
-#pragma unroll
-  for (int i = 0; i < kScanPer; ++i) {
-    const int idx = i * kScanThreads + threadIdx.x;
-    const int64_t k = base + idx;
-    tile[idx] = k < n ? data[k] : 0;
-  }
-  __syncthreads();
+  const int64_t e0 = base + static_cast<int64_t>(threadIdx.x) * kScanPer;
+  const bool whole = base + kScanTile <= n;
   int32_t loc[kScanPer];
+  if (whole) {
+    const int4* src = reinterpret_cast<const int4*>(data + e0);
+#pragma unroll
+    for (int q = 0; q < kScanPer / 4; ++q) {
+      const int4 v = src[q];
+      loc[4 * q] = v.x; loc[4 * q + 1] = v.y; loc[4 * q + 2] = v.z; loc[4 * q + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kScanPer; ++i) loc[i] = e0 + i < n ? data[e0 + i] : 0;
+  }
   int32_t sum = 0;
 #pragma unroll
-  for (int i = 0; i < kScanPer; ++i) {
-    loc[i] = tile[threadIdx.x * kScanPer + i];
-    sum += loc[i];
-  }
+  for (int i = 0; i < kScanPer; ++i) sum += loc[i];
   int32_t total;
   int32_t run = block_exclusive_scan(sum, wt, total) + bsum[blockIdx.x];
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
-    tile[threadIdx.x * kScanPer + i] = run;
-    run += loc[i];
+    const int32_t c = loc[i];
+    loc[i] = run;
+    run += c;
   }
-  __syncthreads();
+  if (whole) {
+    int4* dst = reinterpret_cast<int4*>(data + e0);
 #pragma unroll
-  for (int i = 0; i < kScanPer; ++i) {
-    const int idx = i * kScanThreads + threadIdx.x;
-    const int64_t k = base + idx;
-    if (k < n) data[k] = tile[idx];
+    for (int q = 0; q < kScanPer / 4; ++q)
+      dst[q] = make_int4(loc[4 * q], loc[4 * q + 1], loc[4 * q + 2], loc[4 * q + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < kScanPer; ++i)
+      if (e0 + i < n) data[e0 + i] = loc[i];
   }
   if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) data[n] = bsum[nblk];
 }
