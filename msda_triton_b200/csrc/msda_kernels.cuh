@@ -843,4 +843,36 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// The same rounding as msda_compact_cast_kernel, one (batch entry[, head],
+// level) span per blockIdx.y: the accumulator rows of a level and its
+// grad_value rows are each one contiguous range (rows of H*C elements, or C
+// head-major), so a span is a plain streaming cast of float4 -> 4 elements.
+// Needs rows of a multiple of 4 elements and grad_value 8-byte aligned.
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    msda_span_cast_kernel(const Problem p, const float* __restrict__ acc, T* __restrict__ gv) {
+  const int l = static_cast<int>(blockIdx.y % static_cast<uint32_t>(p.L));
+  const int64_t bh = blockIdx.y / static_cast<uint32_t>(p.L);
+  if ((p.direct16 >> l) & 1) return;  // a level the accumulator does not hold
+  const int64_t b = p.head_major ? bh / p.H : bh;
+  const int64_t h = p.head_major ? bh - b * p.H : 0;
+  const int64_t row = key_stride(p);
+  const int64_t nvox = int64_t{p.lv.size[l][0]} * p.lv.size[l][1] * p.lv.size[l][2];
+  const float4* src = reinterpret_cast<const float4*>(
+      acc + bh_base(p, b, h, p.acc_keys) + int64_t{p.acc_start[l]} * row);
+  T* dst = gv + bh_base(p, b, h, p.K) + int64_t{p.lv.start[l]} * row;
+  const int64_t n4 = nvox * row / 4;
+  struct alignas(8) Quad { T e[4]; };
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const float4 v = src[i];
+    Quad o;
+    o.e[0] = Elem<T>::from_f(v.x);
+    o.e[1] = Elem<T>::from_f(v.y);
+    o.e[2] = Elem<T>::from_f(v.z);
+    o.e[3] = Elem<T>::from_f(v.w);
+    reinterpret_cast<Quad*>(dst)[i] = o;
+  }
+}
+
 }  // namespace msda

@@ -137,6 +137,20 @@ cudaError_t launch_compact_cast(const Problem& p, const float* acc, void* gv, cu
   const bool vec = row % 4 == 0 && reinterpret_cast<uintptr_t>(gv) % 8 == 0;
   const int64_t nrows = p.B * p.acc_keys * (p.head_major ? p.H : 1);
   if (nrows <= 0 || row <= 0) return cudaSuccess;
+  // host-resolved levels: one streaming span per (batch entry[, head], level)
+  const int64_t spans = p.B * (p.head_major ? p.H : 1) * p.L;
+  if (vec && p.shapes_dev == nullptr && spans > 0 && spans <= 65535) {
+    int64_t maxn4 = 0;
+    for (int64_t l = 0; l < p.L; ++l)
+      maxn4 = std::max<int64_t>(
+          maxn4, int64_t{p.lv.size[l][0]} * p.lv.size[l][1] * p.lv.size[l][2] * row / 4);
+    // about 8 float4 per thread on the largest level, at most 16 waves
+    int64_t bx = (maxn4 + kThreads * 8 - 1) / (kThreads * 8);
+    bx = std::max<int64_t>(1, std::min<int64_t>(bx, (148 * 16 + spans - 1) / spans * 4));
+    msda_span_cast_kernel<T><<<dim3(static_cast<unsigned>(bx), static_cast<unsigned>(spans)),
+                               kThreads, 0, st>>>(p, acc, static_cast<T*>(gv));
+    return cudaGetLastError();
+  }
   int64_t blocks = (nrows + kThreads / 32 - 1) / (kThreads / 32);  // a grid-stride loop covers the rest
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (vec)
