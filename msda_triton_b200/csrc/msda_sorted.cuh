@@ -518,23 +518,21 @@ __global__ void __launch_bounds__(kThreads, 4)
   constexpr int EPV = CK::EPV;
   constexpr int NC = 1 << NDIM;
   constexpr int NV = kDotBatch * 4;
-  // CTA -> (b, level, stretch, h) with h fastest: the heads' rows of a key
-  // share value lines.  Head-major value: (b, level, h, stretch), one head's
-  // slice of the level at a time.
+  // CTA -> (b, level, head group, stretch, head in group), fastest last:
+  // the heads of a group (p.hg: those whose rows share 128-byte value lines;
+  // one head for a head-major value) walk the same stretch of positions
+  // together, and one group's value lines and grad_out rows (a quarter of
+  // the batch entry's for groups of 2 of 8 heads) stay in L2.
   uint32_t u = blockIdx.x;
-  const uint32_t H = static_cast<uint32_t>(p.H), nch = static_cast<uint32_t>(sp.sd_chunks);
-  int32_t h, k;
-  if (p.head_major) {
-    k = static_cast<int32_t>(u % nch);
-    u /= nch;
-    h = static_cast<int32_t>(u % H);
-    u /= H;
-  } else {
-    h = static_cast<int32_t>(u % H);
-    u /= H;
-    k = static_cast<int32_t>(u % nch);
-    u /= nch;
-  }
+  const uint32_t nch = static_cast<uint32_t>(sp.sd_chunks);
+  const uint32_t hgs = p.head_major ? 1u : static_cast<uint32_t>(p.hg);
+  const uint32_t ngrp = static_cast<uint32_t>(p.H) / hgs;
+  const uint32_t hi = u % hgs;
+  u /= hgs;
+  const int32_t k = static_cast<int32_t>(u % nch);
+  u /= nch;
+  const int32_t h = static_cast<int32_t>((u % ngrp) * hgs + hi);
+  u /= ngrp;
   const int32_t li = static_cast<int32_t>(u % static_cast<uint32_t>(sp.nsl));
   const int64_t b = u / static_cast<uint32_t>(sp.nsl);
   const int l = sp.sl_level[li];
