@@ -511,7 +511,10 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   const int64_t bounds_max = int64_t{4} * (tile_max + 2) * 4 + 4 * 64;
   const int64_t acc_bytes = int64_t{kThreads / 32} * 32 * 32 * 4;
   // per staged sample: its record (32 B), cell row / x offset (4 B), grad_out row
-  int64_t cap = (72 * 1024 - acc_bytes - bounds_max) / (36 + row_bytes);
+  // MSDA_VOXEL_SMEM_KB (tuning): the voxel kernel's shared-memory budget
+  const char* vs_env = std::getenv("MSDA_VOXEL_SMEM_KB");
+  const int64_t vbudget = (vs_env && std::atoll(vs_env) > 0 ? std::atoll(vs_env) : 72) * 1024;
+  int64_t cap = (vbudget - acc_bytes - bounds_max) / (36 + row_bytes);
   cap = std::min<int64_t>(cap, kVoxelCap) & ~int64_t{1};
   if (cap < 16) max_dens = -1.0;
   SortPlan sp{};
