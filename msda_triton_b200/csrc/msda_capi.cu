@@ -500,16 +500,25 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   if (!forced && (!kSortedByDefault || samples < kSortedMinSamples)) return false;
   const char* dens_env = std::getenv("MSDA_VOXEL_DENSITY");
   double max_dens = dens_env ? std::atof(dens_env) : kVoxelMaxDensity;
-  // The voxel kernel takes the forward's lane shape (16-byte chunks where the
-  // row allows); shapes it is not instantiated for keep every level dense.
-  if (!((ls.vb == 16 && ls.vpl <= 4) || ((ls.vb == 4 || ls.vb == 2) && ls.vpl == 1)))
+  // 16-bit values with C = 16, 32 or 64 form the voxel levels on the tensor
+  // cores (msda_voxel_mma_kernel; MSDA_VOXEL_MMA=0: msda_voxel_kernel).
+  const char* vm_env = std::getenv("MSDA_VOXEL_MMA");
+  const bool vmma = dtype_bytes(a.vdt) == 2 && (a.C == 16 || a.C == 32 || a.C == 64) &&
+                    !(vm_env && std::strcmp(vm_env, "0") == 0);
+  // msda_voxel_kernel takes the forward's lane shape (16-byte chunks where
+  // the row allows); shapes it is not instantiated for keep every level dense.
+  if (!vmma && !((ls.vb == 16 && ls.vpl <= 4) || ((ls.vb == 4 || ls.vb == 2) && ls.vpl == 1)))
     max_dens = -1.0;
   const int tile_max = (kThreads / 32) * 32;         // voxels per voxel-kernel CTA (a warp per 32)
   const int64_t row_bytes = a.C * dtype_bytes(a.vdt);
   // samples the voxel kernel stages per round: as many as fit next to the
-  // warps' accumulators (32 KB) and the range bounds in 72 KB, at most 512
+  // warps' areas (fp32 accumulators, 32 KB; or the tensor-core kernel's
+  // 16-bit weight tiles and the zero row) and the range bounds in 72 KB, at
+  // most 512
   const int64_t bounds_max = int64_t{4} * (tile_max + 2) * 4 + 4 * 64;
-  const int64_t acc_bytes = int64_t{kThreads / 32} * 32 * 32 * 4;
+  const int64_t acc_bytes =
+      vmma ? 32 + int64_t{kThreads / 32} * vm_warp_bytes(static_cast<int>(a.C / 8))
+           : int64_t{kThreads / 32} * 32 * 32 * 4;
   // per staged sample: its record (32 B), cell row / x offset (4 B), grad_out row
   // MSDA_VOXEL_SMEM_KB (tuning): the voxel kernel's shared-memory budget
   const char* vs_env = std::getenv("MSDA_VOXEL_SMEM_KB");
@@ -617,6 +626,7 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   sp.vnv = p.nv;
   sp.div_nv = make_fdiv(static_cast<uint32_t>(std::max<int32_t>(p.nv, 1)));
   sp.vsmem = static_cast<int32_t>(acc_bytes + cap * (36 + row_bytes) + max_bounds * 4);
+  sp.vmma = vmma ? 1 : 0;
   if (nvl > 0 && sp.vsmem > 100 * 1024) return false;
   sp.div_lp = make_fdiv(static_cast<uint32_t>(a.L * a.P));
   sp.div_p = make_fdiv(static_cast<uint32_t>(a.P));

@@ -32,6 +32,7 @@
 //   msda_sdots_finish_kernel  ... staged, then written out in query order
 //   msda_dense_kernel      dense-level value gradient, per cell segment
 //   msda_voxel_kernel      sparse-level value gradient, gathered per value row
+//                          (msda_voxel_mma_kernel: the same on the tensor cores)
 //
 // Cells.  A sample at level l falls in the cell of its lower corner
 // (i0x, i0y[, i0z]) with each i0 in [-1, size-1] (grid_sample's corner
@@ -108,6 +109,7 @@ struct SortPlan {
   int32_t vnv;                     // msda_voxel_kernel: VB-byte chunks per channel row
   FastDiv div_nv;                  // / vnv
   int32_t vsmem;                   // its dynamic shared memory
+  int32_t vmma;                    // voxel levels on msda_voxel_mma_kernel instead (16-bit, C = 16/32/64)
   FastDiv div_lp, div_p, div_h, div_l, div_q;
   int32_t sdots_mask;              // levels whose dot products msda_sdots_kernel takes in sorted order
   int32_t nsl;                     // such levels
@@ -1026,6 +1028,20 @@ template <> struct MmaT<__nv_bfloat16> {
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
   }
+  // all four A registers (rows 0-15)
+  static __device__ __forceinline__ void mma4(float* d, const uint32_t* a, uint32_t b0,
+                                              uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  // two values rounded to the 16-bit type, the first in the low half
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
 };
 template <> struct MmaT<__half> {
   static __device__ __forceinline__ uint16_t bits(float x) {
@@ -1041,6 +1057,20 @@ template <> struct MmaT<__half> {
         "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+  }
+  // all four A registers (rows 0-15)
+  static __device__ __forceinline__ void mma4(float* d, const uint32_t* a, uint32_t b0,
+                                              uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  // two values rounded to the 16-bit type, the first in the low half
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
   }
 };
 
@@ -1240,21 +1270,140 @@ __global__ void __launch_bounds__(kThreads, 4)
 
 // ------------------------------------------------------------------ voxel gather
 // Value gradient of the sparse levels.  One CTA per tile of NY voxel rows x TX
-// voxels at one (b, h, level, z); one warp per 32-voxel segment of a row,
-// lanes over channels.  Voxel (x, y, z) is a corner of the cells with lower
-// corner (x-1 or x, y-1 or y, z-1 or z), so the tile's samples lie in the
-// cell rows (y', z') = (y0-1 .. y0+NY-1, z-1 .. z), each row's cells
-// x0-1 .. x0+TX-1 being one contiguous range of the sorted records.  The CTA
-// stages, in rounds of sp.vcap samples (cp.async: three memory round trips):
-// the range bounds, the records -- turned into their four (bx, by) corner
-// weights a * w (the reference's product order) and their cell's x offset --
-// and their grad_out rows.  A warp then walks, for each of the 2^(d-1) cell
-// rows its voxel row touches, the samples of the 33 cells around its
-// segment, every lane adding its channel's a * w * grad_out to the sample's
-// two x-corners in a warp-private fp32 accumulator in shared memory (the
-// lanes of a row hit 32 distinct banks).  Each voxel row is stored once.
-// The work follows the number of samples, not the busiest voxel.
+// voxels at one (b, h, level, z); one warp per 32-voxel segment of a row.
+// Voxel (x, y, z) is a corner of the cells with lower corner (x-1 or x, y-1
+// or y, z-1 or z), so the tile's samples lie in the cell rows (y', z') =
+// (y0-1 .. y0+NY-1, z-1 .. z), each row's cells x0-1 .. x0+TX-1 being one
+// contiguous range of the sorted records.  The CTA stages, in rounds of
+// sp.vcap samples (cp.async: three memory round trips): the range bounds, the
+// records -- turned into their four (bx, by) corner weights a * w (the
+// reference's product order) and their cell's x offset -- and their grad_out
+// rows.  Each voxel row is stored once: no reductions, no zero-fill.
 
+// The voxel-kernel unit: (b, h, voxel level, z, y tile, x tile) and its cell rows.
+struct VoxUnit {
+  uint32_t bh;
+  int32_t b, h, l;
+  VoxTile vt;
+  int32_t W, Hs;       // level size along x and y
+  int32_t x0, y0, vz;  // the tile's first voxel
+  int32_t cxn, cyn;    // cells along x and y
+  int32_t kb;          // the level's first bucket key inside the (b, h) block
+  int32_t nyr, ncr;    // cell rows per z, cell rows
+  int32_t cw;          // range bounds per cell row
+};
+
+template <int NDIM>
+__device__ __forceinline__ VoxUnit voxel_unit(const Problem& p, const SortPlan& sp) {
+  VoxUnit U;
+  const uint32_t u = blockIdx.x;
+  U.bh = u / static_cast<uint32_t>(sp.units_per_bh);
+  uint32_t rem = u - U.bh * static_cast<uint32_t>(sp.units_per_bh);
+  int k = 0;
+  while (k + 1 < sp.nvl && rem >= static_cast<uint32_t>(sp.vl_ubase[k + 1])) ++k;
+  rem -= static_cast<uint32_t>(sp.vl_ubase[k]);
+  U.l = sp.vl_level[k];
+  U.vt = sp.vl_tile[k];
+  U.W = p.lv.size[U.l][0];
+  U.Hs = p.lv.size[U.l][1];
+  const uint32_t xt = rem % static_cast<uint32_t>(U.vt.ntx);
+  const uint32_t r2 = rem / static_cast<uint32_t>(U.vt.ntx);
+  const uint32_t yt = r2 % static_cast<uint32_t>(U.vt.nty);
+  U.vz = static_cast<int32_t>(r2 / static_cast<uint32_t>(U.vt.nty));
+  U.x0 = static_cast<int32_t>(xt) * U.vt.tx;
+  U.y0 = static_cast<int32_t>(yt) * U.vt.ny;
+  U.b = static_cast<int32_t>(U.bh / static_cast<uint32_t>(p.H));
+  U.h = static_cast<int32_t>(U.bh - static_cast<uint32_t>(U.b) * static_cast<uint32_t>(p.H));
+  U.cxn = sp.cells[U.l][0];
+  U.cyn = sp.cells[U.l][1];
+  U.kb = static_cast<int32_t>(U.bh) * sp.seg_keys + sp.lvl_base[U.l];
+  U.nyr = U.vt.ny + 1;
+  U.ncr = (NDIM == 3 ? 2 : 1) * U.nyr;
+  U.cw = U.vt.tx + 2;
+  return U;
+}
+
+// The unit's range bounds, cnt_s[cr][c] = start of cell x0-1+c of cell row cr
+// (cr = dz * nyr + row, the row's lower corner y0-1+row at z - dz), and the
+// cell rows' offsets in the staged order, off_s[0..ncr].  Returns the unit's
+// sample count.  Ends with the CTA synchronised.
+template <int NDIM>
+__device__ __forceinline__ int32_t voxel_bounds(const SortPlan& sp, const VoxUnit& U,
+                                                int32_t* cnt_s, int32_t* off_s) {
+  for (int cr = 0; cr < U.ncr; ++cr) {
+    const int dz = (NDIM == 3 && cr >= U.nyr) ? 1 : 0;
+    const int32_t yc = U.y0 - 1 + (cr - dz * U.nyr);  // the cell row's i0y
+    const int32_t zc = NDIM == 3 ? U.vz - dz : -1;
+    const int32_t krow = U.kb + ((zc + 1) * U.cyn + (yc + 1)) * U.cxn;
+    for (int c = threadIdx.x; c < U.cw; c += kThreads) {
+      if (yc <= U.Hs - 1)  // past the row end: its end bound
+        cp_async<4>(cnt_s + cr * U.cw + c, sp.cnt + krow + min(U.x0 + c, U.cxn));
+      else
+        cnt_s[cr * U.cw + c] = 0;  // rows outside the level are empty
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t o = 0;
+    for (int cr = 0; cr < U.ncr; ++cr) {
+      off_s[cr] = o;
+      o += cnt_s[cr * U.cw + U.cw - 1] - cnt_s[cr * U.cw];
+    }
+    off_s[U.ncr] = o;
+  }
+  __syncthreads();
+  return off_s[U.ncr];
+}
+
+// First staging phase of a round: the records of staged positions q0 ..
+// q0+nr-1 (cp.async) and each one's cell row in lo_s.
+__device__ __forceinline__ void voxel_stage_records(const SortPlan& sp, const VoxUnit& U,
+                                                    int32_t q0, int nr, SRec* rec_s,
+                                                    int32_t* lo_s, const int32_t* cnt_s,
+                                                    const int32_t* off_s) {
+  for (int q = threadIdx.x; q < nr; q += kThreads) {
+    const int32_t qq = q0 + q;
+    int lo = 0, hi = U.ncr;  // cell row: off_s[lo] <= qq < off_s[lo + 1]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (off_s[mid] <= qq) lo = mid; else hi = mid;
+    }
+    lo_s[q] = lo;
+    const SRec* src = sp.srec + cnt_s[lo * U.cw] + (qq - off_s[lo]);
+    cp_async<16>(reinterpret_cast<char*>(rec_s + q), src);
+    cp_async<16>(reinterpret_cast<char*>(rec_s + q) + 16, reinterpret_cast<const char*>(src) + 16);
+  }
+}
+
+// A staged record of cell row cr: its four (bx, by) corner weights a * w at
+// the unit's z plane -- (bx, by) = (0, 0), (0, 1), (1, 0), (1, 1) -- and its
+// cell's x offset in the tile (cell i0x = x0 + offset - 1).
+template <int NDIM>
+__device__ __forceinline__ float4 voxel_weights(const SRec& rec, int cr, const VoxUnit& U,
+                                                int32_t& xoff) {
+  const int dz = (NDIM == 3 && cr >= U.nyr) ? 1 : 0;
+  const int32_t yc = U.y0 - 1 + (cr - dz * U.nyr);
+  const int32_t zc = NDIM == 3 ? U.vz - dz : -1;
+  xoff = rec.key - (U.kb + ((zc + 1) * U.cyn + (yc + 1)) * U.cxn) - U.x0;
+  const float wx0 = __fsub_rn(1.0f, rec.f[0]), wx1 = rec.f[0];
+  const float wy0 = __fsub_rn(1.0f, rec.f[1]), wy1 = rec.f[1];
+  float w00 = __fmul_rn(wx0, wy0), w01 = __fmul_rn(wx0, wy1);
+  float w10 = __fmul_rn(wx1, wy0), w11 = __fmul_rn(wx1, wy1);
+  if (NDIM == 3) {
+    const float wz = dz ? rec.f[2] : __fsub_rn(1.0f, rec.f[2]);
+    w00 = __fmul_rn(w00, wz); w01 = __fmul_rn(w01, wz);
+    w10 = __fmul_rn(w10, wz); w11 = __fmul_rn(w11, wz);
+  }
+  return make_float4(rec.a * w00, rec.a * w01, rec.a * w10, rec.a * w11);
+}
+
+// msda_voxel_kernel: a warp per 32-voxel row segment, lanes over channels.
+// A warp walks, for each of the 2^(d-1) cell rows its voxel row touches, the
+// samples of the 33 cells around its segment, every lane adding its
+// channel's a * w * grad_out to the sample's two x-corners in a warp-private
+// fp32 accumulator in shared memory (the lanes of a row hit 32 distinct
+// banks).  The work follows the number of samples, not the busiest voxel.
 template <typename T, int NDIM, int VB, int VPL>
 __global__ void __launch_bounds__(kThreads)
     msda_voxel_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
@@ -1265,69 +1414,23 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t row_bytes = p.C * static_cast<int64_t>(sizeof(T));
   const int rowb = static_cast<int>(row_bytes);
   const int nv = sp.vnv;  // VB-byte chunks per row (staging)
-
-  // unit -> (b, h, voxel level, z, y tile, x tile)
-  const uint32_t u = blockIdx.x;
-  const uint32_t bh = u / static_cast<uint32_t>(sp.units_per_bh);
-  uint32_t rem = u - bh * static_cast<uint32_t>(sp.units_per_bh);
-  int k = 0;
-  while (k + 1 < sp.nvl && rem >= static_cast<uint32_t>(sp.vl_ubase[k + 1])) ++k;
-  rem -= static_cast<uint32_t>(sp.vl_ubase[k]);
-  const int l = sp.vl_level[k];
-  const VoxTile vt = sp.vl_tile[k];
-  const int32_t W = p.lv.size[l][0], Hs = p.lv.size[l][1];
-  const uint32_t xt = rem % static_cast<uint32_t>(vt.ntx);
-  const uint32_t r2 = rem / static_cast<uint32_t>(vt.ntx);
-  const uint32_t yt = r2 % static_cast<uint32_t>(vt.nty);
-  const int32_t vz = static_cast<int32_t>(r2 / static_cast<uint32_t>(vt.nty));
-  const int32_t x0 = static_cast<int32_t>(xt) * vt.tx;
-  const int32_t y0 = static_cast<int32_t>(yt) * vt.ny;
-  const int32_t b = static_cast<int32_t>(bh / static_cast<uint32_t>(p.H));
-  const int32_t h = static_cast<int32_t>(bh - static_cast<uint32_t>(b) * static_cast<uint32_t>(p.H));
-  const int32_t cxn = sp.cells[l][0], cyn = sp.cells[l][1];
-  const int32_t kb = static_cast<int32_t>(bh) * sp.seg_keys + sp.lvl_base[l];
-  const int nyr = vt.ny + 1;                       // cell rows per z
-  const int ncr = (NDIM == 3 ? 2 : 1) * nyr;       // cell rows
-  const int cw = vt.tx + 2;                        // bounds per cell row
+  const VoxUnit U = voxel_unit<NDIM>(p, sp);
+  const int32_t W = U.W, Hs = U.Hs, x0 = U.x0, y0 = U.y0, vz = U.vz;
+  const int nyr = U.nyr, cw = U.cw;
 
   float* acc_s = reinterpret_cast<float*>(vsm);                       // warps x 32 voxels x 32 lanes
   SRec* rec_s = reinterpret_cast<SRec*>(vsm + (kThreads / 32) * 32 * 32 * sizeof(float));  // vcap
   unsigned char* go_s = reinterpret_cast<unsigned char*>(rec_s + sp.vcap);               // vcap * rowb
   int32_t* lo_s = reinterpret_cast<int32_t*>(go_s + static_cast<size_t>(sp.vcap) * rowb);
   int32_t* cnt_s = lo_s + sp.vcap;                                    // ncr * cw
-  int32_t* off_s = cnt_s + ncr * cw;                                  // ncr + 1
-
-  // range bounds: cnt_s[cr][c] = start of cell x0-1+c of cell row cr
-  for (int cr = 0; cr < ncr; ++cr) {
-    const int dz = (NDIM == 3 && cr >= nyr) ? 1 : 0;
-    const int32_t yc = y0 - 1 + (cr - dz * nyr);  // the cell row's i0y
-    const int32_t zc = NDIM == 3 ? vz - dz : -1;
-    const int32_t krow = kb + ((zc + 1) * cyn + (yc + 1)) * cxn;
-    for (int c = threadIdx.x; c < cw; c += kThreads) {
-      if (yc <= Hs - 1)  // past the row end: its end bound
-        cp_async<4>(cnt_s + cr * cw + c, sp.cnt + krow + min(x0 + c, cxn));
-      else
-        cnt_s[cr * cw + c] = 0;  // rows outside the level are empty
-    }
-  }
-  cp_async_wait_all();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int32_t o = 0;
-    for (int cr = 0; cr < ncr; ++cr) {
-      off_s[cr] = o;
-      o += cnt_s[cr * cw + cw - 1] - cnt_s[cr * cw];
-    }
-    off_s[ncr] = o;
-  }
-  __syncthreads();
-  const int32_t total = off_s[ncr];
+  int32_t* off_s = cnt_s + U.ncr * cw;                                // ncr + 1
+  const int32_t total = voxel_bounds<NDIM>(sp, U, cnt_s, off_s);
 
   // this warp's 32-voxel segment
-  const int segs = (vt.tx + 31) / 32;
+  const int segs = (U.vt.tx + 31) / 32;
   const int ry = warp / segs, sgi = warp - ry * segs;
   const int32_t xw = x0 + sgi * 32;  // first voxel of the segment
-  const bool wactive = ry < vt.ny && y0 + ry < Hs && xw < W;
+  const bool wactive = ry < U.vt.ny && y0 + ry < Hs && xw < W;
   float* acc = acc_s + warp * 32 * 32;
 
   const int ncb = (static_cast<int>(p.C) + 31) / 32;  // 32-channel blocks
@@ -1344,39 +1447,14 @@ __global__ void __launch_bounds__(kThreads)
         // stage the round: records, then per record its four (bx, by) corner
         // weights in place of (a, f), its cell's x offset and its grad_out row
         if (q0 > 0 || cb > 0) __syncthreads();
-        for (int q = threadIdx.x; q < nr; q += kThreads) {
-          const int32_t qq = q0 + q;
-          int lo = 0, hi = ncr;  // cell row: off_s[lo] <= qq < off_s[lo + 1]
-          while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (off_s[mid] <= qq) lo = mid; else hi = mid;
-          }
-          lo_s[q] = lo;
-          const SRec* src = sp.srec + cnt_s[lo * cw] + (qq - off_s[lo]);
-          cp_async<16>(reinterpret_cast<char*>(rec_s + q), src);
-          cp_async<16>(reinterpret_cast<char*>(rec_s + q) + 16, reinterpret_cast<const char*>(src) + 16);
-        }
+        voxel_stage_records(sp, U, q0, nr, rec_s, lo_s, cnt_s, off_s);
         cp_async_wait_all();
         __syncthreads();
         for (int q = threadIdx.x; q < nr; q += kThreads) {
           const SRec rec = rec_s[q];
-          const int lo = lo_s[q];
-          const int dz = (NDIM == 3 && lo >= nyr) ? 1 : 0;
-          const int32_t yc = y0 - 1 + (lo - dz * nyr);
-          const int32_t zc = NDIM == 3 ? vz - dz : -1;
-          // the cell's x offset in the tile: shifted cell index - x0 (cell i0x = x0 + c - 1)
-          lo_s[q] = rec.key - (kb + ((zc + 1) * cyn + (yc + 1)) * cxn) - x0;
-          const float wx0 = __fsub_rn(1.0f, rec.f[0]), wx1 = rec.f[0];
-          const float wy0 = __fsub_rn(1.0f, rec.f[1]), wy1 = rec.f[1];
-          float w00 = __fmul_rn(wx0, wy0), w01 = __fmul_rn(wx0, wy1);
-          float w10 = __fmul_rn(wx1, wy0), w11 = __fmul_rn(wx1, wy1);
-          if (NDIM == 3) {
-            const float wz = dz ? rec.f[2] : __fsub_rn(1.0f, rec.f[2]);
-            w00 = __fmul_rn(w00, wz); w01 = __fmul_rn(w01, wz);
-            w10 = __fmul_rn(w10, wz); w11 = __fmul_rn(w11, wz);
-          }
-          *reinterpret_cast<float4*>(rec_s + q) =
-              make_float4(rec.a * w00, rec.a * w01, rec.a * w10, rec.a * w11);
+          int32_t xoff;
+          *reinterpret_cast<float4*>(rec_s + q) = voxel_weights<NDIM>(rec, lo_s[q], U, xoff);
+          lo_s[q] = xoff;
           for (int c = 0; c < nv; ++c)
             stage_chunk<VB>(go_s + static_cast<size_t>(q) * rowb + c * VB,
                             reinterpret_cast<const char*>(grad_out) +
@@ -1413,7 +1491,7 @@ __global__ void __launch_bounds__(kThreads)
     }
     if (wactive) {
       const int32_t y = y0 + ry;
-      const int64_t key0 = static_cast<int64_t>(p.lv.start[l]) + (static_cast<int64_t>(vz) * Hs + y) * W;
+      const int64_t key0 = static_cast<int64_t>(p.lv.start[U.l]) + (static_cast<int64_t>(vz) * Hs + y) * W;
       const int64_t ks = key_stride(p);
       const int nvox = min(32, W - xw);
       if (p.C % 32 == 0) {
@@ -1421,7 +1499,7 @@ __global__ void __launch_bounds__(kThreads)
         // 8-element vector store per lane and voxel
         __syncwarp();
         const int vv = lane >> 2, qq = lane & 3;
-        T* gvb = grad_value + bh_base(p, b, h, p.K) + cb * 32 + qq * 8;
+        T* gvb = grad_value + bh_base(p, U.b, U.h, p.K) + cb * 32 + qq * 8;
 #pragma unroll
         for (int pass = 0; pass < 4; ++pass) {
           const int v = pass * 8 + vv;
@@ -1437,12 +1515,238 @@ __global__ void __launch_bounds__(kThreads)
           }
         }
       } else if (lact) {
-        T* gvb = grad_value + bh_base(p, b, h, p.K) + ch;
+        T* gvb = grad_value + bh_base(p, U.b, U.h, p.K) + ch;
         for (int v = 0; v < nvox; ++v)
           gvb[(key0 + xw + v) * ks] = Elem<T>::from_f(acc[v * 32 + lane]);
       }
     }
     if (cb + 1 < ncb) __syncwarp();
+  }
+}
+
+// ------------------------------------------------------------------ voxel levels, tensor cores
+// The same value gradient for 16-bit values with C = 8 * NT channels (NT 2,
+// 4 or 8) as small products on the tensor cores.  A warp's 32-voxel row
+// segment gets
+//   G[v][ch] = sum over the samples s of its 2^(d-1) cell rows of A[v][s] * go[s][ch]
+// with A[v][s] = a * w of sample s's corner at voxel v: two entries per
+// sample (its lower and upper x-corner in this row), zero elsewhere.  The
+// warp walks the concatenated samples of its cell rows 16 at a time with
+// mma.sync m16n8k16 (rows: the segment's 32 voxels as two m-tiles, K:
+// samples, N: channels).  Each step writes the 16 samples' two weights -- as
+// two 16-bit halves W = W_hi + W_lo, as msda_dense_mma_kernel does -- into a
+// zeroed 32 x 16 tile per half in shared memory, loads the A fragments with
+// ldmatrix and clears what it wrote; the grad_out rows come with
+// ldmatrix.trans from the staged rows, whose 16-byte chunks are
+// XOR-swizzled by slot so that eight consecutive slots hit distinct banks.
+// Samples past the step's end read the zero row.  The fp32 accumulators are
+// rounded once, staged through shared memory with stmatrix and stored as
+// whole 16-byte chunks.  A sample whose grad_out row holds an Inf or NaN
+// spreads NaN over its whole segment (0 * Inf in the product), where the
+// reference's per-corner scatter confines it to the sample's corners.
+constexpr int kVmStride = 24;  // A-tile row stride (16-bit values): 48 bytes, conflict-free ldmatrix
+
+// Bytes of a warp's area: its two A tiles (32 rows each) or, after the last
+// step, its 32 output rows of 16 * nt bytes.
+__host__ __device__ constexpr int vm_warp_bytes(int nt) {
+  return 2 * 32 * kVmStride * 2 > 32 * 16 * nt ? 2 * 32 * kVmStride * 2 : 32 * 16 * nt;
+}
+
+// Position of 16-byte chunk c in row r of a 16 * NT-byte row array: c XOR a
+// function of r that puts chunk c of eight consecutive rows into eight
+// distinct 16-byte bank groups.
+template <int NT>
+__device__ __forceinline__ int vm_swz(int c, int r) {
+  return c ^ ((r / (8 / NT)) % NT);
+}
+
+__device__ __forceinline__ void ldmatrix_x4_m(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void ldmatrix_x4_trans_m(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                                    uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void stmatrix_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2,
+                                            uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr),
+               "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+               : "memory");
+}
+
+template <typename T, int NDIM, int NT>
+__global__ void __launch_bounds__(kThreads, NT > 4 ? 2 : 3)
+    msda_voxel_mma_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
+                          T* __restrict__ grad_value) {
+  constexpr int ROWB = 16 * NT;                 // grad_out row bytes
+  constexpr int WB = vm_warp_bytes(NT);
+  constexpr int NR = NDIM == 3 ? 4 : 2;         // cell rows per voxel row
+  extern __shared__ __align__(16) unsigned char vsm[];
+  const int lane = static_cast<int>(threadIdx.x & 31u);
+  const int warp = static_cast<int>(threadIdx.x >> 5);
+  const VoxUnit U = voxel_unit<NDIM>(p, sp);
+  const int cw = U.cw;
+
+  unsigned char* zrow = vsm;                    // 16 zero bytes (32 reserved)
+  unsigned char* wa_s = vsm + 32;               // warps x WB
+  SRec* rec_s = reinterpret_cast<SRec*>(wa_s + (kThreads / 32) * WB);       // vcap
+  unsigned char* go_s = reinterpret_cast<unsigned char*>(rec_s + sp.vcap);  // vcap * ROWB
+  int32_t* lo_s = reinterpret_cast<int32_t*>(go_s + static_cast<size_t>(sp.vcap) * ROWB);
+  int32_t* cnt_s = lo_s + sp.vcap;              // ncr * cw
+  int32_t* off_s = cnt_s + U.ncr * cw;          // ncr + 1
+  for (int i = threadIdx.x; i < (32 + (kThreads / 32) * WB) / 16; i += kThreads)
+    reinterpret_cast<uint4*>(vsm)[i] = make_uint4(0u, 0u, 0u, 0u);
+  const int32_t total = voxel_bounds<NDIM>(sp, U, cnt_s, off_s);  // synchronises the CTA
+
+  // this warp's 32-voxel segment
+  const int segs = (U.vt.tx + 31) / 32;
+  const int ry = warp / segs, sgi = warp - ry * segs;
+  const int32_t xw = U.x0 + sgi * 32;
+  const bool wactive = ry < U.vt.ny && U.y0 + ry < U.Hs && xw < U.W;
+  unsigned char* wa = wa_s + warp * WB;
+  uint16_t* at = reinterpret_cast<uint16_t*>(wa);  // [half][32 voxels][kVmStride]
+  const int j = lane & 15, hl = lane >> 4;         // this lane's sample of a step, its half
+  // ldmatrix: this lane's A row (voxel) and column block; B n-tile offset
+  const uint32_t a_addr =
+      smem_addr(at + ((lane & 7) + ((lane >> 3) & 1) * 8) * kVmStride + (lane >> 4) * 8);
+  const int jo = lane >> 4;
+  float d[2][NT][4];
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int jn = 0; jn < NT; ++jn) d[mi][jn][0] = d[mi][jn][1] = d[mi][jn][2] = d[mi][jn][3] = 0.0f;
+
+  for (int32_t q0 = 0; q0 < total; q0 += sp.vcap) {
+    const int nr = min(sp.vcap, total - q0);
+    // stage the round: records, then per record its corner weights as 16-bit
+    // halves -- words (by 0: high, low; by 1: high, low), each word the
+    // (bx 0, bx 1) pair -- in place of (a, f), its cell's x offset and its
+    // grad_out row
+    if (q0 > 0) __syncthreads();
+    voxel_stage_records(sp, U, q0, nr, rec_s, lo_s, cnt_s, off_s);
+    cp_async_wait_all();
+    __syncthreads();
+    for (int q = threadIdx.x; q < nr; q += kThreads) {
+      const SRec rec = rec_s[q];
+      int32_t xoff;
+      const float4 w4 = voxel_weights<NDIM>(rec, lo_s[q], U, xoff);
+      lo_s[q] = xoff;
+      const float wv[4] = {w4.x, w4.z, w4.y, w4.w};  // (bx, by) = (0,0) (1,0) (0,1) (1,1)
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint16_t h16 = MmaT<T>::bits(wv[i]);
+        hi[i] = h16;
+        lo[i] = MmaT<T>::bits(wv[i] - MmaT<T>::value(h16));
+      }
+      *reinterpret_cast<uint4*>(rec_s + q) =
+          make_uint4(hi[0] | (hi[1] << 16), lo[0] | (lo[1] << 16), hi[2] | (hi[3] << 16),
+                     lo[2] | (lo[3] << 16));
+      const char* src = reinterpret_cast<const char*>(grad_out) + static_cast<int64_t>(rec.row) * ROWB;
+#pragma unroll
+      for (int c = 0; c < NT; ++c)
+        cp_async<16>(go_s + static_cast<size_t>(q) * ROWB + vm_swz<NT>(c, q) * 16, src + c * 16);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    if (!wactive) continue;
+    // the warp's cell rows (dz, dy) = (r >> 1, r & 1) in this round: slots
+    // qa[r] .. qa[r] + nn[r] - 1
+    int32_t qa[NR], nn[NR];
+    int32_t n = 0;
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      const int cr = (r >> 1) * U.nyr + (ry - (r & 1) + 1);
+      const int32_t* crp = cnt_s + cr * cw;
+      const int32_t slot0 = off_s[cr] - crp[0] - q0;  // position -> round slot
+      const int c0 = sgi * 32;                        // cells c0 .. c0+32 touch the segment
+      const int32_t a = max(crp[c0] + slot0, 0);
+      const int32_t e = min(crp[min(c0 + 33, cw - 1)] + slot0, nr);
+      qa[r] = a;
+      nn[r] = max(e - a, 0);
+      n += nn[r];
+    }
+    for (int32_t k0 = 0; k0 < n; k0 += 16) {
+      // this lane's sample: entry k0 + j of the concatenated cell rows
+      int32_t rem = k0 + j;
+      int q = -1, dyv = 0;
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        if (q < 0 && rem < nn[r]) { q = qa[r] + rem; dyv = r & 1; }
+        rem -= nn[r];
+      }
+      int vlo = -2;
+      uint16_t* col = at + hl * 32 * kVmStride + j;
+      if (q >= 0) {
+        vlo = lo_s[q] - 1 - sgi * 32;  // the cell's lower-x voxel in the segment
+        const uint32_t w2 = reinterpret_cast<const uint32_t*>(rec_s + q)[dyv * 2 + hl];
+        if (static_cast<unsigned>(vlo) < 32u) col[vlo * kVmStride] = static_cast<uint16_t>(w2);
+        if (static_cast<unsigned>(vlo + 1) < 32u)
+          col[(vlo + 1) * kVmStride] = static_cast<uint16_t>(w2 >> 16);
+      }
+      __syncwarp();
+      uint32_t a[2][2][4];  // [half][m-tile]
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+        for (int mi = 0; mi < 2; ++mi)
+          ldmatrix_x4_m(a_addr + (hf * 32 + mi * 16) * kVmStride * 2, a[hf][mi]);
+      const unsigned char* rowp = go_s + static_cast<size_t>(q < 0 ? 0 : q) * ROWB;
+#pragma unroll
+      for (int jj = 0; jj < NT; jj += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans_m(smem_addr(q >= 0 ? rowp + vm_swz<NT>(jj + jo, q) * 16 : zrow), b0, b1,
+                            b2, b3);
+#pragma unroll
+        for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            MmaT<T>::mma4(d[mi][jj], a[hf][mi], b0, b1);
+            MmaT<T>::mma4(d[mi][jj + 1], a[hf][mi], b2, b3);
+          }
+      }
+      __syncwarp();
+      if (static_cast<unsigned>(vlo) < 32u) col[vlo * kVmStride] = 0;
+      if (static_cast<unsigned>(vlo + 1) < 32u) col[(vlo + 1) * kVmStride] = 0;
+    }
+  }
+  if (!wactive) return;
+  // round once; the 32 rows (chunks swizzled by voxel) into the warp's area
+  // with stmatrix: 8x8 matrices (m-tile, half, n-tile), n-tile fastest
+  __syncwarp();
+#pragma unroll
+  for (int s = 0; s < NT; ++s) {
+    uint32_t r[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int mm = 4 * s + k;
+      const int jn = mm % NT, hf = (mm / NT) & 1, mi = mm / (2 * NT);
+      r[k] = MmaT<T>::pack(d[mi][jn][2 * hf], d[mi][jn][2 * hf + 1]);
+    }
+    const int mm = 4 * s + (lane >> 3);
+    const int jn = mm % NT, hf = (mm / NT) & 1, mi = mm / (2 * NT);
+    const int row = 16 * mi + 8 * hf + (lane & 7);
+    stmatrix_x4(smem_addr(wa + row * ROWB + vm_swz<NT>(jn, row) * 16), r[0], r[1], r[2], r[3]);
+  }
+  __syncwarp();
+  const int32_t y = U.y0 + ry;
+  const int64_t key0 =
+      static_cast<int64_t>(p.lv.start[U.l]) + (static_cast<int64_t>(U.vz) * U.Hs + y) * U.W;
+  const int64_t ks = key_stride(p);
+  const int nvox = min(32, U.W - xw);
+  T* gvb = grad_value + bh_base(p, U.b, U.h, p.K);
+#pragma unroll
+  for (int i = lane; i < 32 * NT; i += 32) {
+    const int v = i / NT, c = i % NT;
+    if (v < nvox)
+      *reinterpret_cast<uint4*>(gvb + (key0 + xw + v) * ks + c * 8) =
+          *reinterpret_cast<const uint4*>(wa + v * ROWB + vm_swz<NT>(c, v) * 16);
   }
 }
 

@@ -48,6 +48,8 @@ PLANS = {
     "scatter": {"MSDA_BWD_PATH": "scatter"},
     "scatter-direct16": {"MSDA_BWD_PATH": "scatter", "MSDA_BWD_DIRECT16": "1"},
     "sorted-voxel": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "1e9"},
+    "sorted-voxel-cc": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "1e9",
+                        "MSDA_VOXEL_MMA": "0"},
     "sorted-cell-sdots": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "0",
                           "MSDA_SORTED_DOTS_MB": "0"},
     "sorted-cell-mma": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "0",
@@ -66,7 +68,7 @@ DTYPES = [torch.float32, torch.bfloat16, torch.float16]
 
 def _set_env(monkeypatch, plan):
     for k in ("MSDA_BWD_PATH", "MSDA_BWD_DIRECT16", "MSDA_VOXEL_DENSITY", "MSDA_SORTED_DOTS_MB",
-              "MSDA_SORTED_CHUNK_B", "MSDA_DENSE_MMA_DENSITY"):
+              "MSDA_SORTED_CHUNK_B", "MSDA_DENSE_MMA_DENSITY", "MSDA_VOXEL_MMA"):
         monkeypatch.delenv(k, raising=False)
     for k, v in PLANS[plan].items():
         monkeypatch.setenv(k, v)

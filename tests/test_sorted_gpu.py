@@ -200,6 +200,26 @@ def test_dense_cuda_core_and_tensor_core_agree(monkeypatch, case, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("case", CASES, ids=[f"{c[0]}d-{len(c[6])}lvl-q{c[2]}" for c in CASES])
+def test_voxel_cuda_core_and_tensor_core_agree(monkeypatch, case, dtype):
+    """16-bit values: the per-row gather of voxel levels on the tensor cores
+    (the default for C = 16, 32, 64; weights split into two 16-bit halves)
+    and on the CUDA cores (MSDA_VOXEL_MMA=0) both meet the half-precision bar
+    against the oracle, with every level gathered per row, in-range and
+    clamped (out-of-range) locations."""
+    ndim, B, Q, H, C, P, shapes = case
+    for clamp, rng in ((True, (0.0, 1.0)), (False, (-0.15, 1.15))):
+        inp = _cast(make_inputs(B, Q, H, C, P, shapes, seed=5 * Q + C, loc_range=rng),
+                    dtype, dtype)
+        ref = oracle_all(*_upcast(inp), clamp=clamp)
+        for mma in ("1", "0"):
+            _env(monkeypatch, "voxel")
+            monkeypatch.setenv("MSDA_VOXEL_MMA", mma)
+            got = cuda_fwd_bwd(ndim, *inp, clamp=clamp)
+            check_all(got, ref, TOL_HALF, TOL_HALF, f"{case} {dtype} voxel mma={mma} clamp={clamp}")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("path", ["sorted", "scatter"])
 def test_module_like_clustered_half_precision(monkeypatch, path, dtype):
     """Sampling points the way the MSDA3D module forms them -- reference point
