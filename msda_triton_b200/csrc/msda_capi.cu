@@ -466,6 +466,7 @@ constexpr bool kSortedByDefault = true;
 // per voxel-kernel round.
 constexpr int64_t kDenseChunk = 512;
 constexpr int64_t kVoxelCap = 512;
+static_assert(kVoxelCap <= 2 * kThreads, "msda_voxel_mma_kernel stages two slots per thread");
 // Levels whose value slice of one batch entry is at least this large take
 // their dot products in sorted order (msda_sdots_kernel): in query order
 // their rows are fetched from DRAM on almost every touch.
@@ -513,17 +514,21 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   const int64_t row_bytes = a.C * dtype_bytes(a.vdt);
   // samples the voxel kernel stages per round: as many as fit next to the
   // warps' areas (fp32 accumulators, 32 KB; or the tensor-core kernel's
-  // 16-bit weight tiles and the zero row) and the range bounds in 72 KB, at
-  // most 512
+  // 16-bit weight tiles, the zero row and the warps' slot lists and ranges)
+  // and the range bounds in 72 KB, at most 512 (two per thread)
+  const int64_t nw = kThreads / 32;
   const int64_t bounds_max = int64_t{4} * (tile_max + 2) * 4 + 4 * 64;
   const int64_t acc_bytes =
-      vmma ? 32 + int64_t{kThreads / 32} * vm_warp_bytes(static_cast<int>(a.C / 8))
-           : int64_t{kThreads / 32} * 32 * 32 * 4;
-  // per staged sample: its record (32 B), cell row / x offset (4 B), grad_out row
+      vmma ? 32 + nw * vm_warp_bytes(static_cast<int>(a.C / 8)) + nw * kVmList * 2 + nw * 8 * 4
+           : nw * 32 * 32 * 4;
   // MSDA_VOXEL_SMEM_KB (tuning): the voxel kernel's shared-memory budget
   const char* vs_env = std::getenv("MSDA_VOXEL_SMEM_KB");
   const int64_t vbudget = (vs_env && std::atoll(vs_env) > 0 ? std::atoll(vs_env) : 72) * 1024;
-  int64_t cap = (vbudget - acc_bytes - bounds_max) / (36 + row_bytes);
+  // per staged sample: its record (32 B; the tensor-core kernel keeps its
+  // 2^d corner weights as 16-bit halves instead), cell row / x offset (4 B)
+  // and grad_out row
+  const int64_t per_smp = (vmma ? (a.ndim == 3 ? 32 : 16) : 32) + 4 + row_bytes;
+  int64_t cap = (vbudget - acc_bytes - bounds_max) / per_smp;
   cap = std::min<int64_t>(cap, kVoxelCap) & ~int64_t{1};
   if (cap < 16) max_dens = -1.0;
   SortPlan sp{};
@@ -551,26 +556,36 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
     if (seg >= INT32_MAX) return false;
     const double dens = static_cast<double>(a.Q * a.P) / static_cast<double>(ncell);
     if (dens <= max_dens && nvox > 0) {
-      // tile: up to tile_max voxels, NY rows of TX; fewer rows when the
-      // expected samples of its cell rows pass two staging rounds
+      // tile: NZ planes x NY rows x TX voxels, TX up to tile_max; fewer rows
+      // when the expected samples of its cell rows pass the staging rounds
+      // aimed at (two; one for the tensor-core kernel)
       const int64_t W = p.lv.size[l][0], Hl = p.lv.size[l][1];
-      // rows of up to 8 segments of 32 voxels (a warp each)
+      const int64_t Dl = a.ndim == 3 ? p.lv.size[l][2] : 1;
+      // msda_voxel_kernel: up to 8 segments of 32 voxels (a warp each) in one
+      // plane; msda_voxel_mma_kernel: up to 16 (two per warp) in two planes
       const int64_t tx = std::min<int64_t>(W, tile_max);
       const int64_t segs = (tx + 31) / 32;
-      int64_t ny = std::max<int64_t>(1, std::min<int64_t>((kThreads / 32) / segs, Hl));
-      const int zr = a.ndim == 3 ? 2 : 1;
-      while (ny > 1 && static_cast<double>(zr * (ny + 1) * (tx + 1)) * dens > 2.0 * cap) --ny;
+      const int64_t nz = vmma && a.ndim == 3 && Dl >= 2 ? 2 : 1;
+      const int64_t wseg = vmma ? 2 * nw : nw;
+      int64_t ny = std::max<int64_t>(1, std::min<int64_t>(wseg / (segs * nz), Hl));
+      const int64_t zr = a.ndim == 3 ? nz + 1 : 1;
+      const double rounds = vmma ? 1.0 : 2.0;
+      while (ny > 1 && static_cast<double>(zr * (ny + 1) * (tx + 1)) * dens > rounds * cap) --ny;
       VoxTile vt;
       vt.tx = static_cast<int32_t>(tx);
       vt.ny = static_cast<int32_t>(ny);
+      vt.nz = static_cast<int32_t>(nz);
       vt.ntx = static_cast<int32_t>((W + tx - 1) / tx);
       vt.nty = static_cast<int32_t>((Hl + ny - 1) / ny);
-      max_bounds = std::max<int64_t>(max_bounds, zr * (ny + 1) * (tx + 2) + zr * (ny + 1) + 1);
+      // range bounds: every cell of the tile's cell rows, or (tensor cores)
+      // two per segment and cell row; then the cell rows' offsets
+      const int64_t nbr = vmma ? 2 * segs : tx + 2;
+      max_bounds = std::max<int64_t>(max_bounds, zr * (ny + 1) * nbr + zr * (ny + 1) + 1);
       sp.voxel_mask |= 1 << l;
       sp.vl_level[nvl] = static_cast<int32_t>(l);
       sp.vl_tile[nvl] = vt;
       sp.vl_ubase[nvl] = static_cast<int32_t>(units);
-      units += int64_t{vt.ntx} * vt.nty * (a.ndim == 3 ? p.lv.size[l][2] : 1);
+      units += int64_t{vt.ntx} * vt.nty * ((Dl + nz - 1) / nz);
       vox += nvox;
       ++nvl;
       if (vox >= INT32_MAX || units >= INT32_MAX) return false;
@@ -625,7 +640,7 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   sp.vcap = static_cast<int32_t>(cap);
   sp.vnv = p.nv;
   sp.div_nv = make_fdiv(static_cast<uint32_t>(std::max<int32_t>(p.nv, 1)));
-  sp.vsmem = static_cast<int32_t>(acc_bytes + cap * (36 + row_bytes) + max_bounds * 4);
+  sp.vsmem = static_cast<int32_t>(acc_bytes + cap * per_smp + max_bounds * 4);
   sp.vmma = vmma ? 1 : 0;
   if (nvl > 0 && sp.vsmem > 100 * 1024) return false;
   sp.div_lp = make_fdiv(static_cast<uint32_t>(a.L * a.P));

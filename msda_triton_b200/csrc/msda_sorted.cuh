@@ -66,7 +66,7 @@ __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
 
 // Tile of msda_voxel_kernel on one level: NY voxel rows x TX voxels.
 struct VoxTile {
-  int32_t tx, ny;     // voxels per row segment, rows per CTA
+  int32_t tx, ny, nz; // voxels per row segment, rows and planes per CTA
   int32_t ntx, nty;   // tiles along x and y
 };
 
@@ -1286,7 +1286,7 @@ struct VoxUnit {
   int32_t b, h, l;
   VoxTile vt;
   int32_t W, Hs;       // level size along x and y
-  int32_t x0, y0, vz;  // the tile's first voxel
+  int32_t x0, y0, vz;  // the tile's first voxel (vz: its first plane)
   int32_t cxn, cyn;    // cells along x and y
   int32_t kb;          // the level's first bucket key inside the (b, h) block
   int32_t nyr, ncr;    // cell rows per z, cell rows
@@ -1309,7 +1309,7 @@ __device__ __forceinline__ VoxUnit voxel_unit(const Problem& p, const SortPlan& 
   const uint32_t xt = rem % static_cast<uint32_t>(U.vt.ntx);
   const uint32_t r2 = rem / static_cast<uint32_t>(U.vt.ntx);
   const uint32_t yt = r2 % static_cast<uint32_t>(U.vt.nty);
-  U.vz = static_cast<int32_t>(r2 / static_cast<uint32_t>(U.vt.nty));
+  U.vz = static_cast<int32_t>(r2 / static_cast<uint32_t>(U.vt.nty)) * U.vt.nz;
   U.x0 = static_cast<int32_t>(xt) * U.vt.tx;
   U.y0 = static_cast<int32_t>(yt) * U.vt.ny;
   U.b = static_cast<int32_t>(U.bh / static_cast<uint32_t>(p.H));
@@ -1526,31 +1526,40 @@ __global__ void __launch_bounds__(kThreads)
 
 // ------------------------------------------------------------------ voxel levels, tensor cores
 // The same value gradient for 16-bit values with C = 8 * NT channels (NT 2,
-// 4 or 8) as small products on the tensor cores.  A warp's 32-voxel row
-// segment gets
+// 4 or 8) as small products on the tensor cores.  A 32-voxel row segment
+// gets
 //   G[v][ch] = sum over the samples s of its 2^(d-1) cell rows of A[v][s] * go[s][ch]
 // with A[v][s] = a * w of sample s's corner at voxel v: two entries per
-// sample (its lower and upper x-corner in this row), zero elsewhere.  The
-// warp walks the concatenated samples of its cell rows 16 at a time with
+// sample (its lower and upper x-corner in this row), zero elsewhere.  A warp
+// walks the concatenated samples of a segment's cell rows 16 at a time with
 // mma.sync m16n8k16 (rows: the segment's 32 voxels as two m-tiles, K:
 // samples, N: channels).  Each step writes the 16 samples' two weights -- as
 // two 16-bit halves W = W_hi + W_lo, as msda_dense_mma_kernel does -- into a
 // zeroed 32 x 16 tile per half in shared memory, loads the A fragments with
 // ldmatrix and clears what it wrote; the grad_out rows come with
-// ldmatrix.trans from the staged rows, whose 16-byte chunks are
-// XOR-swizzled by slot so that eight consecutive slots hit distinct banks.
-// Samples past the step's end read the zero row.  The fp32 accumulators are
-// rounded once, staged through shared memory with stmatrix and stored as
-// whole 16-byte chunks.  A sample whose grad_out row holds an Inf or NaN
-// spreads NaN over its whole segment (0 * Inf in the product), where the
-// reference's per-corner scatter confines it to the sample's corners.
-constexpr int kVmStride = 24;  // A-tile row stride (16-bit values): 48 bytes, conflict-free ldmatrix
+// ldmatrix.trans from the staged rows.  Samples past the step's end read the
+// zero row.  The fp32 accumulators are rounded once, staged through shared
+// memory with stmatrix and stored as whole 16-byte chunks.  A sample whose
+// grad_out row holds an Inf or NaN spreads NaN over its whole segment (0 *
+// Inf in the product), where the reference's per-corner scatter confines it
+// to the sample's corners.
+//
+// Tile: NZ voxel planes (2 in 3D) x NY rows x TX voxels per CTA, staged
+// once for all its segments (each warp takes every eighth): the cell planes
+// z0-1 .. z0+NZ-1 x cell rows y0-1 .. y0+NY-1, so a sample is staged by
+// (NZ+1)/NZ x (NY+1)/NY CTAs on average.  Per staged sample the CTA keeps
+// its 2^d corner weights as 16-bit halves (word (bz*2 + by)*2 + half: the
+// (bx 0, bx 1) pair), its cell's x offset and its grad_out row (16-byte
+// chunks XOR-swizzled by slot so that eight consecutive slots hit distinct
+// banks).  Of the range bounds only those at segment edges are loaded.
 
-// Bytes of a warp's area: its two A tiles (32 rows each) or, after the last
-// step, its 32 output rows of 16 * nt bytes.
+// Bytes of a warp's area: its two A tiles (32 rows of 32 bytes each) or,
+// after a segment's last step, its 32 output rows of 16 * nt bytes.
 __host__ __device__ constexpr int vm_warp_bytes(int nt) {
-  return 2 * 32 * kVmStride * 2 > 32 * 16 * nt ? 2 * 32 * kVmStride * 2 : 32 * 16 * nt;
+  return 2 * 32 * 32 > 32 * 16 * nt ? 2 * 32 * 32 : 32 * 16 * nt;
 }
+// Entries of a warp's slot list (a chunk of a segment's samples).
+constexpr int kVmList = 64;
 
 // Position of 16-byte chunk c in row r of a 16 * NT-byte row array: c XOR a
 // function of r that puts chunk c of eight consecutive rows into eight
@@ -1558,6 +1567,12 @@ __host__ __device__ constexpr int vm_warp_bytes(int nt) {
 template <int NT>
 __device__ __forceinline__ int vm_swz(int c, int r) {
   return c ^ ((r / (8 / NT)) % NT);
+}
+// 16-bit element (row v, column j) of a 32 x 16 A tile with 32-byte rows:
+// the two 8-column halves of rows 4-7 of every 8 swap places, which keeps
+// ldmatrix's eight row reads in distinct bank groups.
+__device__ __forceinline__ int vm_at(int v, int j) {
+  return v * 16 + ((((j >> 3) ^ (v >> 2)) & 1) << 3) + (j & 7);
 }
 
 __device__ __forceinline__ void ldmatrix_x4_m(uint32_t addr, uint32_t* r) {
@@ -1580,6 +1595,35 @@ __device__ __forceinline__ void stmatrix_x4(uint32_t addr, uint32_t r0, uint32_t
                : "memory");
 }
 
+// The staged form of one record for the tensor-core voxel kernel: its
+// corner weights a * w (the reference's product order, w = wx * wy [* wz])
+// as 16-bit halves in wt (2^(d-1) * 2 words), its cell's x offset.
+template <typename T, int NDIM>
+__device__ __forceinline__ void vm_stage_weights(const uint4& r0, uint32_t* wt) {
+  const float a = __uint_as_float(r0.x);
+  const float fx = __uint_as_float(r0.y), fy = __uint_as_float(r0.z), fz = __uint_as_float(r0.w);
+  const float wx[2] = {__fsub_rn(1.0f, fx), fx};
+  const float wy[2] = {__fsub_rn(1.0f, fy), fy};
+  const float wz[2] = {__fsub_rn(1.0f, fz), fz};
+#pragma unroll
+  for (int bz = 0; bz < (NDIM == 3 ? 2 : 1); ++bz)
+#pragma unroll
+    for (int by = 0; by < 2; ++by) {
+      uint32_t hi = 0u, lo = 0u;
+#pragma unroll
+      for (int bx = 0; bx < 2; ++bx) {
+        float w = __fmul_rn(wx[bx], wy[by]);
+        if (NDIM == 3) w = __fmul_rn(w, wz[bz]);
+        const float aw = a * w;
+        const uint16_t h16 = MmaT<T>::bits(aw);
+        hi |= static_cast<uint32_t>(h16) << (16 * bx);
+        lo |= static_cast<uint32_t>(MmaT<T>::bits(aw - MmaT<T>::value(h16))) << (16 * bx);
+      }
+      wt[(bz * 2 + by) * 2] = hi;
+      wt[(bz * 2 + by) * 2 + 1] = lo;
+    }
+}
+
 template <typename T, int NDIM, int NT>
 __global__ void __launch_bounds__(kThreads, NT > 4 ? 2 : 3)
     msda_voxel_mma_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
@@ -1587,166 +1631,241 @@ __global__ void __launch_bounds__(kThreads, NT > 4 ? 2 : 3)
   constexpr int ROWB = 16 * NT;                 // grad_out row bytes
   constexpr int WB = vm_warp_bytes(NT);
   constexpr int NR = NDIM == 3 ? 4 : 2;         // cell rows per voxel row
+  constexpr int NWW = NR * 2;                   // weight words per staged sample
+  constexpr int NW = kThreads / 32;
   extern __shared__ __align__(16) unsigned char vsm[];
   const int lane = static_cast<int>(threadIdx.x & 31u);
   const int warp = static_cast<int>(threadIdx.x >> 5);
   const VoxUnit U = voxel_unit<NDIM>(p, sp);
-  const int cw = U.cw;
+  const int nzp = NDIM == 3 ? U.vt.nz : 1;      // voxel planes of the tile
+  const int D = NDIM == 3 ? p.lv.size[U.l][2] : 1;
+  const int segs = (U.vt.tx + 31) / 32;         // segments per voxel row
+  const int nb = 2 * segs;                      // range bounds per cell row
+  const int nyr = U.vt.ny + 1;
+  const int ncr = (NDIM == 3 ? nzp + 1 : 1) * nyr;  // cell rows (iz, iy), iz slowest
 
   unsigned char* zrow = vsm;                    // 16 zero bytes (32 reserved)
   unsigned char* wa_s = vsm + 32;               // warps x WB
-  SRec* rec_s = reinterpret_cast<SRec*>(wa_s + (kThreads / 32) * WB);       // vcap
-  unsigned char* go_s = reinterpret_cast<unsigned char*>(rec_s + sp.vcap);  // vcap * ROWB
-  int32_t* lo_s = reinterpret_cast<int32_t*>(go_s + static_cast<size_t>(sp.vcap) * ROWB);
-  int32_t* cnt_s = lo_s + sp.vcap;              // ncr * cw
-  int32_t* off_s = cnt_s + U.ncr * cw;          // ncr + 1
-  for (int i = threadIdx.x; i < (32 + (kThreads / 32) * WB) / 16; i += kThreads)
+  uint32_t* wt_s = reinterpret_cast<uint32_t*>(wa_s + NW * WB);                  // vcap x NWW
+  unsigned char* go_s = reinterpret_cast<unsigned char*>(wt_s + static_cast<size_t>(sp.vcap) * NWW);
+  int32_t* lo_s = reinterpret_cast<int32_t*>(go_s + static_cast<size_t>(sp.vcap) * ROWB);  // vcap
+  uint16_t* lst_s = reinterpret_cast<uint16_t*>(lo_s + sp.vcap);                 // warps x kVmList
+  int32_t* rng_s = reinterpret_cast<int32_t*>(lst_s + NW * kVmList);             // warps x 2 NR
+  int32_t* bnd_s = rng_s + NW * 2 * NR;                                         // ncr x nb
+  int32_t* off_s = bnd_s + ncr * nb;                                            // ncr + 1
+  for (int i = threadIdx.x; i < (32 + NW * WB) / 16; i += kThreads)
     reinterpret_cast<uint4*>(vsm)[i] = make_uint4(0u, 0u, 0u, 0u);
-  const int32_t total = voxel_bounds<NDIM>(sp, U, cnt_s, off_s);  // synchronises the CTA
 
-  // this warp's 32-voxel segment
-  const int segs = (U.vt.tx + 31) / 32;
-  const int ry = warp / segs, sgi = warp - ry * segs;
-  const int32_t xw = U.x0 + sgi * 32;
-  const bool wactive = ry < U.vt.ny && U.y0 + ry < U.Hs && xw < U.W;
-  unsigned char* wa = wa_s + warp * WB;
-  uint16_t* at = reinterpret_cast<uint16_t*>(wa);  // [half][32 voxels][kVmStride]
-  const int j = lane & 15, hl = lane >> 4;         // this lane's sample of a step, its half
-  // ldmatrix: this lane's A row (voxel) and column block; B n-tile offset
-  const uint32_t a_addr =
-      smem_addr(at + ((lane & 7) + ((lane >> 3) & 1) * 8) * kVmStride + (lane >> 4) * 8);
+  // range bounds at the segment edges: bnd_s[cr][2s] = start of cell 32s,
+  // bnd_s[cr][2s+1] = start of cell min(32s+33, TX+1) (the end of the cells
+  // touching segment s; for the last segment the row's end) of cell row cr =
+  // iz * nyr + iy, whose cells have lower corner (y0-1+iy, z0-1+iz)
+  for (int i = threadIdx.x; i < ncr * nb; i += kThreads) {
+    const int cr = i / nb, e = i - cr * nb;
+    const int iz = cr / nyr, iy = cr - iz * nyr;
+    const int32_t yc = U.y0 - 1 + iy, zc = NDIM == 3 ? U.vz - 1 + iz : -1;
+    const int c = (e & 1) ? min(32 * (e >> 1) + 33, U.cw - 1) : 32 * (e >> 1);
+    if (yc <= U.Hs - 1 && zc <= D - 1)
+      cp_async<4>(bnd_s + i, sp.cnt + U.kb + ((zc + 1) * U.cyn + (yc + 1)) * U.cxn +
+                                 min(U.x0 + c, U.cxn));
+    else
+      bnd_s[i] = 0;  // rows outside the level are empty
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t o = 0;
+    for (int cr = 0; cr < ncr; ++cr) {
+      off_s[cr] = o;
+      o += bnd_s[cr * nb + nb - 1] - bnd_s[cr * nb];
+    }
+    off_s[ncr] = o;
+  }
+  __syncthreads();
+  const int32_t total = off_s[ncr];
+  const bool one_round = total <= sp.vcap;
+
+  uint16_t* at = reinterpret_cast<uint16_t*>(wa_s + warp * WB);  // [half][32 x 16]
+  const int j = lane & 15, hl = lane >> 4;      // this lane's sample of a step, its half
+  // ldmatrix: this lane's A row and column block (half 0, m-tile 0); B n-tile offset
+  const int ar = (lane & 7) + ((lane >> 3) & 1) * 8;
+  const uint32_t a_addr = smem_addr(at + vm_at(ar, (lane >> 4) * 8));
   const int jo = lane >> 4;
-  float d[2][NT][4];
-#pragma unroll
-  for (int mi = 0; mi < 2; ++mi)
-#pragma unroll
-    for (int jn = 0; jn < NT; ++jn) d[mi][jn][0] = d[mi][jn][1] = d[mi][jn][2] = d[mi][jn][3] = 0.0f;
+  uint16_t* lst = lst_s + warp * kVmList;
+  int32_t* rng = rng_s + warp * 2 * NR;
+  const int nseg = segs * U.vt.ny * nzp;
 
-  for (int32_t q0 = 0; q0 < total; q0 += sp.vcap) {
-    const int nr = min(sp.vcap, total - q0);
-    // stage the round: records, then per record its corner weights as 16-bit
-    // halves -- words (by 0: high, low; by 1: high, low), each word the
-    // (bx 0, bx 1) pair -- in place of (a, f), its cell's x offset and its
-    // grad_out row
-    if (q0 > 0) __syncthreads();
-    voxel_stage_records(sp, U, q0, nr, rec_s, lo_s, cnt_s, off_s);
-    cp_async_wait_all();
-    __syncthreads();
-    for (int q = threadIdx.x; q < nr; q += kThreads) {
-      const SRec rec = rec_s[q];
-      int32_t xoff;
-      const float4 w4 = voxel_weights<NDIM>(rec, lo_s[q], U, xoff);
-      lo_s[q] = xoff;
-      const float wv[4] = {w4.x, w4.z, w4.y, w4.w};  // (bx, by) = (0,0) (1,0) (0,1) (1,1)
-      uint32_t hi[4], lo[4];
+  for (int sg0 = 0; sg0 < nseg; sg0 += NW) {
+    // this warp's segment: (plane pz, row ry, segment sgi)
+    const int sg = sg0 + warp;
+    const int sgi = sg % segs, t = sg / segs;
+    const int ry = t % U.vt.ny, pz = t / U.vt.ny;
+    const int32_t xw = U.x0 + sgi * 32;
+    const bool wactive = sg < nseg && U.y0 + ry < U.Hs && U.vz + pz < D && xw < U.W;
+    float d[2][NT][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint16_t h16 = MmaT<T>::bits(wv[i]);
-        hi[i] = h16;
-        lo[i] = MmaT<T>::bits(wv[i] - MmaT<T>::value(h16));
-      }
-      *reinterpret_cast<uint4*>(rec_s + q) =
-          make_uint4(hi[0] | (hi[1] << 16), lo[0] | (lo[1] << 16), hi[2] | (hi[3] << 16),
-                     lo[2] | (lo[3] << 16));
-      const char* src = reinterpret_cast<const char*>(grad_out) + static_cast<int64_t>(rec.row) * ROWB;
+    for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-      for (int c = 0; c < NT; ++c)
-        cp_async<16>(go_s + static_cast<size_t>(q) * ROWB + vm_swz<NT>(c, q) * 16, src + c * 16);
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    if (!wactive) continue;
-    // the warp's cell rows (dz, dy) = (r >> 1, r & 1) in this round: slots
-    // qa[r] .. qa[r] + nn[r] - 1
-    int32_t qa[NR], nn[NR];
-    int32_t n = 0;
+      for (int jn = 0; jn < NT; ++jn) d[mi][jn][0] = d[mi][jn][1] = d[mi][jn][2] = d[mi][jn][3] = 0.0f;
+
+    for (int32_t q0 = 0; q0 < total; q0 += sp.vcap) {
+      const int nr = min(sp.vcap, total - q0);
+      if (sg0 == 0 || !one_round) {
+        // stage the round: per slot its cell row, record (into registers),
+        // corner weights, x offset and grad_out row; at most two slots per thread
+        if (q0 > 0 || sg0 > 0) __syncthreads();
+        uint4 r0[2], r1[2];
+        int crs[2];
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
-      const int cr = (r >> 1) * U.nyr + (ry - (r & 1) + 1);
-      const int32_t* crp = cnt_s + cr * cw;
-      const int32_t slot0 = off_s[cr] - crp[0] - q0;  // position -> round slot
-      const int c0 = sgi * 32;                        // cells c0 .. c0+32 touch the segment
-      const int32_t a = max(crp[c0] + slot0, 0);
-      const int32_t e = min(crp[min(c0 + 33, cw - 1)] + slot0, nr);
-      qa[r] = a;
-      nn[r] = max(e - a, 0);
-      n += nn[r];
-    }
-    for (int32_t k0 = 0; k0 < n; k0 += 16) {
-      // this lane's sample: entry k0 + j of the concatenated cell rows
-      int32_t rem = k0 + j;
-      int q = -1, dyv = 0;
-#pragma unroll
-      for (int r = 0; r < NR; ++r) {
-        if (q < 0 && rem < nn[r]) { q = qa[r] + rem; dyv = r & 1; }
-        rem -= nn[r];
-      }
-      int vlo = -2;
-      uint16_t* col = at + hl * 32 * kVmStride + j;
-      if (q >= 0) {
-        vlo = lo_s[q] - 1 - sgi * 32;  // the cell's lower-x voxel in the segment
-        const uint32_t w2 = reinterpret_cast<const uint32_t*>(rec_s + q)[dyv * 2 + hl];
-        if (static_cast<unsigned>(vlo) < 32u) col[vlo * kVmStride] = static_cast<uint16_t>(w2);
-        if (static_cast<unsigned>(vlo + 1) < 32u)
-          col[(vlo + 1) * kVmStride] = static_cast<uint16_t>(w2 >> 16);
-      }
-      __syncwarp();
-      uint32_t a[2][2][4];  // [half][m-tile]
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-        for (int mi = 0; mi < 2; ++mi)
-          ldmatrix_x4_m(a_addr + (hf * 32 + mi * 16) * kVmStride * 2, a[hf][mi]);
-      const unsigned char* rowp = go_s + static_cast<size_t>(q < 0 ? 0 : q) * ROWB;
-#pragma unroll
-      for (int jj = 0; jj < NT; jj += 2) {
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4_trans_m(smem_addr(q >= 0 ? rowp + vm_swz<NT>(jj + jo, q) * 16 : zrow), b0, b1,
-                            b2, b3);
-#pragma unroll
-        for (int mi = 0; mi < 2; ++mi)
-#pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            MmaT<T>::mma4(d[mi][jj], a[hf][mi], b0, b1);
-            MmaT<T>::mma4(d[mi][jj + 1], a[hf][mi], b2, b3);
+        for (int i = 0; i < 2; ++i) {
+          const int q = threadIdx.x + i * kThreads;
+          crs[i] = -1;
+          if (q < nr) {
+            const int32_t qq = q0 + q;
+            int lo = 0, hi = ncr;  // cell row: off_s[lo] <= qq < off_s[lo + 1]
+            while (hi - lo > 1) {
+              const int mid = (lo + hi) >> 1;
+              if (off_s[mid] <= qq) lo = mid; else hi = mid;
+            }
+            crs[i] = lo;
+            ld_rec(sp.srec + bnd_s[lo * nb] + (qq - off_s[lo]), r0[i], r1[i]);
           }
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          if (crs[i] < 0) continue;
+          const int q = threadIdx.x + i * kThreads;
+          const int cr = crs[i];
+          const int iz = cr / nyr, iy = cr - iz * nyr;
+          // the cell's x offset in the tile (cell i0x = x0 + offset - 1)
+          lo_s[q] = static_cast<int32_t>(r1[i].y) -
+                    (U.kb + ((U.vz + iz) * U.cyn + (U.y0 + iy)) * U.cxn) - U.x0;
+          uint32_t wt[NWW];
+          vm_stage_weights<T, NDIM>(r0[i], wt);
+          uint4* wq = reinterpret_cast<uint4*>(wt_s + static_cast<size_t>(q) * NWW);
+#pragma unroll
+          for (int k = 0; k < NWW / 4; ++k)
+            wq[k] = make_uint4(wt[4 * k], wt[4 * k + 1], wt[4 * k + 2], wt[4 * k + 3]);
+          const char* src = reinterpret_cast<const char*>(grad_out) + static_cast<int64_t>(r1[i].x) * ROWB;
+#pragma unroll
+          for (int c = 0; c < NT; ++c)
+            cp_async<16>(go_s + static_cast<size_t>(q) * ROWB + vm_swz<NT>(c, q) * 16, src + c * 16);
+        }
+        cp_async_wait_all();
+        __syncthreads();
+      }
+      if (!wactive) continue;
+      // the segment's cell rows r = (dz, dy) = (r >> 1, r & 1) (lower corner
+      // dz, dy below the voxel row) in this round: slots rng[r] ..
+      // rng[r] + rng[NR + r] - 1
+      int32_t n = 0;
+      if (lane < NR) {
+        const int r = lane;
+        const int cr = (NDIM == 3 ? pz + 1 - (r >> 1) : 0) * nyr + (ry + 1 - (r & 1));
+        const int32_t* bp = bnd_s + cr * nb;
+        const int32_t slot0 = off_s[cr] - bp[0] - q0;  // position -> round slot
+        const int32_t a = max(bp[2 * sgi] + slot0, 0);
+        const int32_t e = min(bp[2 * sgi + 1] + slot0, nr);
+        rng[r] = a;
+        rng[NR + r] = max(e - a, 0);
       }
       __syncwarp();
-      if (static_cast<unsigned>(vlo) < 32u) col[vlo * kVmStride] = 0;
-      if (static_cast<unsigned>(vlo + 1) < 32u) col[(vlo + 1) * kVmStride] = 0;
+#pragma unroll
+      for (int r = 0; r < NR; ++r) n += rng[NR + r];
+      for (int32_t c0 = 0; c0 < n; c0 += kVmList) {
+        // the chunk's list: entries slot | r << 12
+        const int m = min(kVmList, n - c0);
+        for (int e = lane; e < m; e += 32) {
+          int32_t rem = c0 + e;
+          uint32_t ent = 0;
+#pragma unroll
+          for (int r = 0; r < NR; ++r) {
+            const int32_t nn = rng[NR + r];
+            if (rem >= 0 && rem < nn) ent = static_cast<uint32_t>(rng[r] + rem) | (r << 12);
+            rem -= nn;
+          }
+          lst[e] = static_cast<uint16_t>(ent);
+        }
+        __syncwarp();
+        for (int k0 = 0; k0 < m; k0 += 16) {
+          const bool ok = k0 + j < m;
+          const uint32_t ent = ok ? lst[k0 + j] : 0u;
+          const int q = static_cast<int>(ent & 0xfffu), r = static_cast<int>(ent >> 12);
+          int vlo = -2;
+          uint16_t* tile = at + hl * 512;
+          if (ok) {
+            vlo = lo_s[q] - 1 - sgi * 32;  // the cell's lower-x voxel in the segment
+            const uint32_t w2 = wt_s[static_cast<size_t>(q) * NWW + r * 2 + hl];
+            if (static_cast<unsigned>(vlo) < 32u) tile[vm_at(vlo, j)] = static_cast<uint16_t>(w2);
+            if (static_cast<unsigned>(vlo + 1) < 32u)
+              tile[vm_at(vlo + 1, j)] = static_cast<uint16_t>(w2 >> 16);
+          }
+          __syncwarp();
+          // B (grad_out rows) for every n-tile pair, then A one m-tile at a time
+          uint32_t bq[NT / 2][4];
+          const unsigned char* rowp = go_s + static_cast<size_t>(q) * ROWB;
+#pragma unroll
+          for (int jp = 0; jp < NT / 2; ++jp)
+            ldmatrix_x4_trans_m(smem_addr(ok ? rowp + vm_swz<NT>(2 * jp + jo, q) * 16 : zrow),
+                                bq[jp][0], bq[jp][1], bq[jp][2], bq[jp][3]);
+#pragma unroll
+          for (int mi = 0; mi < 2; ++mi) {
+            uint32_t ah[4], al[4];
+            ldmatrix_x4_m(a_addr + mi * 16 * 32, ah);
+            ldmatrix_x4_m(a_addr + 1024 + mi * 16 * 32, al);
+#pragma unroll
+            for (int jp = 0; jp < NT / 2; ++jp) {
+              MmaT<T>::mma4(d[mi][2 * jp], ah, bq[jp][0], bq[jp][1]);
+              MmaT<T>::mma4(d[mi][2 * jp], al, bq[jp][0], bq[jp][1]);
+              MmaT<T>::mma4(d[mi][2 * jp + 1], ah, bq[jp][2], bq[jp][3]);
+              MmaT<T>::mma4(d[mi][2 * jp + 1], al, bq[jp][2], bq[jp][3]);
+            }
+          }
+          __syncwarp();
+          if (static_cast<unsigned>(vlo) < 32u) tile[vm_at(vlo, j)] = 0;
+          if (static_cast<unsigned>(vlo + 1) < 32u) tile[vm_at(vlo + 1, j)] = 0;
+        }
+        __syncwarp();
+      }
     }
-  }
-  if (!wactive) return;
-  // round once; the 32 rows (chunks swizzled by voxel) into the warp's area
-  // with stmatrix: 8x8 matrices (m-tile, half, n-tile), n-tile fastest
-  __syncwarp();
+    if (!wactive) continue;
+    // round once; the 32 rows (chunks swizzled by voxel) into the warp's area
+    // with stmatrix: 8x8 matrices (m-tile, half, n-tile), n-tile fastest
+    unsigned char* wa = wa_s + warp * WB;
+    __syncwarp();
 #pragma unroll
-  for (int s = 0; s < NT; ++s) {
-    uint32_t r[4];
+    for (int s = 0; s < NT; ++s) {
+      uint32_t rr[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int mm = 4 * s + k;
+      for (int k = 0; k < 4; ++k) {
+        const int mm = 4 * s + k;
+        const int jn = mm % NT, hf = (mm / NT) & 1, mi = mm / (2 * NT);
+        rr[k] = MmaT<T>::pack(d[mi][jn][2 * hf], d[mi][jn][2 * hf + 1]);
+      }
+      const int mm = 4 * s + (lane >> 3);
       const int jn = mm % NT, hf = (mm / NT) & 1, mi = mm / (2 * NT);
-      r[k] = MmaT<T>::pack(d[mi][jn][2 * hf], d[mi][jn][2 * hf + 1]);
+      const int row = 16 * mi + 8 * hf + (lane & 7);
+      stmatrix_x4(smem_addr(wa + row * ROWB + vm_swz<NT>(jn, row) * 16), rr[0], rr[1], rr[2], rr[3]);
     }
-    const int mm = 4 * s + (lane >> 3);
-    const int jn = mm % NT, hf = (mm / NT) & 1, mi = mm / (2 * NT);
-    const int row = 16 * mi + 8 * hf + (lane & 7);
-    stmatrix_x4(smem_addr(wa + row * ROWB + vm_swz<NT>(jn, row) * 16), r[0], r[1], r[2], r[3]);
-  }
-  __syncwarp();
-  const int32_t y = U.y0 + ry;
-  const int64_t key0 =
-      static_cast<int64_t>(p.lv.start[U.l]) + (static_cast<int64_t>(U.vz) * U.Hs + y) * U.W;
-  const int64_t ks = key_stride(p);
-  const int nvox = min(32, U.W - xw);
-  T* gvb = grad_value + bh_base(p, U.b, U.h, p.K);
+    __syncwarp();
+    const int32_t y = U.y0 + ry;
+    const int64_t key0 =
+        static_cast<int64_t>(p.lv.start[U.l]) + (static_cast<int64_t>(U.vz + pz) * U.Hs + y) * U.W;
+    const int64_t ks = key_stride(p);
+    const int nvox = min(32, U.W - xw);
+    T* gvb = grad_value + bh_base(p, U.b, U.h, p.K);
 #pragma unroll
-  for (int i = lane; i < 32 * NT; i += 32) {
-    const int v = i / NT, c = i % NT;
-    if (v < nvox)
-      *reinterpret_cast<uint4*>(gvb + (key0 + xw + v) * ks + c * 8) =
-          *reinterpret_cast<const uint4*>(wa + v * ROWB + vm_swz<NT>(c, v) * 16);
+    for (int i = lane; i < 32 * NT; i += 32) {
+      const int v = i / NT, c = i % NT;
+      if (v < nvox)
+        *reinterpret_cast<uint4*>(gvb + (key0 + xw + v) * ks + c * 8) =
+            *reinterpret_cast<const uint4*>(wa + v * ROWB + vm_swz<NT>(c, v) * 16);
+    }
+    // the area is the next segment's A tiles again: all zero
+    __syncwarp();
+    for (int i = lane; i < WB / 16; i += 32)
+      reinterpret_cast<uint4*>(wa)[i] = make_uint4(0u, 0u, 0u, 0u);
+    __syncwarp();
   }
 }
 
