@@ -6,7 +6,9 @@
  * The checked build runs the same kernels with a bounds check on every value
  * gather and value-gradient scatter: an address outside its buffer is not
  * accessed and sets a bit of a per-device word (1: value gather, 2: 16-bit
- * grad_value scatter, 4: fp32 accumulator scatter).  It stands in for a
+ * grad_value scatter, 4: fp32 accumulator scatter, 8: a kernel whose
+ * shared-memory layout would pass its launch's size and which therefore did
+ * no work).  It stands in for a
  * memory checker and is for tests and debugging; it is slower.  In the
  * cell-sorted backward the value gathers are checked; its record, fp32
  * accumulator and grad_value stores are not instrumented.

@@ -579,7 +579,7 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
       vt.nty = static_cast<int32_t>((Hl + ny - 1) / ny);
       // range bounds: every cell of the tile's cell rows, or (tensor cores)
       // two per segment and cell row; then the cell rows' offsets
-      const int64_t nbr = vmma ? 2 * segs : tx + 2;
+      const int64_t nbr = vmma ? vm_bounds_per_row(static_cast<int>(segs)) : tx + 2;
       max_bounds = std::max<int64_t>(max_bounds, zr * (ny + 1) * nbr + zr * (ny + 1) + 1);
       sp.voxel_mask |= 1 << l;
       sp.vl_level[nvl] = static_cast<int32_t>(l);

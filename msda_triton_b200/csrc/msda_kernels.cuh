@@ -163,8 +163,8 @@ static __device__ __align__(16) unsigned char g_zero_row[2048];
 // Checked build (-DMSDA_CHECKED): every value gather and value-gradient
 // scatter address is tested against the buffer it must stay inside.  A
 // violation sets a bit in *p.check_flag (1: value gather, 2: 16-bit
-// grad_value scatter, 4: fp32 accumulator scatter) and the access is skipped;
-// nothing traps.  The normal build compiles the plain accesses.
+// grad_value scatter, 4: fp32 accumulator scatter, 8: a shared-memory layout
+// larger than its launch's) and the access is skipped; nothing traps.  The normal build compiles the plain accesses.
 #ifdef MSDA_CHECKED
 __device__ __forceinline__ bool msda_within(const void* a, int n, const void* base,
                                             int64_t bytes) {

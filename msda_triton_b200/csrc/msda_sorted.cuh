@@ -1022,7 +1022,7 @@ template <> struct MmaT<__nv_bfloat16> {
   }
   static __device__ __forceinline__ void mma(float* d, uint32_t a0, uint32_t a2, uint32_t b0,
                                              uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
         "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -1031,7 +1031,7 @@ template <> struct MmaT<__nv_bfloat16> {
   // all four A registers (rows 0-15)
   static __device__ __forceinline__ void mma4(float* d, const uint32_t* a, uint32_t b0,
                                               uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
         "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -1052,7 +1052,7 @@ template <> struct MmaT<__half> {
   }
   static __device__ __forceinline__ void mma(float* d, uint32_t a0, uint32_t a2, uint32_t b0,
                                              uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
         "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -1061,7 +1061,7 @@ template <> struct MmaT<__half> {
   // all four A registers (rows 0-15)
   static __device__ __forceinline__ void mma4(float* d, const uint32_t* a, uint32_t b0,
                                               uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
         "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -1243,14 +1243,27 @@ __global__ void __launch_bounds__(kThreads, 4)
       const int sr = k0 + kr;
       const bool rin = sr >= ta && sr < tb;
       const unsigned char* rowp = go_s + static_cast<size_t>(rin ? sr : 0) * ROWB;
+      // every n-tile's high-half product before the low halves, so that the
+      // two products into one accumulator are NT instructions apart (C = 64:
+      // per pair of n-tiles, within the register bound)
+      constexpr int NP = NT <= 4 ? NT / 2 : 1;  // n-tile pairs per pass
 #pragma unroll
-      for (int jj = 0; jj < NT; jj += 2) {
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4_trans(smem_addr(rin ? rowp + (jj + jo) * 16 : zrow), b0, b1, b2, b3);
-        MmaT<T>::mma(d[jj], ah0, ah2, b0, b1);
-        MmaT<T>::mma(d[jj], al0, al2, b0, b1);
-        MmaT<T>::mma(d[jj + 1], ah0, ah2, b2, b3);
-        MmaT<T>::mma(d[jj + 1], al0, al2, b2, b3);
+      for (int jb = 0; jb < NT / 2; jb += NP) {
+        uint32_t bq[NP][4];
+#pragma unroll
+        for (int jp = 0; jp < NP; ++jp)
+          ldmatrix_x4_trans(smem_addr(rin ? rowp + (2 * (jb + jp) + jo) * 16 : zrow), bq[jp][0],
+                            bq[jp][1], bq[jp][2], bq[jp][3]);
+#pragma unroll
+        for (int jp = 0; jp < NP; ++jp) {
+          MmaT<T>::mma(d[2 * (jb + jp)], ah0, ah2, bq[jp][0], bq[jp][1]);
+          MmaT<T>::mma(d[2 * (jb + jp) + 1], ah0, ah2, bq[jp][2], bq[jp][3]);
+        }
+#pragma unroll
+        for (int jp = 0; jp < NP; ++jp) {
+          MmaT<T>::mma(d[2 * (jb + jp)], al0, al2, bq[jp][0], bq[jp][1]);
+          MmaT<T>::mma(d[2 * (jb + jp) + 1], al0, al2, bq[jp][2], bq[jp][3]);
+        }
       }
     }
     if (g < NC) {
@@ -1560,6 +1573,9 @@ __host__ __device__ constexpr int vm_warp_bytes(int nt) {
 }
 // Entries of a warp's slot list (a chunk of a segment's samples).
 constexpr int kVmList = 64;
+// Range bounds per cell row of a tile with segs 32-voxel segments: two per
+// segment (the first and past-the-last cell touching it).
+__host__ __device__ constexpr int vm_bounds_per_row(int segs) { return 2 * segs; }
 
 // Position of 16-byte chunk c in row r of a 16 * NT-byte row array: c XOR a
 // function of r that puts chunk c of eight consecutive rows into eight
@@ -1593,6 +1609,20 @@ __device__ __forceinline__ void stmatrix_x4(uint32_t addr, uint32_t r0, uint32_t
   asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr),
                "r"(r0), "r"(r1), "r"(r2), "r"(r3)
                : "memory");
+}
+// Shared-memory accesses by 32-bit shared-window address.
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void sts_u16(uint32_t a, uint32_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(static_cast<unsigned short>(v)) : "memory");
 }
 
 // The staged form of one record for the tensor-core voxel kernel: its
@@ -1640,7 +1670,7 @@ __global__ void __launch_bounds__(kThreads, NT > 4 ? 2 : 3)
   const int nzp = NDIM == 3 ? U.vt.nz : 1;      // voxel planes of the tile
   const int D = NDIM == 3 ? p.lv.size[U.l][2] : 1;
   const int segs = (U.vt.tx + 31) / 32;         // segments per voxel row
-  const int nb = 2 * segs;                      // range bounds per cell row
+  const int nb = vm_bounds_per_row(segs);       // range bounds per cell row
   const int nyr = U.vt.ny + 1;
   const int ncr = (NDIM == 3 ? nzp + 1 : 1) * nyr;  // cell rows (iz, iy), iz slowest
 
@@ -1653,6 +1683,18 @@ __global__ void __launch_bounds__(kThreads, NT > 4 ? 2 : 3)
   int32_t* rng_s = reinterpret_cast<int32_t*>(lst_s + NW * kVmList);             // warps x 2 NR
   int32_t* bnd_s = rng_s + NW * 2 * NR;                                         // ncr x nb
   int32_t* off_s = bnd_s + ncr * nb;                                            // ncr + 1
+  {
+    // the layout inside the launch's dynamic shared memory, or no access at
+    // all (checked build: bit 8 of the check word)
+    uint32_t dyn;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+    if (static_cast<size_t>(reinterpret_cast<unsigned char*>(off_s + ncr + 1) - vsm) > dyn) {
+#ifdef MSDA_CHECKED
+      if (threadIdx.x == 0) atomicOr(p.check_flag, 8u);
+#endif
+      return;
+    }
+  }
   for (int i = threadIdx.x; i < (32 + NW * WB) / 16; i += kThreads)
     reinterpret_cast<uint4*>(vsm)[i] = make_uint4(0u, 0u, 0u, 0u);
 
@@ -1694,6 +1736,15 @@ __global__ void __launch_bounds__(kThreads, NT > 4 ? 2 : 3)
   uint16_t* lst = lst_s + warp * kVmList;
   int32_t* rng = rng_s + warp * 2 * NR;
   const int nseg = segs * U.vt.ny * nzp;
+  // 32-bit shared addresses of the step's accesses: this lane's list entry,
+  // the x offsets, its weight half, the grad_out rows, the zero row and its
+  // A-tile column (row v at + v * 32, the 8-column halves of rows 4-7 of
+  // every 8 swapped: see vm_at)
+  const uint32_t lst_a = smem_addr(lst) + j * 2;
+  const uint32_t lo_a = smem_addr(lo_s), wt_a = smem_addr(wt_s) + hl * 4;
+  const uint32_t go_a = smem_addr(go_s), zrow_a = smem_addr(zrow);
+  const uint32_t tcol = smem_addr(at) + hl * 1024 + (j & 7) * 2;
+  const int jb = (j >> 3) & 1;
 
   for (int sg0 = 0; sg0 < nseg; sg0 += NW) {
     // this warp's segment: (plane pz, row ry, segment sgi)
@@ -1789,24 +1840,28 @@ __global__ void __launch_bounds__(kThreads, NT > 4 ? 2 : 3)
         __syncwarp();
         for (int k0 = 0; k0 < m; k0 += 16) {
           const bool ok = k0 + j < m;
-          const uint32_t ent = ok ? lst[k0 + j] : 0u;
-          const int q = static_cast<int>(ent & 0xfffu), r = static_cast<int>(ent >> 12);
-          int vlo = -2;
-          uint16_t* tile = at + hl * 512;
+          uint32_t q = 0, ta = 0, tb = 0;
+          bool wa_lo = false, wa_hi = false;
           if (ok) {
-            vlo = lo_s[q] - 1 - sgi * 32;  // the cell's lower-x voxel in the segment
-            const uint32_t w2 = wt_s[static_cast<size_t>(q) * NWW + r * 2 + hl];
-            if (static_cast<unsigned>(vlo) < 32u) tile[vm_at(vlo, j)] = static_cast<uint16_t>(w2);
-            if (static_cast<unsigned>(vlo + 1) < 32u)
-              tile[vm_at(vlo + 1, j)] = static_cast<uint16_t>(w2 >> 16);
+            const uint32_t ent = lds_u16(lst_a + k0 * 2);
+            q = ent & 0xfffu;
+            // the cell's lower-x voxel in the segment, and this lane's weight half
+            const int vlo = static_cast<int>(lds_u32(lo_a + q * 4)) - (1 + sgi * 32);
+            const uint32_t w2 = lds_u32(wt_a + q * (NWW * 4) + (ent >> 12) * 8);
+            wa_lo = static_cast<unsigned>(vlo) < 32u;
+            wa_hi = static_cast<unsigned>(vlo + 1) < 32u;
+            ta = tcol + vlo * 32 + (((jb ^ (vlo >> 2)) & 1) << 4);
+            tb = tcol + (vlo + 1) * 32 + (((jb ^ ((vlo + 1) >> 2)) & 1) << 4);
+            if (wa_lo) sts_u16(ta, w2);
+            if (wa_hi) sts_u16(tb, w2 >> 16);
           }
           __syncwarp();
           // B (grad_out rows) for every n-tile pair, then A one m-tile at a time
           uint32_t bq[NT / 2][4];
-          const unsigned char* rowp = go_s + static_cast<size_t>(q) * ROWB;
+          const uint32_t rowa = go_a + q * ROWB;
 #pragma unroll
           for (int jp = 0; jp < NT / 2; ++jp)
-            ldmatrix_x4_trans_m(smem_addr(ok ? rowp + vm_swz<NT>(2 * jp + jo, q) * 16 : zrow),
+            ldmatrix_x4_trans_m(ok ? rowa + (vm_swz<NT>(2 * jp + jo, static_cast<int>(q)) << 4) : zrow_a,
                                 bq[jp][0], bq[jp][1], bq[jp][2], bq[jp][3]);
 #pragma unroll
           for (int mi = 0; mi < 2; ++mi) {
@@ -1822,8 +1877,8 @@ __global__ void __launch_bounds__(kThreads, NT > 4 ? 2 : 3)
             }
           }
           __syncwarp();
-          if (static_cast<unsigned>(vlo) < 32u) tile[vm_at(vlo, j)] = 0;
-          if (static_cast<unsigned>(vlo + 1) < 32u) tile[vm_at(vlo + 1, j)] = 0;
+          if (wa_lo) sts_u16(ta, 0u);
+          if (wa_hi) sts_u16(tb, 0u);
         }
         __syncwarp();
       }

@@ -112,6 +112,20 @@ def main() -> None:
                 ndim, 1, 97, 3, C, 3, shapes)))
             cases.append((f"{ndim}d bf16 C={C}", lambda ndim=ndim, shapes=shapes, C=C: _plain(
                 ndim, 1, 97, 3, C, 3, shapes, dtype=torch.bfloat16)))
+        # the cell-sorted backward with every level gathered per value row:
+        # tensor-core and CUDA-core voxel kernels (their layout guard reports
+        # bit 8), fp32 with parity
+        for vm in ("1", "0"):
+            for C in (16, 32, 64):
+                cases.append((f"{ndim}d bf16 sorted voxel mma={vm} C={C}",
+                              lambda ndim=ndim, shapes=shapes, vm=vm, C=C: _plain(
+                                  ndim, 2, 257, 4, C, 4, shapes, dtype=torch.bfloat16,
+                                  loc_range=(-0.5, 1.5), env={"MSDA_BWD_PATH": "sorted",
+                                                              "MSDA_VOXEL_DENSITY": "1e9",
+                                                              "MSDA_VOXEL_MMA": vm})))
+        cases.append((f"{ndim}d fp32 sorted voxel", lambda ndim=ndim, shapes=shapes: _plain(
+            ndim, 2, 257, 4, 32, 4, shapes, env={"MSDA_BWD_PATH": "sorted",
+                                                 "MSDA_VOXEL_DENSITY": "1e9"})))
         cases.append((f"{ndim}d fused bf16", lambda ndim=ndim: _fused(ndim)))
         cases.append((f"{ndim}d fused fp32 far offsets", lambda ndim=ndim: _fused(
             ndim, torch.float32, off_scale=40.0)))
