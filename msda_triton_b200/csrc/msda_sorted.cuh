@@ -193,6 +193,20 @@ __device__ __forceinline__ void cp_async(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
+// Shared-memory accesses by 32-bit shared-window address.
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void sts_u16(uint32_t a, uint32_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(static_cast<unsigned short>(v)) : "memory");
+}
 // One VB-byte chunk, asynchronously where cp.async has the width.
 template <int VB>
 __device__ __forceinline__ void stage_chunk(void* dst, const void* src) {
@@ -1201,7 +1215,11 @@ __global__ void __launch_bounds__(kThreads, 4)
   const int64_t kshift = p.acc_compact ? p.acc_start[l] : p.lv.start[l];
   const int64_t ks = key_stride(p);
   float* gbase = gacc + bh_base(p, b, h, p.acc_keys) + kshift * ks + 2 * t4;
-  const uint16_t* wts = reinterpret_cast<const uint16_t*>(rec_s);  // [16][kWStride]
+  // 32-bit shared addresses: this lane's row of the corner-weight table
+  // [16][kWStride] (high halves; the low halves 8 rows further), the
+  // grad_out rows and the zero row
+  const uint32_t wts_a = smem_addr(rec_s) + g * kWStride * 2;
+  const uint32_t go_a = smem_addr(go_s), zrow_a = smem_addr(zrow);
   // this lane's ldmatrix row: sample kr of the 16-sample step, n-tile offset jo
   const int kr = (lane & 7) + ((lane >> 3) & 1) * 8;
   const int jo = lane >> 4;
@@ -1231,9 +1249,8 @@ __global__ void __launch_bounds__(kThreads, 4)
           const uint32_t keep = (s >= ta && s < tb ? 0x0000ffffu : 0u) |
                                 (s + 1 >= ta && s + 1 < tb ? 0xffff0000u : 0u);
           const bool any = keep != 0u;
-          w[e][0] = any ? *reinterpret_cast<const uint32_t*>(wts + g * kWStride + s) & keep : 0u;
-          w[e][1] = any ? *reinterpret_cast<const uint32_t*>(wts + (8 + g) * kWStride + s) & keep
-                        : 0u;
+          w[e][0] = any ? lds_u32(wts_a + s * 2) & keep : 0u;
+          w[e][1] = any ? lds_u32(wts_a + (8 * kWStride + s) * 2) & keep : 0u;
         }
         ah0 = w[0][0];
         ah2 = w[1][0];
@@ -1242,7 +1259,7 @@ __global__ void __launch_bounds__(kThreads, 4)
       }
       const int sr = k0 + kr;
       const bool rin = sr >= ta && sr < tb;
-      const unsigned char* rowp = go_s + static_cast<size_t>(rin ? sr : 0) * ROWB;
+      const uint32_t rowa = go_a + static_cast<uint32_t>(rin ? sr : 0) * ROWB;
       // every n-tile's high-half product before the low halves, so that the
       // two products into one accumulator are NT instructions apart (C = 64:
       // per pair of n-tiles, within the register bound)
@@ -1252,8 +1269,8 @@ __global__ void __launch_bounds__(kThreads, 4)
         uint32_t bq[NP][4];
 #pragma unroll
         for (int jp = 0; jp < NP; ++jp)
-          ldmatrix_x4_trans(smem_addr(rin ? rowp + (2 * (jb + jp) + jo) * 16 : zrow), bq[jp][0],
-                            bq[jp][1], bq[jp][2], bq[jp][3]);
+          ldmatrix_x4_trans(rin ? rowa + (2 * (jb + jp) + jo) * 16 : zrow_a, bq[jp][0], bq[jp][1],
+                            bq[jp][2], bq[jp][3]);
 #pragma unroll
         for (int jp = 0; jp < NP; ++jp) {
           MmaT<T>::mma(d[2 * (jb + jp)], ah0, ah2, bq[jp][0], bq[jp][1]);
@@ -1609,20 +1626,6 @@ __device__ __forceinline__ void stmatrix_x4(uint32_t addr, uint32_t r0, uint32_t
   asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr),
                "r"(r0), "r"(r1), "r"(r2), "r"(r3)
                : "memory");
-}
-// Shared-memory accesses by 32-bit shared-window address.
-__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
-  unsigned short v;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a) : "memory");
-  return v;
-}
-__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
-  return v;
-}
-__device__ __forceinline__ void sts_u16(uint32_t a, uint32_t v) {
-  asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(static_cast<unsigned short>(v)) : "memory");
 }
 
 // The staged form of one record for the tensor-core voxel kernel: its
