@@ -412,7 +412,7 @@ def _bwd_entry_name(wl, ws_bytes):
     if _bwd_plan_is_sorted(wl, ws_bytes):
         return ("backward entry, cell-sorted (msda_dots_kernel + scan + msda_place_kernel + "
                 "msda_sdots_kernel + msda_dense_kernel / msda_dense_mma_kernel + "
-                "msda_voxel_kernel + cast)")
+                "msda_voxel_mma_kernel / msda_voxel_kernel + cast)")
     return "backward entry, gather/scatter (zero-fill + msda_bwd_kernel + cast)"
 
 
