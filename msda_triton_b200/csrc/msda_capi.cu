@@ -502,13 +502,15 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   const char* dens_env = std::getenv("MSDA_VOXEL_DENSITY");
   double max_dens = dens_env ? std::atof(dens_env) : kVoxelMaxDensity;
   // 16-bit values with C = 16, 32 or 64 form the voxel levels on the tensor
-  // cores (msda_voxel_mma_kernel; MSDA_VOXEL_MMA=0: msda_voxel_kernel).
+  // cores (msda_voxel_mma_kernel; MSDA_VOXEL_MMA=0: msda_voxel_kernel;
+  // MSDA_VOXEL_MMA=tc: msda_voxel_tc_kernel, tcgen05 with TMEM accumulators).
   const char* vm_env = std::getenv("MSDA_VOXEL_MMA");
-  const bool vmma = dtype_bytes(a.vdt) == 2 && (a.C == 16 || a.C == 32 || a.C == 64) &&
-                    !(vm_env && std::strcmp(vm_env, "0") == 0);
+  const bool mma16 = dtype_bytes(a.vdt) == 2 && (a.C == 16 || a.C == 32 || a.C == 64);
+  const bool vtc = mma16 && vm_env && std::strcmp(vm_env, "tc") == 0;
+  const bool vmma = mma16 && !vtc && !(vm_env && std::strcmp(vm_env, "0") == 0);
   // msda_voxel_kernel takes the forward's lane shape (16-byte chunks where
   // the row allows); shapes it is not instantiated for keep every level dense.
-  if (!vmma && !((ls.vb == 16 && ls.vpl <= 4) || ((ls.vb == 4 || ls.vb == 2) && ls.vpl == 1)))
+  if (!vmma && !vtc && !((ls.vb == 16 && ls.vpl <= 4) || ((ls.vb == 4 || ls.vb == 2) && ls.vpl == 1)))
     max_dens = -1.0;
   const int tile_max = (kThreads / 32) * 32;         // voxels per voxel-kernel CTA (a warp per 32)
   const int64_t row_bytes = a.C * dtype_bytes(a.vdt);
@@ -530,6 +532,7 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   const int64_t per_smp = (vmma ? (a.ndim == 3 ? 32 : 16) : 32) + 4 + row_bytes;
   int64_t cap = (vbudget - acc_bytes - bounds_max) / per_smp;
   cap = std::min<int64_t>(cap, kVoxelCap) & ~int64_t{1};
+  if (vtc) cap = kVoxelCap;  // its layout (vtc_layout) stays inside two CTAs per SM at C = 32
   if (cap < 16) max_dens = -1.0;
   SortPlan sp{};
   // 16-bit values with C = 16, 32 or 64: dense levels with at least
@@ -540,7 +543,7 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
                       !(mma_env && std::strcmp(mma_env, "0") == 0);
   const char* mma_dens_env = std::getenv("MSDA_DENSE_MMA_DENSITY");
   const double mma_dens = mma_dens_env ? std::atof(mma_dens_env) : kDenseMmaMinDensity;
-  int64_t seg = 0, vox = 0, acc_keys = 0, units = 0, max_bounds = 0;
+  int64_t seg = 0, vox = 0, acc_keys = 0, units = 0, max_bounds = 0, vtc_ncr = 0;
   int nvl = 0;
   const bool f32 = a.vdt == MSDA_FLOAT32;
   for (int64_t l = 0; l < a.L; ++l) {
@@ -563,14 +566,18 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
       const int64_t Dl = a.ndim == 3 ? p.lv.size[l][2] : 1;
       // msda_voxel_kernel: up to 8 segments of 32 voxels (a warp each) in one
       // plane; msda_voxel_mma_kernel: up to 16 (two per warp) in two planes
-      const int64_t tx = std::min<int64_t>(W, tile_max);
+      // msda_voxel_tc_kernel: four voxel rows of at most 128 voxels (one
+      // tensor-memory accumulator each), 2 planes x 2 rows in 3D, 4 rows in 2D
+      const int64_t tx = std::min<int64_t>(W, vtc ? 128 : tile_max);
       const int64_t segs = (tx + 31) / 32;
-      const int64_t nz = vmma && a.ndim == 3 && Dl >= 2 ? 2 : 1;
+      const int64_t nz = a.ndim == 3 && (vtc || (vmma && Dl >= 2)) ? 2 : 1;
       const int64_t wseg = vmma ? 2 * nw : nw;
-      int64_t ny = std::max<int64_t>(1, std::min<int64_t>(wseg / (segs * nz), Hl));
+      int64_t ny = vtc ? (a.ndim == 3 ? 2 : 4)
+                       : std::max<int64_t>(1, std::min<int64_t>(wseg / (segs * nz), Hl));
       const int64_t zr = a.ndim == 3 ? nz + 1 : 1;
       const double rounds = vmma ? 1.0 : 2.0;
-      while (ny > 1 && static_cast<double>(zr * (ny + 1) * (tx + 1)) * dens > rounds * cap) --ny;
+      while (!vtc && ny > 1 && static_cast<double>(zr * (ny + 1) * (tx + 1)) * dens > rounds * cap)
+        --ny;
       VoxTile vt;
       vt.tx = static_cast<int32_t>(tx);
       vt.ny = static_cast<int32_t>(ny);
@@ -581,6 +588,7 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
       // two per segment and cell row; then the cell rows' offsets
       const int64_t nbr = vmma ? vm_bounds_per_row(static_cast<int>(segs)) : tx + 2;
       max_bounds = std::max<int64_t>(max_bounds, zr * (ny + 1) * nbr + zr * (ny + 1) + 1);
+      vtc_ncr = std::max<int64_t>(vtc_ncr, zr * (ny + 1));
       sp.voxel_mask |= 1 << l;
       sp.vl_level[nvl] = static_cast<int32_t>(l);
       sp.vl_tile[nvl] = vt;
@@ -641,8 +649,11 @@ bool plan_sorted(const Args& a, const Problem& p, const LaunchShape& ls, BwdPlan
   sp.vnv = p.nv;
   sp.div_nv = make_fdiv(static_cast<uint32_t>(std::max<int32_t>(p.nv, 1)));
   sp.vsmem = static_cast<int32_t>(acc_bytes + cap * per_smp + max_bounds * 4);
-  sp.vmma = vmma ? 1 : 0;
-  if (nvl > 0 && sp.vsmem > 100 * 1024) return false;
+  sp.vmma = vtc ? 2 : vmma ? 1 : 0;
+  if (vtc)  // its layout from a 1024-byte aligned base
+    sp.vsmem = 1024 + vtc_layout(static_cast<int>(a.C / 8), static_cast<int>(a.ndim),
+                                 static_cast<int>(cap), static_cast<int>(vtc_ncr)).end;
+  if (nvl > 0 && sp.vsmem > (vtc ? 200 : 100) * 1024) return false;
   sp.div_lp = make_fdiv(static_cast<uint32_t>(a.L * a.P));
   sp.div_p = make_fdiv(static_cast<uint32_t>(a.P));
   sp.div_h = make_fdiv(static_cast<uint32_t>(a.H));

@@ -109,7 +109,8 @@ struct SortPlan {
   int32_t vnv;                     // msda_voxel_kernel: VB-byte chunks per channel row
   FastDiv div_nv;                  // / vnv
   int32_t vsmem;                   // its dynamic shared memory
-  int32_t vmma;                    // voxel levels on msda_voxel_mma_kernel instead (16-bit, C = 16/32/64)
+  int32_t vmma;                    // voxel levels on the tensor cores (16-bit, C = 16/32/64):
+                                   // 1 msda_voxel_mma_kernel, 2 msda_voxel_tc_kernel
   FastDiv div_lp, div_p, div_h, div_l, div_q;
   int32_t sdots_mask;              // levels whose dot products msda_sdots_kernel takes in sorted order
   int32_t nsl;                     // such levels
@@ -1925,6 +1926,362 @@ __global__ void __launch_bounds__(kThreads, NT > 4 ? 2 : 3)
       reinterpret_cast<uint4*>(wa)[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncwarp();
   }
+}
+
+// ------------------------------------------------------------------ voxel levels, tcgen05
+// The voxel-level value gradient of 16-bit values (C = 8 * NT, NT 2, 4 or 8)
+// on the fifth-generation tensor cores.  A CTA takes four voxel rows of at
+// most 128 voxels (3D: 2 planes x 2 rows; 2D: 4 rows); each row is one
+// 128 x C fp32 accumulator in tensor memory (TMEM), formed as
+//   D[v][ch] = sum over the samples s of the row's 2^(d-1) cell rows of
+//              A[v][s] * go[s][ch],
+// A[v][s] = a * w of sample s's corner at voxel v (two entries per sample,
+// split into 16-bit high and low halves, two products).  Warp R (0-3) owns
+// row R: per step of 16 staged slots it writes their weights into its
+// zeroed 128 x 16 A tiles (K-major, no swizzle), fences them for the tensor
+// core, and one lane issues `tcgen05.mma ... kind::f16` for the high and the
+// low halves against 16 consecutive staged grad_out rows and commits to the
+// row's mbarrier; the warp waits (bounded) and clears what it wrote.  The
+// staged grad_out rows are the B operand in place: their chunk XOR (see
+// vm_swz) is the 32/64/128-byte swizzle of the MN-major layout for 32, 64
+// and 128-byte rows, so no copy is made.  A step starts at a multiple of 8
+// slots and may take slots of other cell rows or past the staged ones: their
+// A entries are zero and the rows past the end are zero-filled.  The
+// epilogue reads the accumulators with `tcgen05.ld` (warp w: TMEM lanes
+// 32 (w mod 4) ..) and stores each voxel row once in the value dtype.
+// Every wait is bounded: on a timeout the warp stops issuing, the kernel
+// frees its TMEM and returns, and g_msda_tc_timeouts counts it (checked
+// build: bit 16 of the check word).
+
+__device__ unsigned int g_msda_tc_timeouts;
+
+// Shared-memory matrix descriptor (tcgen05): start address, leading and
+// stride byte offsets (16-byte units), descriptor version 1, layout type
+// (0: no swizzle; 6, 4, 2: 32, 64, 128-byte swizzle).
+__device__ __forceinline__ uint64_t tc_sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                             uint32_t layout) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3fffu) |
+         (static_cast<uint64_t>((lbo >> 4) & 0x3fffu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3fffu) << 32) | (uint64_t{1} << 46) |
+         (static_cast<uint64_t>(layout & 7u) << 61);
+}
+// Instruction descriptor of kind::f16: fp32 accumulator, 16-bit A and B of
+// type T (bf16 or f16), A K-major, B MN-major, N columns, M = 128.
+template <typename T>
+__device__ __forceinline__ uint32_t tc_idesc(uint32_t n) {
+  const uint32_t ab = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  return (1u << 4) | (ab << 7) | (ab << 10) | (1u << 16) | ((n >> 3) << 17) | ((128u >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   mbar)
+               : "memory");
+}
+// mbarrier phase wait with an iteration limit; false when it ran out.
+__device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity) {
+  for (int it = 0; it < (1 << 20); ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred P1;\n mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n"
+        " selp.b32 %0, 1, 0, P1;\n}"
+        : "=r"(done)
+        : "r"(mbar), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+// 16 consecutive fp32 TMEM columns of this warp's 32 lanes.
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// Layout of msda_voxel_tc_kernel's dynamic shared memory (byte offsets from
+// a 1024-byte aligned base), shared with the host plan.
+struct VtcLayout {
+  int32_t a, go, wt, lo, cr, bnd, mbar, end;
+};
+__host__ __device__ constexpr int vtc_rows_extra() { return 24; }  // zero rows after the staged ones
+__host__ __device__ inline VtcLayout vtc_layout(int nt, int ndim, int vcap, int ncr) {
+  VtcLayout L{};
+  const int rowb = 16 * nt;
+  const int nww = (ndim == 3 ? 4 : 2) * 2;
+  L.a = 0;                                              // 4 rows x (high, low) x 4 KB
+  L.go = 4 * 2 * 4096;                                  // (vcap + extra) x rowb, 1024-aligned
+  L.wt = L.go + ((vcap + vtc_rows_extra()) * rowb + 1023) / 1024 * 1024;  // vcap x nww words
+  L.lo = L.wt + vcap * nww * 4;                         // vcap x 4 (x offset)
+  L.cr = L.lo + vcap * 4;                               // vcap bytes (cell row iz << 4 | iy)
+  L.bnd = L.cr + (vcap + 15) / 16 * 16;                 // ncr x 2 bounds, then ncr + 1 offsets
+  L.mbar = L.bnd + ((ncr * 3 + 1) * 4 + 15) / 16 * 16;  // 4 mbarriers, TMEM slot, flags
+  L.end = L.mbar + 64;
+  return L;
+}
+
+template <typename T, int NDIM, int NT>
+__global__ void __launch_bounds__(kThreads, 2)
+    msda_voxel_tc_kernel(const Problem p, const SortPlan sp, const T* __restrict__ grad_out,
+                         T* __restrict__ grad_value) {
+  constexpr int ROWB = 16 * NT;                 // grad_out row bytes
+  constexpr int N = 8 * NT;                     // channels: accumulator columns per voxel row
+  constexpr int NR = NDIM == 3 ? 4 : 2;         // cell rows per voxel row
+  constexpr int NWW = NR * 2;                   // weight words per staged sample
+  constexpr int VR = 4;                         // voxel rows per CTA
+  constexpr uint32_t TCOLS = VR * N < 32 ? 32 : VR * N;  // TMEM columns (a power of 2)
+  constexpr uint32_t BLAYOUT = NT == 2 ? 6u : NT == 4 ? 4u : 2u;  // B swizzle: 32 / 64 / 128 B
+  extern __shared__ __align__(16) unsigned char vsm[];
+  const int lane = static_cast<int>(threadIdx.x & 31u);
+  const int warp = static_cast<int>(threadIdx.x >> 5);
+  const VoxUnit U = voxel_unit<NDIM>(p, sp);
+  const int nzp = NDIM == 3 ? U.vt.nz : 1;      // voxel planes of the tile (ny * nzp = VR)
+  const int D = NDIM == 3 ? p.lv.size[U.l][2] : 1;
+  const int nyr = U.vt.ny + 1;
+  const int ncr = (NDIM == 3 ? nzp + 1 : 1) * nyr;  // cell rows (iz, iy), iz slowest
+  const uint32_t pad = ((smem_addr(vsm) + 1023u) & ~1023u) - smem_addr(vsm);
+  unsigned char* base = vsm + pad;
+  const VtcLayout LY = vtc_layout(NT, NDIM, sp.vcap, ncr);
+  {
+    // the layout inside the launch's dynamic shared memory, or no access at
+    // all (checked build: bit 8 of the check word)
+    uint32_t dyn;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+    if (pad + static_cast<uint32_t>(LY.end) > dyn) {
+#ifdef MSDA_CHECKED
+      if (threadIdx.x == 0) atomicOr(p.check_flag, 8u);
+#endif
+      return;
+    }
+  }
+  const uint32_t a_a = smem_addr(base + LY.a), go_a = smem_addr(base + LY.go);
+  uint32_t* wt_s = reinterpret_cast<uint32_t*>(base + LY.wt);
+  int32_t* lo_s = reinterpret_cast<int32_t*>(base + LY.lo);
+  uint8_t* cr_s = base + LY.cr;
+  int32_t* bnd_s = reinterpret_cast<int32_t*>(base + LY.bnd);  // ncr x 2
+  int32_t* off_s = bnd_s + ncr * 2;                              // ncr + 1
+  uint64_t* mbar_s = reinterpret_cast<uint64_t*>(base + LY.mbar);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(base + LY.mbar + 8 * VR);
+  uint32_t* any_s = tslot + 1;                  // per voxel row: a product was issued
+  uint32_t* bad_s = tslot + 2;                  // a wait ran out
+
+  // zero A tiles; mbarriers; TMEM; each cell row's range (start of cell 0,
+  // start of cell TX+1 = the row's end)
+  for (int i = threadIdx.x; i < 4 * 2 * 4096 / 16; i += kThreads)
+    reinterpret_cast<uint4*>(base + LY.a)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (threadIdx.x < VR) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(mbar_s + threadIdx.x)));
+    any_s[0] = 0u;
+  }
+  if (threadIdx.x == 0) {
+    *bad_s = 0u;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(tslot)),
+                 "r"(TCOLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  for (int i = threadIdx.x; i < ncr * 2; i += kThreads) {
+    const int cr = i >> 1, iz = cr / nyr, iy = cr - iz * nyr;
+    const int32_t yc = U.y0 - 1 + iy, zc = NDIM == 3 ? U.vz - 1 + iz : -1;
+    const int c = (i & 1) ? U.cw - 1 : 0;
+    if (yc <= U.Hs - 1 && zc <= D - 1)
+      cp_async<4>(bnd_s + i, sp.cnt + U.kb + ((zc + 1) * U.cyn + (yc + 1)) * U.cxn +
+                                 min(U.x0 + c, U.cxn));
+    else
+      bnd_s[i] = 0;  // rows outside the level are empty
+  }
+  cp_async_wait_all();
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tslot;
+  if (threadIdx.x == 0) {
+    int32_t o = 0;
+    for (int cr = 0; cr < ncr; ++cr) {
+      off_s[cr] = o;
+      o += bnd_s[2 * cr + 1] - bnd_s[2 * cr];
+    }
+    off_s[ncr] = o;
+  }
+  __syncthreads();
+  const int32_t total = off_s[ncr];
+
+  // this warp's voxel row (warps 0-3): plane pz, row ry
+  const int R = warp;
+  const int pz = R / U.vt.ny, ry = R - (R / U.vt.ny) * U.vt.ny;
+  const bool issuer = warp < VR && U.y0 + ry < U.Hs && U.vz + pz < D;
+  const int j = lane & 15, hl = lane >> 4;      // this lane's slot of a step, its weight half
+  const uint32_t tile = a_a + static_cast<uint32_t>(R * 2 + hl) * 4096u;  // its A tile
+  const uint32_t idesc = tc_idesc<T>(N);
+  const uint32_t mbar = smem_addr(mbar_s + (R & 3));
+  uint32_t phase = 0;
+  bool started = false;
+
+  for (int32_t q0 = 0; q0 < total; q0 += sp.vcap) {
+    const int nr = min(sp.vcap, total - q0);
+    // stage the round (every product of the previous one has completed):
+    // per slot its cell row, record (into registers), corner weights as
+    // 16-bit halves, x offset and grad_out row; zero rows past the end
+    if (q0 > 0) __syncthreads();
+    {
+      uint4 r0[2], r1[2];
+      int crs[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int q = threadIdx.x + i * kThreads;
+        crs[i] = -1;
+        if (q < nr) {
+          const int32_t qq = q0 + q;
+          int lo = 0, hi = ncr;  // cell row: off_s[lo] <= qq < off_s[lo + 1]
+          while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (off_s[mid] <= qq) lo = mid; else hi = mid;
+          }
+          crs[i] = lo;
+          ld_rec(sp.srec + bnd_s[2 * lo] + (qq - off_s[lo]), r0[i], r1[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        if (crs[i] < 0) continue;
+        const int q = threadIdx.x + i * kThreads;
+        const int cr = crs[i];
+        const int iz = cr / nyr, iy = cr - iz * nyr;
+        // the cell's x offset in the tile (cell i0x = x0 + offset - 1)
+        lo_s[q] = static_cast<int32_t>(r1[i].y) -
+                  (U.kb + ((U.vz + iz) * U.cyn + (U.y0 + iy)) * U.cxn) - U.x0;
+        cr_s[q] = static_cast<uint8_t>((iz << 4) | iy);
+        uint32_t wt[NWW];
+        vm_stage_weights<T, NDIM>(r0[i], wt);
+        uint4* wq = reinterpret_cast<uint4*>(wt_s + static_cast<size_t>(q) * NWW);
+#pragma unroll
+        for (int k = 0; k < NWW / 4; ++k)
+          wq[k] = make_uint4(wt[4 * k], wt[4 * k + 1], wt[4 * k + 2], wt[4 * k + 3]);
+        const char* src = reinterpret_cast<const char*>(grad_out) + static_cast<int64_t>(r1[i].x) * ROWB;
+#pragma unroll
+        for (int c = 0; c < NT; ++c)
+          cp_async<16>(base + LY.go + static_cast<size_t>(q) * ROWB + vm_swz<NT>(c, q) * 16,
+                       src + c * 16);
+      }
+      for (int i = threadIdx.x; i < vtc_rows_extra() * ROWB / 16; i += kThreads)
+        reinterpret_cast<uint4*>(base + LY.go + static_cast<size_t>(nr) * ROWB)[i] =
+            make_uint4(0u, 0u, 0u, 0u);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    if (!issuer) continue;
+    // the row's two blocks of slots (3D: cell planes pz and pz+1, each the
+    // cell rows ry and ry+1; 2D: one block), in this round's slots
+#pragma unroll
+    for (int blk = 0; blk < (NDIM == 3 ? 2 : 1); ++blk) {
+      const int cr0 = (NDIM == 3 ? pz + blk : 0) * nyr + ry;
+      const int32_t a = max(off_s[cr0] - q0, 0), e = min(off_s[cr0 + 2] - q0, nr);
+      for (int32_t s0 = a & ~7; s0 < e; s0 += 16) {
+        if (__shfl_sync(0xffffffffu, *bad_s, 0)) break;  // warp-uniform
+        const int32_t q = s0 + j;
+        uint32_t ta = 0, tb = 0;
+        bool wl = false, wh = false;
+        if (q >= a && q < e) {
+          const uint32_t code = cr_s[q];
+          const int dz = NDIM == 3 ? pz + 1 - static_cast<int>(code >> 4) : 0;
+          const int dy = ry + 1 - static_cast<int>(code & 15u);
+          const uint32_t w2 = wt_s[static_cast<size_t>(q) * NWW + (dz * 2 + dy) * 2 + hl];
+          const int v = lo_s[q] - 1;  // the cell's lower-x voxel in the row
+          // K-major, no swizzle: (v, k) at (v / 8) * 256 + (k / 8) * 128 + (v % 8) * 16 + (k % 8) * 2
+          const uint32_t kb2 = static_cast<uint32_t>((j >> 3) * 128 + (j & 7) * 2);
+          wl = static_cast<unsigned>(v) < 128u;
+          wh = static_cast<unsigned>(v + 1) < 128u;
+          ta = tile + static_cast<uint32_t>((v >> 3) * 256 + (v & 7) * 16) + kb2;
+          tb = tile + static_cast<uint32_t>(((v + 1) >> 3) * 256 + ((v + 1) & 7) * 16) + kb2;
+          if (wl) sts_u16(ta, w2);
+          if (wh) sts_u16(tb, w2 >> 16);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          const uint64_t bd = tc_sdesc(go_a + static_cast<uint32_t>(s0) * ROWB, 16, 8 * ROWB, BLAYOUT);
+          const uint32_t ah = a_a + static_cast<uint32_t>(R * 2) * 4096u;
+          tc_mma(tmem + static_cast<uint32_t>(R * N), tc_sdesc(ah, 128, 256, 0), bd, idesc,
+                 started ? 1u : 0u);
+          tc_mma(tmem + static_cast<uint32_t>(R * N), tc_sdesc(ah + 4096u, 128, 256, 0), bd, idesc, 1u);
+          tc_commit(mbar);
+        }
+        started = true;
+        const bool ok = mbar_wait(mbar, phase);
+        phase ^= 1u;
+        if (!ok && lane == 0) {
+          atomicAdd(&g_msda_tc_timeouts, 1u);
+#ifdef MSDA_CHECKED
+          atomicOr(p.check_flag, 0x10000u);
+#endif
+          *bad_s = 1u;
+        }
+        __syncwarp();
+        if (wl) sts_u16(ta, 0u);
+        if (wh) sts_u16(tb, 0u);
+      }
+    }
+    if (lane == 0 && started) atomicOr(any_s, 1u << R);
+  }
+  // every issued product has completed (each step waited): read each valid
+  // row's accumulators (warp w: voxels 32 (w mod 4) .., rows w / 4, + 2),
+  // round once and store; rows without samples are zero
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  {
+    const uint32_t anyb = *any_s;
+    const bool bad = *bad_s != 0u;
+    const int qd = warp & 3;
+    const int v = 32 * qd + lane;
+    const int64_t ks = key_stride(p);
+    T* gvb = grad_value + bh_base(p, U.b, U.h, p.K);
+    for (int rr = warp >> 2; rr < VR; rr += kThreads / 32 / 4) {
+      const int pz2 = rr / U.vt.ny, ry2 = rr - (rr / U.vt.ny) * U.vt.ny;
+      if (U.y0 + ry2 >= U.Hs || U.vz + pz2 >= D) continue;  // warp-uniform
+      uint32_t r[N];
+      if (((anyb >> rr) & 1u) && !bad) {
+#pragma unroll
+        for (int c16 = 0; c16 < N / 16; ++c16)
+          tc_ld16(tmem + (static_cast<uint32_t>(qd * 32) << 16) + static_cast<uint32_t>(rr * N + c16 * 16),
+                  r + 16 * c16);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      } else {
+#pragma unroll
+        for (int c = 0; c < N; ++c) r[c] = 0u;
+      }
+      const int32_t xv = U.x0 + v;
+      if (v < U.vt.tx && xv < U.W) {
+        const int64_t key = static_cast<int64_t>(p.lv.start[U.l]) +
+                            (static_cast<int64_t>(U.vz + pz2) * U.Hs + (U.y0 + ry2)) * U.W + xv;
+        uint4* dst = reinterpret_cast<uint4*>(gvb + key * ks);
+#pragma unroll
+        for (int c8 = 0; c8 < N / 8; ++c8) {
+          const float* f = reinterpret_cast<const float*>(r + 8 * c8);
+          dst[c8] = make_uint4(MmaT<T>::pack(f[0], f[1]), MmaT<T>::pack(f[2], f[3]),
+                               MmaT<T>::pack(f[4], f[5]), MmaT<T>::pack(f[6], f[7]));
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
 }
 
 }  // namespace msda

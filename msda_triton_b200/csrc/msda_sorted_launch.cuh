@@ -110,6 +110,23 @@ static cudaError_t voxel_mma_one(const Problem& p, const SortPlan& sp, const voi
   return cudaErrorInvalidValue;
 }
 
+template <typename T, int NDIM, int NT>
+static cudaError_t voxel_tc_one(const Problem& p, const SortPlan& sp, const void* go, void* gv,
+                                cudaStream_t st) {
+  if constexpr (sizeof(T) == 2) {
+    const int64_t units = p.B * p.H * int64_t{sp.units_per_bh};
+    cudaError_t err = cudaFuncSetAttribute(msda_voxel_tc_kernel<T, NDIM, NT>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, sp.vsmem);
+    if (err != cudaSuccess) return err;
+    msda_voxel_tc_kernel<T, NDIM, NT>
+        <<<dim3(static_cast<unsigned>(units)), kThreads, static_cast<size_t>(sp.vsmem), st>>>(
+            p, sp, static_cast<const T*>(go), static_cast<T*>(gv));
+    return cudaGetLastError();
+  }
+  (void)p; (void)sp; (void)go; (void)gv; (void)st;
+  return cudaErrorInvalidValue;
+}
+
 // The forward shape: chunk bytes 16 (VPL 1, 2, 4) or 4 / 2 (VPL 1 or 8).
 #define MSDA_FWD_SHAPE_SWITCH(vb, vpl, CALL)                                        \
   switch (vb * 16 + vpl) {                                                          \
@@ -174,7 +191,15 @@ static cudaError_t sorted_chunk(const LaunchShape& ls, const LaunchShape& lsd, c
     }
     if (err != cudaSuccess) return err;
   }
-  if (sp.nvl > 0 && sp.vmma) {
+  if (sp.nvl > 0 && sp.vmma == 2) {
+    switch (p.C) {
+      case 16: err = voxel_tc_one<T, NDIM, 2>(p, sp, go, gv, st); break;
+      case 32: err = voxel_tc_one<T, NDIM, 4>(p, sp, go, gv, st); break;
+      case 64: err = voxel_tc_one<T, NDIM, 8>(p, sp, go, gv, st); break;
+      default: return cudaErrorInvalidValue;
+    }
+    if (err != cudaSuccess) return err;
+  } else if (sp.nvl > 0 && sp.vmma) {
     switch (p.C) {
       case 16: err = voxel_mma_one<T, NDIM, 2>(p, sp, go, gv, st); break;
       case 32: err = voxel_mma_one<T, NDIM, 4>(p, sp, go, gv, st); break;

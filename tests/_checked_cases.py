@@ -115,7 +115,7 @@ def main() -> None:
         # the cell-sorted backward with every level gathered per value row:
         # tensor-core and CUDA-core voxel kernels (their layout guard reports
         # bit 8), fp32 with parity
-        for vm in ("1", "0"):
+        for vm in ("1", "tc", "0"):
             for C in (16, 32, 64):
                 cases.append((f"{ndim}d bf16 sorted voxel mma={vm} C={C}",
                               lambda ndim=ndim, shapes=shapes, vm=vm, C=C: _plain(

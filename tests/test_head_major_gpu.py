@@ -50,6 +50,8 @@ PLANS = {
     "sorted-voxel": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "1e9"},
     "sorted-voxel-cc": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "1e9",
                         "MSDA_VOXEL_MMA": "0"},
+    "sorted-voxel-tc": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "1e9",
+                        "MSDA_VOXEL_MMA": "tc"},
     "sorted-cell-sdots": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "0",
                           "MSDA_SORTED_DOTS_MB": "0"},
     "sorted-cell-mma": {"MSDA_BWD_PATH": "sorted", "MSDA_VOXEL_DENSITY": "0",

@@ -203,16 +203,18 @@ def test_dense_cuda_core_and_tensor_core_agree(monkeypatch, case, dtype):
 @pytest.mark.parametrize("case", CASES, ids=[f"{c[0]}d-{len(c[6])}lvl-q{c[2]}" for c in CASES])
 def test_voxel_cuda_core_and_tensor_core_agree(monkeypatch, case, dtype):
     """16-bit values: the per-row gather of voxel levels on the tensor cores
-    (the default for C = 16, 32, 64; weights split into two 16-bit halves)
-    and on the CUDA cores (MSDA_VOXEL_MMA=0) both meet the half-precision bar
-    against the oracle, with every level gathered per row, in-range and
-    clamped (out-of-range) locations."""
+    (`mma.sync`, the default for C = 16, 32, 64; weights split into two
+    16-bit halves), on the fifth-generation tensor cores (MSDA_VOXEL_MMA=tc:
+    tcgen05 with accumulators in tensor memory) and on the CUDA cores
+    (MSDA_VOXEL_MMA=0) all meet the half-precision bar against the oracle,
+    with every level gathered per row, in-range and clamped (out-of-range)
+    locations."""
     ndim, B, Q, H, C, P, shapes = case
     for clamp, rng in ((True, (0.0, 1.0)), (False, (-0.15, 1.15))):
         inp = _cast(make_inputs(B, Q, H, C, P, shapes, seed=5 * Q + C, loc_range=rng),
                     dtype, dtype)
         ref = oracle_all(*_upcast(inp), clamp=clamp)
-        for mma in ("1", "0"):
+        for mma in ("1", "tc", "0"):
             _env(monkeypatch, "voxel")
             monkeypatch.setenv("MSDA_VOXEL_MMA", mma)
             got = cuda_fwd_bwd(ndim, *inp, clamp=clamp)
