@@ -457,8 +457,9 @@ size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
 // the value gradient is formed: gathered per value row (levels with at most
 // kVoxelMaxDensity samples per cell and (b, h)) or aggregated per cell in
 // registers and flushed with fp32 reductions (denser levels).  Measured on
-// the 3D xl workload (B=8, bf16): level 0 (0.38 samples per cell) 6.9 ms
-// gathered; level 1 (3.0 per cell) 7.5 ms gathered against ~2 ms aggregated.
+// the 3D xl workload (B=8, bf16): level 0 (0.38 samples per cell) 4.07 ms
+// gathered on the tensor cores; level 1 (2.9 per cell) 4.2 ms gathered there
+// against 2.0 ms aggregated (on the CUDA cores: 7.5 against ~2 ms).
 constexpr int64_t kSortedMinSamples = int64_t{1} << 20;
 constexpr double kVoxelMaxDensity = 2.0;
 constexpr bool kSortedByDefault = true;

@@ -64,7 +64,8 @@ __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
   return static_cast<uint32_t>((static_cast<uint64_t>(n) * f.m) >> f.shift);
 }
 
-// Tile of msda_voxel_kernel on one level: NY voxel rows x TX voxels.
+// Tile of the voxel kernels on one level: NZ voxel planes x NY rows x TX
+// voxels (NZ = 1 for msda_voxel_kernel).
 struct VoxTile {
   int32_t tx, ny, nz; // voxels per row segment, rows and planes per CTA
   int32_t ntx, nty;   // tiles along x and y
