@@ -221,6 +221,22 @@ def test_voxel_cuda_core_and_tensor_core_agree(monkeypatch, case, dtype):
             check_all(got, ref, TOL_HALF, TOL_HALF, f"{case} {dtype} voxel mma={mma} clamp={clamp}")
 
 
+@pytest.mark.parametrize("ndim", [2, 3])
+def test_voxel_tensor_core_many_staging_rounds(monkeypatch, ndim):
+    """The tensor-core voxel gather with a shared-memory budget of 24 KB:
+    about 24 samples staged per round, so every tile runs many rounds (the
+    accumulators carry across them, and a warp's second segment restages
+    them).  bf16 against the oracle at the half-precision bar."""
+    shapes = [(30, 40), (15, 20)] if ndim == 2 else [(10, 24, 24), (5, 12, 12)]
+    inp = _cast(make_inputs(2, 700, 4, 32, 4, shapes, seed=29 + ndim, loc_range=(-0.1, 1.1)),
+                torch.bfloat16, torch.bfloat16)
+    ref = oracle_all(*_upcast(inp))
+    _env(monkeypatch, "voxel")
+    monkeypatch.setenv("MSDA_VOXEL_SMEM_KB", "24")
+    got = cuda_fwd_bwd(ndim, *inp)
+    check_all(got, ref, TOL_HALF, TOL_HALF, f"{ndim}d voxel mma, 24 KB staging")
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("path", ["sorted", "scatter"])
 def test_module_like_clustered_half_precision(monkeypatch, path, dtype):
