@@ -258,6 +258,34 @@ MSDA_API int msda3d_fused_bwd(const void* value, int value_dtype, int64_t batch,
                void* grad_attention_logits, void* workspace, size_t workspace_bytes,
                void* stream);
 
+/* The same prologue as its own pass, for problems that run the unfused
+ * entries (the cell-sorted backward has no fused form).  It replaces the
+ * tensor operations of the modules (src/msda_triton/pytorch/msda_3d.py:
+ * 336-350, src/msda_triton/pytorch/msda_2d.py:325-339).  spatial_shapes:
+ * host, the reference's order per level; every tensor in sampling_dtype:
+ *   reference_points (B, Q, L, d), sampling_offsets (B, Q, H, L, P, d),
+ *   attention_logits (B, Q, H, L*P) ->
+ *   sampling_locations (B, Q, H, L, P, d), attention_weights (B, Q, H, L, P)
+ * A location has the rounding of `reference_points + sampling_offsets /
+ * normalizer` in sampling_dtype (size converted to it, quotient rounded,
+ * then the sum); the weights are the fused entries' row softmax.  The
+ * backward takes the forward's attention_weights and the two gradients and
+ * writes grad_sampling_offsets, grad_attention_logits (sampling_dtype) and
+ * grad_reference_partial, fp32 (B, Q, H, L, d): the sum over points of the
+ * location gradient (its sum over H is the reference-point gradient). */
+MSDA_API int msda_prologue_fwd(int ndim, int64_t batch, int64_t num_queries, int64_t num_heads,
+               int64_t num_levels, int64_t num_points, const int32_t* spatial_shapes,
+               const void* reference_points, const void* sampling_offsets,
+               const void* attention_logits, int sampling_dtype, void* sampling_locations,
+               void* attention_weights, void* stream);
+
+MSDA_API int msda_prologue_bwd(int ndim, int64_t batch, int64_t num_queries, int64_t num_heads,
+               int64_t num_levels, int64_t num_points, const int32_t* spatial_shapes,
+               const void* attention_weights, const void* grad_sampling_locations,
+               const void* grad_attention_weights, int sampling_dtype,
+               float* grad_reference_partial, void* grad_sampling_offsets,
+               void* grad_attention_logits, void* stream);
+
 /* Workspace bytes of msda{2,3}d_fused_bwd (always the gather/scatter plan). */
 MSDA_API size_t msda_fused_bwd_workspace_bytes(int ndim, int value_dtype, int64_t batch,
                                                int64_t num_keys, int64_t num_heads,

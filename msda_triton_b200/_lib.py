@@ -52,6 +52,8 @@ EXPORTED_SYMBOLS = (
     "msda2d_fused_bwd",
     "msda3d_fused_bwd",
     "msda_fused_bwd_workspace_bytes",
+    "msda_prologue_fwd",
+    "msda_prologue_bwd",
     "msda_status_string",
     "msda_last_error",
     "msda_abi_version",
@@ -87,6 +89,20 @@ _FUSED_BWD_ARGS = _FUSED_FWD_ARGS[:-2] + [
     _vp, _vp, _vp, _vp, _vp,            # grad_output, grad_value, grad_reference_partial (fp32),
                                         # grad_sampling_offsets, grad_attention_logits
     _vp, ctypes.c_size_t, _vp,          # workspace, workspace_bytes, stream
+]
+
+_PROLOGUE_FWD_ARGS = [
+    _int, _i64, _i64, _i64, _i64, _i64,  # ndim, B, Q, H, L, P
+    _vp,                                 # spatial_shapes (host int32)
+    _vp, _vp, _vp, _int,                 # reference_points, offsets, logits, sampling_dtype
+    _vp, _vp, _vp,                       # sampling_locations, attention_weights, stream
+]
+_PROLOGUE_BWD_ARGS = [
+    _int, _i64, _i64, _i64, _i64, _i64,  # ndim, B, Q, H, L, P
+    _vp,                                 # spatial_shapes (host int32)
+    _vp, _vp, _vp, _int,                 # attention_weights, grad_loc, grad_attn, sampling_dtype
+    _vp, _vp, _vp, _vp,                  # grad_reference_partial (fp32), grad_offsets,
+                                         # grad_logits, stream
 ]
 
 _ACC_ARGS = _FWD_ARGS[:-2] + [
@@ -134,6 +150,10 @@ def lib() -> ctypes.CDLL:
             for name in ("msda2d_fused_bwd", "msda3d_fused_bwd"):
                 getattr(handle, name).argtypes = _FUSED_BWD_ARGS
                 getattr(handle, name).restype = _int
+            handle.msda_prologue_fwd.argtypes = _PROLOGUE_FWD_ARGS
+            handle.msda_prologue_fwd.restype = _int
+            handle.msda_prologue_bwd.argtypes = _PROLOGUE_BWD_ARGS
+            handle.msda_prologue_bwd.restype = _int
             handle.msda_status_string.argtypes = [_int]
             handle.msda_status_string.restype = ctypes.c_char_p
             handle.msda_last_error.argtypes = []

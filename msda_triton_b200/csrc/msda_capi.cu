@@ -11,6 +11,7 @@
 #include "../../include/msda_b200_checked.h"
 #endif
 #include "msda_launch.cuh"
+#include "msda_prologue.cuh"
 #include "msda_sorted_launch.cuh"
 
 namespace msda {
@@ -1069,6 +1070,94 @@ int msda_cast_from_f32(const float* src, void* dst, int dst_dtype, int64_t count
   const cudaError_t err =
       msda::cast_from_f32(src, dst, dst_dtype, count, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? msda::ok() : msda::cuda_fail(err, "cast launch");
+}
+
+// The modules' sampling prologue (msda_prologue.cuh): shapes, sizes and
+// levels checked, then one launch.
+static int prologue_args(int ndim, int64_t batch, int64_t num_queries, int64_t num_heads,
+                         int64_t num_levels, int64_t num_points, const int32_t* spatial_shapes,
+                         int sampling_dtype, msda::PrologueArgs& pa) {
+  if (ndim != 2 && ndim != 3) return msda::fail(MSDA_ERROR_INVALID_ARGUMENT, "ndim must be 2 or 3");
+  if (batch < 0 || num_queries < 0 || num_heads < 0 || num_levels < 0 || num_points < 0)
+    return msda::fail(MSDA_ERROR_INVALID_ARGUMENT, "negative size");
+  if (num_levels > msda::kMaxLevels)
+    return msda::fail(MSDA_ERROR_TOO_MANY_LEVELS, "num_levels %lld > %d",
+                      static_cast<long long>(num_levels), msda::kMaxLevels);
+  if (num_levels * num_points > (int64_t{1} << 20))
+    return msda::fail(MSDA_ERROR_INVALID_ARGUMENT, "num_levels * num_points above 2^20");
+  if (batch * num_queries * num_heads >= (int64_t{1} << 31))
+    return msda::fail(MSDA_ERROR_INVALID_ARGUMENT, "batch * num_queries * num_heads above 2^31");
+  if (msda::dtype_bytes(sampling_dtype) == 0)
+    return msda::fail(MSDA_ERROR_UNSUPPORTED_DTYPE, "sampling_dtype %d", sampling_dtype);
+  if (num_levels > 0 && spatial_shapes == nullptr)
+    return msda::fail(MSDA_ERROR_INVALID_ARGUMENT, "NULL spatial_shapes");
+  pa = msda::PrologueArgs{};
+  pa.ndim = ndim;
+  pa.B = batch;
+  pa.Q = num_queries;
+  pa.H = num_heads;
+  pa.L = num_levels;
+  pa.P = num_points;
+  // rows of spatial_shapes in the reference's order ((H, W) or (D, H, W));
+  // axis 0 of a location is x
+  for (int64_t l = 0; l < num_levels; ++l)
+    for (int ax = 0; ax < ndim; ++ax) pa.size[l][ax] = spatial_shapes[l * ndim + (ndim - 1 - ax)];
+  return MSDA_SUCCESS;
+}
+
+static bool prologue_buffers_ok(const void* const* bufs, int n, int elem) {
+  for (int i = 0; i < n; ++i)
+    if (bufs[i] == nullptr || !msda::aligned(bufs[i], elem)) return false;
+  return true;
+}
+
+int msda_prologue_fwd(int ndim, int64_t batch, int64_t num_queries, int64_t num_heads,
+                      int64_t num_levels, int64_t num_points, const int32_t* spatial_shapes,
+                      const void* reference_points, const void* sampling_offsets,
+                      const void* attention_logits, int sampling_dtype,
+                      void* sampling_locations, void* attention_weights, void* stream) {
+  msda::PrologueArgs pa;
+  const int st = prologue_args(ndim, batch, num_queries, num_heads, num_levels, num_points,
+                               spatial_shapes, sampling_dtype, pa);
+  if (st != MSDA_SUCCESS) return st;
+  if (batch * num_queries * num_heads * num_levels * num_points == 0) return msda::ok();
+  const void* bufs[5] = {reference_points, sampling_offsets, attention_logits, sampling_locations,
+                         attention_weights};
+  if (!prologue_buffers_ok(bufs, 5, msda::dtype_bytes(sampling_dtype)))
+    return msda::fail(MSDA_ERROR_MISALIGNED, "NULL or unaligned prologue buffer");
+  pa.ref = reference_points;
+  pa.off = sampling_offsets;
+  pa.logits = attention_logits;
+  pa.loc = sampling_locations;
+  pa.wout = attention_weights;
+  const cudaError_t err = msda::prologue_fwd(pa, sampling_dtype, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? msda::ok() : msda::cuda_fail(err, "prologue forward launch");
+}
+
+int msda_prologue_bwd(int ndim, int64_t batch, int64_t num_queries, int64_t num_heads,
+                      int64_t num_levels, int64_t num_points, const int32_t* spatial_shapes,
+                      const void* attention_weights, const void* grad_sampling_locations,
+                      const void* grad_attention_weights, int sampling_dtype,
+                      float* grad_reference_partial, void* grad_sampling_offsets,
+                      void* grad_attention_logits, void* stream) {
+  msda::PrologueArgs pa;
+  const int st = prologue_args(ndim, batch, num_queries, num_heads, num_levels, num_points,
+                               spatial_shapes, sampling_dtype, pa);
+  if (st != MSDA_SUCCESS) return st;
+  if (batch * num_queries * num_heads * num_levels * num_points == 0) return msda::ok();
+  const void* bufs[5] = {attention_weights, grad_sampling_locations, grad_attention_weights,
+                         grad_sampling_offsets, grad_attention_logits};
+  if (!prologue_buffers_ok(bufs, 5, msda::dtype_bytes(sampling_dtype)) ||
+      grad_reference_partial == nullptr || !msda::aligned(grad_reference_partial, 4))
+    return msda::fail(MSDA_ERROR_MISALIGNED, "NULL or unaligned prologue buffer");
+  pa.weights = attention_weights;
+  pa.gloc = grad_sampling_locations;
+  pa.gattn = grad_attention_weights;
+  pa.gref_partial = grad_reference_partial;
+  pa.goff = grad_sampling_offsets;
+  pa.glogits = grad_attention_logits;
+  const cudaError_t err = msda::prologue_bwd(pa, sampling_dtype, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? msda::ok() : msda::cuda_fail(err, "prologue backward launch");
 }
 
 static size_t workspace_bytes(int ndim, int value_dtype, int64_t batch, int64_t num_keys,

@@ -161,4 +161,73 @@ def msda3d_fused(value: torch.Tensor, value_spatial_shapes: torch.Tensor,
                   attention_logits, clamp_grid, clamp_eps)
 
 
-__all__ = ["msda2d_fused", "msda3d_fused", "MSDAFusedFn"]
+class SamplingPrologueFn(torch.autograd.Function):
+    """The prologue alone (msda_prologue_fwd / msda_prologue_bwd): locations
+    and softmax weights as tensors, for calls that then run msda{2,3}d (the
+    large-problem path of the modules, whose cell-sorted backward has no
+    fused form).  Two passes replace the module's separate tensor ops and
+    their backward: the locations round as `reference_points + offsets /
+    normalizer` does in the sampling dtype; the weights are the fused
+    kernels' row softmax."""
+
+    @staticmethod
+    def forward(ctx, ndim, shapes_host, reference_points, sampling_offsets, attention_logits):
+        off = sampling_offsets.contiguous()
+        ref = reference_points.contiguous()
+        lg = attention_logits.contiguous()
+        B, Q, H, L, P, _ = off.shape
+        loc = torch.empty_like(off)
+        w = torch.empty((B, Q, H, L, P), dtype=off.dtype, device=off.device)
+        _core.check_status(_lib.lib().msda_prologue_fwd(
+            ndim, B, Q, H, L, P, shapes_host.data_ptr(), ref.data_ptr(), off.data_ptr(),
+            lg.data_ptr(), _core._DTYPE_CODE[off.dtype], loc.data_ptr(), w.data_ptr(),
+            _core._stream_ptr(off.device)))
+        ctx.save_for_backward(w)
+        ctx.ndim, ctx.shapes_host = ndim, shapes_host
+        ctx.logits_shape = attention_logits.shape
+        return loc, w
+
+    @staticmethod
+    def backward(ctx, grad_loc, grad_w):
+        (w,) = ctx.saved_tensors
+        ndim = ctx.ndim
+        B, Q, H, L, P = w.shape
+        gl = (torch.zeros((B, Q, H, L, P, ndim), dtype=w.dtype, device=w.device)
+              if grad_loc is None else grad_loc.to(w.dtype).contiguous())
+        gw = torch.zeros_like(w) if grad_w is None else grad_w.to(w.dtype).contiguous()
+        goff = torch.empty_like(gl)
+        glg = torch.empty_like(w)
+        gref_p = torch.empty((B, Q, H, L, ndim), dtype=torch.float32, device=w.device)
+        _core.check_status(_lib.lib().msda_prologue_bwd(
+            ndim, B, Q, H, L, P, ctx.shapes_host.data_ptr(), w.data_ptr(), gl.data_ptr(),
+            gw.data_ptr(), _core._DTYPE_CODE[w.dtype], gref_p.data_ptr(), goff.data_ptr(),
+            glg.data_ptr(), _core._stream_ptr(w.device)))
+        gref = gref_p.sum(2).to(w.dtype)
+        return None, None, gref, goff, glg.view(ctx.logits_shape)
+
+
+def sampling_prologue_applies(reference_points: torch.Tensor, sampling_offsets: torch.Tensor,
+                              attention_logits: torch.Tensor) -> bool:
+    """Whether SamplingPrologueFn takes these tensors: CUDA, one of the
+    kernels' dtypes for all three, and not under torch.compile tracing
+    (which keeps the traceable tensor ops)."""
+    dt = sampling_offsets.dtype
+    return (sampling_offsets.is_cuda and reference_points.dtype == dt
+            and attention_logits.dtype == dt and dt in _core._DTYPE_CODE
+            and reference_points.device == sampling_offsets.device
+            and not torch.compiler.is_compiling())
+
+
+def sampling_prologue(ndim: int, spatial_shapes_host: torch.Tensor,
+                      reference_points: torch.Tensor, sampling_offsets: torch.Tensor,
+                      attention_logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(sampling_locations, attention_weights) from reference points (B, Q, L,
+    d), raw offsets (B, Q, H, L, P, d) and raw logits (B, Q, H, L, P) or (B,
+    Q, H, L*P), with autograd; spatial_shapes_host (L, d) on the CPU."""
+    shp = spatial_shapes_host.detach().to(torch.int32).contiguous()
+    return SamplingPrologueFn.apply(ndim, shp, reference_points, sampling_offsets,
+                                    attention_logits)
+
+
+__all__ = ["msda2d_fused", "msda3d_fused", "MSDAFusedFn", "SamplingPrologueFn",
+           "sampling_prologue", "sampling_prologue_applies"]

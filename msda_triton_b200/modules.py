@@ -10,10 +10,12 @@ itself is msda2d / msda3d of this package; with fused_prologue=True (the
 default, an extra keyword the reference's modules ignore) the locations and
 softmax weights are formed inside the kernels from the raw projections
 (msda2d_fused / msda3d_fused) instead of as separate tensors -- for calls
-below FUSED_MAX_SAMPLES samples.  Larger calls form them with torch ops and
-call msda2d / msda3d, whose backward is then the cell-sorted pipeline: on
-the 3D xl module step (B=8, Q=100000) that is 40.6 ms against 41.8 ms for
-the fused prologue, whose backward is the gather/scatter kernel.
+below FUSED_MAX_SAMPLES samples.  Larger calls form them in two passes of
+their own (fused.sampling_prologue: the same rounding as the tensor ops,
+the fused kernels' softmax) and call msda2d / msda3d, whose backward is then
+the cell-sorted pipeline (the fused kernels' backward is the gather/scatter
+one).  With fused_prologue=False, mixed dtypes or under torch.compile
+tracing, the locations and weights are the reference's tensor ops.
 
 Forward, with q the (batch-first) query and v the projected value:
     offsets = Linear(q) -> (B, Q, H, L, P, d)
@@ -31,7 +33,8 @@ import torch
 from torch import nn
 from torch.utils.checkpoint import checkpoint
 
-from msda_triton_b200.fused import msda2d_fused, msda3d_fused
+from msda_triton_b200.fused import (msda2d_fused, msda3d_fused, sampling_prologue,
+                                    sampling_prologue_applies)
 from msda_triton_b200.msda_2d import msda2d
 from msda_triton_b200.msda_3d import msda3d
 
@@ -159,9 +162,15 @@ class _MSDAModule(nn.Module):
                 run = lambda h0, h1: self._run(self._sample_fused, v[:, :, h0:h1], shapes_host,
                                                ref, offsets[:, :, h0:h1], logits[:, :, h0:h1])
             else:
-                weights = logits.view(bs, q1 - q0, H, L * P).softmax(-1)
-                weights = weights.view(bs, q1 - q0, H, L, P)
-                loc = reference_points[:, q0:q1, None, :, None, :] + offsets / normalizer
+                ref = reference_points[:, q0:q1]
+                if self.fused_prologue and sampling_prologue_applies(ref, offsets, logits):
+                    # the locations and weights in two passes of their own
+                    # (msda_prologue_fwd / _bwd) instead of the tensor ops
+                    loc, weights = sampling_prologue(d, shapes_host[:, :d], ref, offsets, logits)
+                else:
+                    weights = logits.view(bs, q1 - q0, H, L * P).softmax(-1)
+                    weights = weights.view(bs, q1 - q0, H, L, P)
+                    loc = ref[:, :, None, :, None, :] + offsets / normalizer
                 run = lambda h0, h1: self._run(self._sample, v[:, :, h0:h1], shapes_host,
                                                loc[:, :, h0:h1], weights[:, :, h0:h1])
             if hc == H:
