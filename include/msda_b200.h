@@ -272,7 +272,8 @@ MSDA_API int msda3d_fused_bwd(const void* value, int value_dtype, int64_t batch,
  * backward takes the forward's attention_weights and the two gradients and
  * writes grad_sampling_offsets, grad_attention_logits (sampling_dtype) and
  * grad_reference_partial, fp32 (B, Q, H, L, d): the sum over points of the
- * location gradient (its sum over H is the reference-point gradient). */
+ * location gradient (its sum over H is the reference-point gradient).
+ * L*P is at most 2048 (MSDA_ERROR_INVALID_ARGUMENT above). */
 MSDA_API int msda_prologue_fwd(int ndim, int64_t batch, int64_t num_queries, int64_t num_heads,
                int64_t num_levels, int64_t num_points, const int32_t* spatial_shapes,
                const void* reference_points, const void* sampling_offsets,

@@ -1083,8 +1083,8 @@ static int prologue_args(int ndim, int64_t batch, int64_t num_queries, int64_t n
   if (num_levels > msda::kMaxLevels)
     return msda::fail(MSDA_ERROR_TOO_MANY_LEVELS, "num_levels %lld > %d",
                       static_cast<long long>(num_levels), msda::kMaxLevels);
-  if (num_levels * num_points > (int64_t{1} << 20))
-    return msda::fail(MSDA_ERROR_INVALID_ARGUMENT, "num_levels * num_points above 2^20");
+  if (num_levels * num_points > 2048)
+    return msda::fail(MSDA_ERROR_INVALID_ARGUMENT, "num_levels * num_points above 2048");
   if (batch * num_queries * num_heads >= (int64_t{1} << 31))
     return msda::fail(MSDA_ERROR_INVALID_ARGUMENT, "batch * num_queries * num_heads above 2^31");
   if (msda::dtype_bytes(sampling_dtype) == 0)

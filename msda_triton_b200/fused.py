@@ -206,13 +206,20 @@ class SamplingPrologueFn(torch.autograd.Function):
         return None, None, gref, goff, glg.view(ctx.logits_shape)
 
 
+# msda_prologue_{fwd,bwd} take rows of at most this many samples (L*P).
+PROLOGUE_MAX_SAMPLES = 2048
+
+
 def sampling_prologue_applies(reference_points: torch.Tensor, sampling_offsets: torch.Tensor,
                               attention_logits: torch.Tensor) -> bool:
-    """Whether SamplingPrologueFn takes these tensors: CUDA, one of the
-    kernels' dtypes for all three, and not under torch.compile tracing
-    (which keeps the traceable tensor ops)."""
+    """Whether SamplingPrologueFn takes these tensors: CUDA, at most
+    PROLOGUE_MAX_SAMPLES samples per (b, q, h) row, one of the kernels'
+    dtypes for all three, and not under torch.compile tracing (which keeps
+    the traceable tensor ops)."""
     dt = sampling_offsets.dtype
-    return (sampling_offsets.is_cuda and reference_points.dtype == dt
+    return (sampling_offsets.is_cuda and sampling_offsets.dim() == 6
+            and sampling_offsets.shape[3] * sampling_offsets.shape[4] <= PROLOGUE_MAX_SAMPLES
+            and reference_points.dtype == dt
             and attention_logits.dtype == dt and dt in _core._DTYPE_CODE
             and reference_points.device == sampling_offsets.device
             and not torch.compiler.is_compiling())

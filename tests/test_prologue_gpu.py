@@ -72,6 +72,43 @@ def test_prologue_matches_tensor_ops(ndim, dt):
                                    msg=lambda m, n=name: f"{n}: {m}")
 
 
+def _shifted(t):
+    """The same values in a contiguous tensor whose data starts one element
+    past an allocation's start: not 16-byte aligned."""
+    buf = torch.empty(t.numel() + 1, dtype=t.dtype, device=t.device)
+    out = buf[1:].view(t.shape)
+    out.copy_(t)
+    return out
+
+
+@pytest.mark.parametrize("dt", DTYPES, ids=lambda d: str(d)[6:])
+@pytest.mark.parametrize("ndim", [2, 3])
+def test_prologue_unaligned_and_ragged(ndim, dt):
+    """Rows whose count leaves a partial vector in the last tile (Q=301, H=3,
+    P=3), through the 16-byte vector copies (aligned tensors) and the
+    element copies (tensors one element off alignment): the same bits, and
+    the tensor ops' locations and offset gradients."""
+    shp, ref, off, lg = _inputs(ndim, dt, seed=40 + ndim, Q=301, H=3, P=3)
+    g = torch.Generator().manual_seed(41)
+    gl = (torch.randn(off.shape, generator=g) * 0.5).to(DEV, dt)
+    gw = torch.randn(lg.shape, generator=g).to(DEV, dt)
+    res = []
+    for shift in (False, True):
+        ins = [_shifted(t) if shift else t.clone() for t in (ref, off, lg)]
+        assert all((t.data_ptr() % 16 != 0) == shift for t in ins[1:])
+        leaves = [t.detach().requires_grad_(True) for t in ins]
+        loc, w = sampling_prologue(ndim, shp, *leaves)
+        gouts = (_shifted(gl), _shifted(gw)) if shift else (gl, gw)
+        res.append([loc, w, *torch.autograd.grad((loc, w), leaves, gouts)])
+    for i, (a, b) in enumerate(zip(*res)):
+        assert torch.equal(a, b), f"tensor {i} differs between the vector and element copies"
+    leaves_t = [t.detach().requires_grad_(True) for t in (ref, off, lg)]
+    loc_t, w_t = _torch_prologue(shp, *leaves_t)
+    want = torch.autograd.grad((loc_t, w_t), leaves_t, (gl, gw))
+    assert torch.equal(res[0][0], loc_t)
+    assert torch.equal(res[0][3], want[1])
+
+
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("cls,ndim", [(MSDA3D, 3), (MSDA2D, 2)])
 def test_large_module_call_matches_tensor_ops(cls, ndim, dt):
