@@ -43,6 +43,48 @@ from msda_triton_b200.msda_3d import msda3d
 FUSED_MAX_SAMPLES = 1 << 20
 
 
+# Value projections over at least this many rows take _WideLinearFn.
+WIDE_LINEAR_MIN_ROWS = 1 << 20
+
+
+class _WideLinearFn(torch.autograd.Function):
+    """nn.Linear over many rows.  The forward is F.linear; the backward takes
+    the bias gradient as a product with a ones vector (one cuBLAS GEMM that
+    reads the output gradient once at HBM speed) instead of torch's sum
+    reduction, which splits inputs above 2^31 elements into several slower
+    launches.  The input and weight gradients are the usual GEMMs."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        ctx.save_for_backward(x, weight)
+        return nn.functional.linear(x, weight, bias)
+
+    @staticmethod
+    def backward(ctx, grad):
+        x, weight = ctx.saved_tensors
+        g2 = grad.reshape(-1, grad.shape[-1])
+        gx = gw = gb = None
+        if ctx.needs_input_grad[0]:
+            gx = grad @ weight
+        if ctx.needs_input_grad[1]:
+            gw = g2.t() @ x.reshape(-1, x.shape[-1])
+        if ctx.needs_input_grad[2]:
+            gb = (g2.new_ones((1, g2.shape[0])) @ g2).view(-1)
+        return gx, gw, gb
+
+
+def _project(linear: nn.Linear, x: torch.Tensor) -> torch.Tensor:
+    """linear(x), through _WideLinearFn for large CUDA inputs in the
+    parameters' dtype (no autocast, no hooks on the layer, not under
+    torch.compile tracing)."""
+    if (x.is_cuda and linear.bias is not None and x.dtype == linear.weight.dtype
+            and x.numel() // max(x.shape[-1], 1) >= WIDE_LINEAR_MIN_ROWS
+            and not torch.is_autocast_enabled("cuda") and not torch.compiler.is_compiling()
+            and not linear._forward_hooks and not linear._forward_pre_hooks):
+        return _WideLinearFn.apply(x, linear.weight, linear.bias)
+    return linear(x)
+
+
 class _MSDAModule(nn.Module):
     """Shared body of MSDA2D / MSDA3D; subclasses set NDIM, the sampling op
     and the init_weights offset pattern."""
@@ -136,7 +178,7 @@ class _MSDAModule(nn.Module):
         assert total == num_value, (
             f"Spatial shapes product {total} doesn't match value size {num_value}")
 
-        v = self.value_proj(value_in)
+        v = _project(self.value_proj, value_in)
         if key_padding_mask is not None:
             v = v.masked_fill(key_padding_mask[..., None], 0.0)
         v = v.view(bs, num_value, H, -1)
