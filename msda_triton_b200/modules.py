@@ -43,8 +43,8 @@ from msda_triton_b200.msda_3d import msda3d
 FUSED_MAX_SAMPLES = 1 << 20
 
 
-# Value projections over at least this many rows take _WideLinearFn.
-WIDE_LINEAR_MIN_ROWS = 1 << 20
+# Projections over at least this many rows take _WideLinearFn.
+WIDE_LINEAR_MIN_ROWS = 1 << 19
 
 
 class _WideLinearFn(torch.autograd.Function):
@@ -196,8 +196,8 @@ class _MSDAModule(nn.Module):
         for q0 in range(0, num_query, qc):
             q1 = min(q0 + qc, num_query)
             qq = q[:, q0:q1]
-            offsets = self.sampling_offsets(qq).view(bs, q1 - q0, H, L, P, d)
-            logits = self.attention_weights(qq).view(bs, q1 - q0, H, L, P)
+            offsets = _project(self.sampling_offsets, qq).view(bs, q1 - q0, H, L, P, d)
+            logits = _project(self.attention_weights, qq).view(bs, q1 - q0, H, L, P)
             if self.fused_prologue and bs * (q1 - q0) * hc * L * P < FUSED_MAX_SAMPLES:
                 # (loc, weights) formed per sample inside the kernels
                 ref = reference_points[:, q0:q1]
@@ -224,7 +224,7 @@ class _MSDAModule(nn.Module):
                 out[:, :, h0 * c:h1 * c] = run(h0, h1)
             chunks.append(out)
         out = chunks[0] if len(chunks) == 1 else torch.cat(chunks, dim=1)
-        out = self.output_proj(out)
+        out = _project(self.output_proj, out)
         if not self.batch_first:
             out = out.permute(1, 0, 2)
         return self.dropout(out) + identity
